@@ -1,0 +1,64 @@
+// Host-side helpers shared by the C-ABI entry points: thread-local error
+// string, argument / CUDA checks that turn into DSV4_E* return codes, and the
+// packed expert slot layout.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/dsv4moe.h"
+
+namespace dsv4 {
+
+void set_error(int code, const std::string& msg);
+int fail(int code, const std::string& msg);
+// Make the device that owns `ptr` current for this library's CUDA runtime
+// (the library links its own runtime, so it does not see the caller's
+// cudaSetDevice).  Optionally returns the device ordinal.
+int bind_device_of(const void* ptr, int* device);
+
+// Byte layout of one packed expert slot (see include/dsv4moe.h).
+struct SlotLayout {
+  int64_t w13p;   // [2I, H/2] packed, w1 rows then w3 rows
+  int64_t w2p;    // [H, I/2] packed
+  int64_t sf13;   // scale atoms of the [2I, H] matrix
+  int64_t sf2;    // scale atoms of the [H, I] matrix
+  int64_t bytes;  // total
+};
+inline SlotLayout slot_layout(int64_t hidden, int64_t inter) {
+  SlotLayout L;
+  L.w13p = 0;
+  L.w2p = L.w13p + 2 * inter * hidden / 2;
+  L.sf13 = L.w2p + hidden * inter / 2;
+  L.sf2 = L.sf13 + 2 * inter * hidden / 32;
+  L.bytes = L.sf2 + hidden * inter / 32;
+  return L;
+}
+
+}  // namespace dsv4
+
+#define DSV4_API_BEGIN try {
+#define DSV4_API_END                                              \
+  return DSV4_OK;                                                 \
+  }                                                               \
+  catch (const std::exception& ex) {                              \
+    return ::dsv4::fail(DSV4_EINVAL, ex.what());                  \
+  }                                                               \
+  catch (...) {                                                   \
+    return ::dsv4::fail(DSV4_EINVAL, "unknown C++ exception");    \
+  }
+
+#define DSV4_CHECK_ARG(cond, msg)                                                     \
+  do {                                                                                \
+    if (!(cond)) return ::dsv4::fail(DSV4_EINVAL, std::string(__func__) + ": " + (msg)); \
+  } while (0)
+
+#define DSV4_CUDA_CHECK(expr)                                                                   \
+  do {                                                                                          \
+    cudaError_t _e = (expr);                                                                    \
+    if (_e != cudaSuccess)                                                                      \
+      return ::dsv4::fail(DSV4_ECUDA, std::string(__func__) + ": " + #expr + ": " +             \
+                                          cudaGetErrorString(_e));                              \
+  } while (0)

@@ -1,0 +1,553 @@
+// Routed-expert layer: moe_align, activation quant + gather, the two grouped
+// GEMMs (moe_gemm.cuh) and the deterministic combine, bound together by a
+// plan that owns the TMA descriptors.  Mirrors _routed / _routed_mxfp4
+// (deepseek_v4.py:150-245) of the reference.
+#include <algorithm>
+#include <memory>
+#include <string>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "moe_gemm.cuh"
+
+namespace dsv4 {
+
+// ---------------------------------------------------------------------------
+// moe_align (deepseek_v4.py:154-164): one CTA of 1024 threads.  Histogram,
+// exclusive scan, then a stable scatter in chunks of 1024 assignments: rank
+// inside a warp from __match_any_sync, rank across warps from a per-warp,
+// per-expert count table.  Also emits the active-expert list and the GEMM
+// work chunks (<= 64 rows of one expert each).
+// ---------------------------------------------------------------------------
+constexpr int AL_THREADS = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  // scratch: 32 ints.  All 1024 threads participate.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = scratch[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    scratch[lane] = w;
+  }
+  __syncthreads();
+  const int excl = x - v + (warp > 0 ? scratch[warp - 1] : 0);
+  if (total) *total = scratch[31];
+  __syncthreads();
+  return excl;
+}
+
+__global__ void __launch_bounds__(AL_THREADS, 1)
+    moe_align_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, const float* __restrict__ w_flat,
+                     int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
+                     int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
+                     float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
+                     int chunk_rows, int* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                 // E
+  int* run = cnt + E;            // E
+  int* tot = run + E;            // E
+  int* scratch = tot + E;        // 32
+  uint16_t* wc = reinterpret_cast<uint16_t*>(scratch + 32);  // [32][E]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  for (int e = tid; e < E; e += AL_THREADS) cnt[e] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += AL_THREADS) {
+    const int e = idx[p];
+    if (e < 0 || e >= E) {
+      set_status(status, DSV4_EINVAL);
+      inv[p] = -1;
+      continue;
+    }
+    atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  // exclusive scan of counts (E <= 1024: one expert per thread)
+  int total = 0;
+  const int c = tid < E ? cnt[tid] : 0;
+  const int off = block_exclusive_scan(c, scratch, &total);
+  if (tid < E) {
+    run[tid] = off;
+    counts[tid] = c;
+    offsets[tid] = off;
+  }
+  if (tid == 0) offsets[E] = total;
+  __syncthreads();
+
+  for (int base = 0; base < P; base += AL_THREADS) {
+    for (int j = tid; j < 32 * E; j += AL_THREADS) wc[j] = 0;
+    __syncthreads();
+    const int p = base + tid;
+    int e = -1;
+    if (p < P) {
+      e = idx[p];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned mask = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(mask & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wc[warp * E + e] = (uint16_t)__popc(mask);
+    __syncthreads();
+    for (int x = tid; x < E; x += AL_THREADS) {
+      int s = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int v = wc[w * E + x];
+        wc[w * E + x] = (uint16_t)s;
+        s += v;
+      }
+      tot[x] = s;
+    }
+    __syncthreads();
+    if (e >= 0) {
+      const int pos = run[e] + wc[warp * E + e] + rank;
+      sorted_flat[pos] = p;
+      inv[p] = pos;
+      if (sorted_w) sorted_w[pos] = w_flat[p];
+    }
+    __syncthreads();
+    for (int x = tid; x < E; x += AL_THREADS) run[x] += tot[x];
+    __syncthreads();
+  }
+
+  // active experts, ascending
+  int nact = 0;
+  const int flag = (tid < E && cnt[tid] > 0) ? 1 : 0;
+  const int apos = block_exclusive_scan(flag, scratch, &nact);
+  if (flag) active[apos] = tid;
+  if (tid == 0) *n_active = nact;
+  // work chunks of <= chunk_rows rows
+  if (chunks) {
+    const int nch = tid < E ? (cnt[tid] + chunk_rows - 1) / chunk_rows : 0;
+    int nchunk_total = 0;
+    const int cpos = block_exclusive_scan(nch, scratch, &nchunk_total);
+    for (int j = 0; j < nch; ++j) {
+      const int r0 = off + j * chunk_rows;
+      chunks[cpos + j] = make_int4(tid, r0, min(chunk_rows, c - j * chunk_rows), 0);
+    }
+    if (tid == 0) *n_chunks = nchunk_total;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// activation quant + gather into the GEMM B operand.  Sorted row p reads token
+// sorted_flat[p] / topk.  Scales go to [K/128][p_cap] words, one byte per
+// 32-block (FP8: the per-128 exponent replicated four times).
+// ---------------------------------------------------------------------------
+__global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
+                                        const int* __restrict__ n_rows, int topk, int K, int64_t p_cap,
+                                        uint8_t* __restrict__ q, uint32_t* __restrict__ sf) {
+  const int lane = threadIdx.x & 31;
+  const int kblk = K / 128;
+  const int64_t nblk = (int64_t)(*n_rows) * kblk;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t b = warp0; b < nblk; b += nwarps) {
+    const int64_t p = b / kblk;
+    const int kb = (int)(b - p * kblk);
+    const int64_t tok = sorted_flat[p] / topk;
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
+    const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
+                        bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
+    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    a = warp_max_f(a);
+    const int e = fp8_scale_exp(a);
+    const float inv = pow2i(-e);
+    uint32_t o = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv, -448.f), 448.f)) << (8 * i);
+    *reinterpret_cast<uint32_t*>(q + p * K + kb * 128 + lane * 4) = o;
+    if (lane == 0) sf[(int64_t)kb * p_cap + p] = (uint32_t)(e + 127) * 0x01010101u;
+  }
+}
+
+__global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
+                                          const int* __restrict__ n_rows, int topk, int K, int64_t p_cap,
+                                          uint8_t* __restrict__ q, uint32_t* __restrict__ sf) {
+  const int lane = threadIdx.x & 31;
+  const int kblk = K / 128;
+  const int64_t nblk = (int64_t)(*n_rows) * kblk;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t b = warp0; b < nblk; b += nwarps) {
+    const int64_t p = b / kblk;
+    const int kb = (int)(b - p * kblk);
+    const int64_t tok = sorted_flat[p] / topk;
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
+    const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
+                        bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
+    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const int e = mx_scale_exp(a);
+    const float inv = pow2_any(-e);
+    const uint32_t packed = e2m1_code(v[0] * inv) | (e2m1_code(v[1] * inv) << 4) | (e2m1_code(v[2] * inv) << 8) |
+                            (e2m1_code(v[3] * inv) << 12);
+    *reinterpret_cast<uint16_t*>(q + p * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
+    if ((lane & 7) == 0)
+      reinterpret_cast<uint8_t*>(sf)[((int64_t)kb * p_cap + p) * 4 + (lane >> 3)] = (uint8_t)(e + 127);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// combine (deepseek_v4.py:195-197): y[t] = bf16(sum over the token's k rows,
+// in ascending sorted position = ascending expert id, fp32 from zero).
+// One block per token, eight columns per thread.
+// ---------------------------------------------------------------------------
+__global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* __restrict__ inv, int topk, int H,
+                               uint16_t* __restrict__ y, int64_t T) {
+  const int64_t t = blockIdx.x;
+  if (t >= T) return;
+  int pos[16];
+  int k = 0;
+  for (int j = 0; j < topk; ++j) {
+    const int v = inv[t * topk + j];
+    if (v < 0) continue;
+    int i = k++;
+    while (i > 0 && pos[i - 1] > v) {
+      pos[i] = pos[i - 1];
+      --i;
+    }
+    pos[i] = v;
+  }
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const uint4 r = *reinterpret_cast<const uint4*>(out + (int64_t)pos[j] * H + c);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16_from_bits(w[q] & 0xffffu);
+        acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = (uint32_t)bf16_bits(acc[2 * q]) | ((uint32_t)bf16_bits(acc[2 * q + 1]) << 16);
+    *reinterpret_cast<uint4*>(y + t * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// plan
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+static int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) return fail(DSV4_ECUDA, "cuTensorMapEncodeTiled is not available");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) s[i] = strides_bytes[i];
+  }
+  CUresult r = enc(m, dt, (cuuint32_t)rank, base, d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSV4_ECUDA, std::string("tensor map encode failed for ") + what +
+                                                     " (CUresult " + std::to_string((int)r) + ")");
+  return DSV4_OK;
+}
+
+struct WsLayout {
+  int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
+  int64_t xq, xsf, hq, hsf, out, bytes;
+  int64_t p_max, p_cap, max_chunks;
+};
+
+static int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
+
+static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens) {
+  WsLayout w;
+  w.p_max = max_tokens * topk;
+  w.p_cap = (w.p_max + 127) / 128 * 128 + 128;
+  w.max_chunks = w.p_max / G_BN + E + 1;
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t at = o;
+    o = al256(o + bytes);
+    return at;
+  };
+  w.status = take(16);
+  w.counts = take(4 * E);
+  w.offsets = take(4 * (E + 1));
+  w.active = take(4 * E);
+  w.n_active = take(4);
+  w.n_chunks = take(4);
+  w.sorted_flat = take(4 * std::max<int64_t>(w.p_max, 1));
+  w.inv = take(4 * std::max<int64_t>(w.p_max, 1));
+  w.sorted_w = take(4 * std::max<int64_t>(w.p_max, 1));
+  w.chunks = take(16 * w.max_chunks);
+  w.xq = take(w.p_cap * H);
+  w.xsf = take(4 * (H / 128) * w.p_cap);
+  w.hq = take(w.p_cap * I);
+  w.hsf = take(4 * (I / 128) * w.p_cap);
+  w.out = take(2 * w.p_cap * H);
+  w.bytes = o;
+  return w;
+}
+
+}  // namespace dsv4
+
+struct dsv4_moe_plan {
+  int device = 0;
+  int num_sms = 148;
+  int H = 0, I = 0, E = 0, topk = 0;
+  int64_t max_tokens = 0;
+  float swiglu_limit = 0.f;
+  uint8_t* arena = nullptr;
+  int64_t n_slots = 0;
+  dsv4::SlotLayout slot;
+  uint8_t* ws = nullptr;
+  dsv4::WsLayout wl;
+  CUtensorMap tmA13, tmA2, tmB1_fp8, tmB1_fp4, tmB2_fp8, tmB2_fp4;
+};
+
+using namespace dsv4;
+
+template <typename T>
+static T* wsp(dsv4_moe_plan* p, int64_t off) {
+  return reinterpret_cast<T*>(p->ws + off);
+}
+
+extern "C" int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                                            int64_t max_tokens) {
+  if (hidden <= 0 || inter <= 0 || n_experts <= 0 || topk <= 0 || max_tokens < 0) return DSV4_EINVAL;
+  return ws_layout(hidden, inter, n_experts, topk, max_tokens).bytes;
+}
+
+// The shared-memory opt-in is a per-device function attribute: set it for
+// the current device every time a plan is created.
+template <int NUM_A, bool B_FP4, int EPI>
+static int prepare_gemm() {
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A>::SMEM_BYTES));
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts,
+                                    int32_t topk, int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena,
+                                    int64_t n_slots, void* workspace, int64_t workspace_bytes) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(out && slot_arena && workspace, "null pointer");
+  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 128 == 0 && inter % 128 == 0,
+                 "hidden and inter must be positive multiples of 128");
+  DSV4_CHECK_ARG(n_experts > 0 && n_experts <= 1024, "n_experts must be in [1, 1024]");
+  DSV4_CHECK_ARG(topk > 0 && topk <= 16, "topk must be in [1, 16]");
+  DSV4_CHECK_ARG(max_tokens > 0 && n_slots > 0, "max_tokens and n_slots must be positive");
+  DSV4_CHECK_ARG(((uintptr_t)slot_arena % 256) == 0 && ((uintptr_t)workspace % 256) == 0,
+                 "slot arena and workspace must be 256-byte aligned");
+  const WsLayout wl = ws_layout(hidden, inter, n_experts, topk, max_tokens);
+  DSV4_CHECK_ARG(workspace_bytes >= wl.bytes, "workspace too small");
+  std::unique_ptr<dsv4_moe_plan> p(new dsv4_moe_plan());
+  int rc0 = bind_device_of(slot_arena, &p->device);
+  if (rc0 != 0) return rc0;
+  DSV4_CUDA_CHECK(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, p->device));
+  p->H = hidden;
+  p->I = inter;
+  p->E = n_experts;
+  p->topk = topk;
+  p->max_tokens = max_tokens;
+  p->swiglu_limit = swiglu_limit;
+  p->arena = slot_arena;
+  p->n_slots = n_slots;
+  p->slot = slot_layout(hidden, inter);
+  p->ws = (uint8_t*)workspace;
+  p->wl = wl;
+  DSV4_CUDA_CHECK(cudaMemset(workspace, 0, (size_t)wl.bytes));
+  const uint64_t H = hidden, I = inter, SB = (uint64_t)p->slot.bytes, PC = (uint64_t)wl.p_cap;
+  const CUtensorMapDataType U4 = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  int rc;
+  {  // w13: [slots][2I rows][H] E2M1
+    const uint64_t dims[3] = {H, 2 * I, (uint64_t)n_slots}, str[2] = {H / 2, SB};
+    const uint32_t box[3] = {G_BK, G_BM, 1};
+    if ((rc = make_map(&p->tmA13, U4, 3, slot_arena + p->slot.w13p, dims, str, box, "w13")) != 0) return rc;
+  }
+  {  // w2: [slots][H rows][I]
+    const uint64_t dims[3] = {I, H, (uint64_t)n_slots}, str[2] = {I / 2, SB};
+    const uint32_t box[3] = {G_BK, G_BM, 1};
+    if ((rc = make_map(&p->tmA2, U4, 3, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
+  }
+  const uint32_t bbox[2] = {G_BK, G_BN};
+  {
+    const uint64_t dims[2] = {H, PC}, s8[1] = {H}, s4[1] = {H / 2};
+    if ((rc = make_map(&p->tmB1_fp8, U8, 2, p->ws + wl.xq, dims, s8, bbox, "x fp8")) != 0) return rc;
+    if ((rc = make_map(&p->tmB1_fp4, U4, 2, p->ws + wl.xq, dims, s4, bbox, "x fp4")) != 0) return rc;
+  }
+  {
+    const uint64_t dims[2] = {I, PC}, s8[1] = {I}, s4[1] = {I / 2};
+    if ((rc = make_map(&p->tmB2_fp8, U8, 2, p->ws + wl.hq, dims, s8, bbox, "h fp8")) != 0) return rc;
+    if ((rc = make_map(&p->tmB2_fp4, U4, 2, p->ws + wl.hq, dims, s4, bbox, "h fp4")) != 0) return rc;
+  }
+  if ((rc = prepare_gemm<2, false, EPI_SWIGLU_FP8>()) != 0) return rc;
+  if ((rc = prepare_gemm<2, true, EPI_SWIGLU_MXFP4>()) != 0) return rc;
+  if ((rc = prepare_gemm<1, false, EPI_STORE_BF16>()) != 0) return rc;
+  if ((rc = prepare_gemm<1, true, EPI_STORE_BF16>()) != 0) return rc;
+  const size_t al_smem = (size_t)(3 * n_experts + 32) * 4 + (size_t)32 * n_experts * 2;
+  DSV4_CUDA_CHECK(
+      cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
+  *out = p.release();
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_plan_destroy(dsv4_moe_plan* plan) {
+  delete plan;
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                                const float* route_weights, const int32_t* route_indices,
+                                const int32_t* slot_of_expert, void* y_bf16, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert && y_bf16, "null pointer");
+  DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= p->max_tokens, "n_tokens exceeds the plan's max_tokens");
+  DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)y_bf16 % 16) == 0, "x and y must be 16-byte aligned");
+  if (n_tokens == 0) return DSV4_OK;
+  DSV4_CUDA_CHECK(cudaSetDevice(p->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const WsLayout& w = p->wl;
+  const int P = (int)(n_tokens * p->topk);
+  int* status = wsp<int>(p, w.status);
+  int32_t* sorted_flat = wsp<int32_t>(p, w.sorted_flat);
+  int32_t* inv = wsp<int32_t>(p, w.inv);
+  int32_t* n_active = wsp<int32_t>(p, w.n_active);
+  int* n_chunks = wsp<int>(p, w.n_chunks);
+  const size_t al_smem = (size_t)(3 * p->E + 32) * 4 + (size_t)32 * p->E * 2;
+  moe_align_kernel<<<1, AL_THREADS, al_smem, st>>>(
+      route_indices, P, p->topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
+      sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w), wsp<int4>(p, w.chunks),
+      n_chunks, G_BN, status);
+  const bool fp4 = profile == DSV4_PROFILE_A4W4;
+  // the gather reads the valid row count from the align output (offsets[E])
+  const int* n_rows = wsp<int>(p, w.offsets) + p->E;
+  {
+    const int64_t warps = (int64_t)P * (p->H / 128);
+    int64_t blocks = (warps * 32 + 255) / 256;
+    blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
+    if (fp4)
+      quant_gather_mxfp4_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
+                                                                  p->topk, p->H, w.p_cap, p->ws + w.xq,
+                                                                  wsp<uint32_t>(p, w.xsf));
+    else
+      quant_gather_fp8_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
+                                                                p->topk, p->H, w.p_cap, p->ws + w.xq,
+                                                                wsp<uint32_t>(p, w.xsf));
+  }
+  GemmParams g1{};
+  g1.arena = p->arena;
+  g1.slot_bytes = p->slot.bytes;
+  g1.sfa_off = p->slot.sf13;
+  g1.k_tiles = p->H / 128;
+  g1.a_row_tiles = p->I / 128;
+  g1.a1_row_offset = p->I;
+  g1.b_sf = wsp<uint32_t>(p, w.xsf);
+  g1.p_cap = w.p_cap;
+  g1.chunks = wsp<int4>(p, w.chunks);
+  g1.n_chunks = n_chunks;
+  g1.slot_of = slot_of_expert;
+  g1.n_slots = (int)p->n_slots;
+  g1.sorted_w = wsp<float>(p, w.sorted_w);
+  g1.out_q = p->ws + w.hq;
+  g1.out_sf = wsp<uint32_t>(p, w.hsf);
+  g1.out_ld = p->I;
+  g1.swiglu_limit = p->swiglu_limit;
+  g1.status = status;
+  GemmParams g2 = g1;
+  g2.sfa_off = p->slot.sf2;
+  g2.k_tiles = p->I / 128;
+  g2.a_row_tiles = p->H / 128;
+  g2.a1_row_offset = 0;
+  g2.b_sf = wsp<uint32_t>(p, w.hsf);
+  g2.out_q = nullptr;
+  g2.out_sf = nullptr;
+  g2.out_bf16 = wsp<uint16_t>(p, w.out);
+  g2.out_ld = p->H;
+  const dim3 grid(p->num_sms), block(G_THREADS);
+  if (fp4) {
+    moe_gemm_kernel<2, true, EPI_SWIGLU_MXFP4><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp4, g1);
+    moe_gemm_kernel<1, true, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp4, g2);
+  } else {
+    moe_gemm_kernel<2, false, EPI_SWIGLU_FP8><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp8, g1);
+    moe_gemm_kernel<1, false, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp8, g2);
+  }
+  combine_kernel<<<(unsigned)n_tokens, std::min(1024, p->H / 8), 0, st>>>(wsp<uint16_t>(p, w.out), inv, p->topk,
+                                                                          p->H, (uint16_t*)y_bf16, n_tokens);
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_status(dsv4_moe_plan* p, void* stream) {
+  if (!p) return fail(DSV4_EINVAL, "dsv4_moe_status: null plan");
+  cudaSetDevice(p->device);
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(DSV4_ECUDA, std::string("dsv4_moe_status: ") + cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpy(&v, p->ws + p->wl.status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(DSV4_ECUDA, std::string("dsv4_moe_status: ") + cudaGetErrorString(e));
+  if (v != 0) {
+    cudaMemset(p->ws + p->wl.status, 0, sizeof(int));
+    return fail(v, "a kernel of the routed-expert layer reported this status");
+  }
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_moe_debug_align(dsv4_moe_plan* p, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,
+                                    int32_t** inv, int32_t** active, int32_t** n_active) {
+  if (!p) return fail(DSV4_EINVAL, "dsv4_moe_debug_align: null plan");
+  if (counts) *counts = wsp<int32_t>(p, p->wl.counts);
+  if (offsets) *offsets = wsp<int32_t>(p, p->wl.offsets);
+  if (sorted_flat) *sorted_flat = wsp<int32_t>(p, p->wl.sorted_flat);
+  if (inv) *inv = wsp<int32_t>(p, p->wl.inv);
+  if (active) *active = wsp<int32_t>(p, p->wl.active);
+  if (n_active) *n_active = wsp<int32_t>(p, p->wl.n_active);
+  return DSV4_OK;
+}
+
+// Standalone moe_align entry point (the same kernel, no chunk outputs).
+extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t topk, int32_t n_experts,
+                              int32_t* counts, int32_t* offsets, int32_t* sorted_flat, int32_t* inv, int32_t* active,
+                              int32_t* n_active, int* status, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(counts && offsets && active && n_active, "null pointer");
+  DSV4_CHECK_ARG(n_tokens == 0 || (indices && sorted_flat && inv), "null pointer");
+  DSV4_CHECK_ARG(n_experts > 0 && n_experts <= 1024 && topk > 0, "bad n_experts / topk");
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * topk < (1LL << 31), "too many assignments");
+  int rc = bind_device_of(counts, nullptr);
+  if (rc != 0) return rc;
+  const size_t al_smem = (size_t)(3 * n_experts + 32) * 4 + (size_t)32 * n_experts * 2;
+  DSV4_CUDA_CHECK(
+      cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
+  moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
+      indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
+      nullptr, nullptr, nullptr, 64, status);
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}

@@ -1,0 +1,143 @@
+/*
+ * dsv4moe — C ABI of the B200 (sm_100a) routed-expert MoE library.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream passed as
+ * `void*` (a cudaStream_t; NULL = legacy default stream), returns 0 or a
+ * negative DSV4_E* code, and never throws.  Device buffers are owned by the
+ * caller.  Work is enqueued asynchronously on the given stream; a kernel that
+ * detects bad input or a timed-out wait records the code in a device status
+ * word that the host reads with dsv4_moe_status().  dsv4_last_error_string()
+ * describes the last failure of the calling thread.
+ *
+ * Each declaration names the reference interface it replaces
+ * (ErnestW2019/deepseek-v4-flash-offload, file:line).
+ */
+#ifndef DSV4MOE_H
+#define DSV4MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSV4_ABI_VERSION 1
+
+#define DSV4_OK 0
+#define DSV4_EINVAL (-1)      /* bad shape, pointer or argument */
+#define DSV4_ENOMEM (-2)      /* workspace / pool / slot budget too small */
+#define DSV4_ECUDA (-3)       /* CUDA runtime or driver error */
+#define DSV4_ETIMEOUT (-4)    /* a bounded device-side wait ran out */
+#define DSV4_ENCCL (-5)       /* collective failure (expert parallel) */
+#define DSV4_ENOTFOUND (-6)   /* expert not registered or not resident */
+#define DSV4_EUNSUPPORTED (-7)
+
+/* router score functions (deepseek_v4.py:126-131) */
+#define DSV4_SCORE_SOFTMAX 0
+#define DSV4_SCORE_SIGMOID 1
+#define DSV4_SCORE_SQRTSOFTPLUS 2
+
+/* expert compute profiles: PROFILE=bf16|a4w4, DSV4_MXFP4_GMM (deepseek_v4.py:28-32) */
+#define DSV4_PROFILE_BF16 0
+#define DSV4_PROFILE_A4W4 1
+
+const char* dsv4_last_error_string(void);
+int dsv4_abi_version(void);
+
+/* ------------------------------------------------------------------------ *
+ * Packed expert slot layout.
+ * One expert = w1/w3 [I, H/2] + w2 [H, I/2] packed E2M1 (low nibble = even k)
+ * and E8M0 per-32 scales, stored as ONE contiguous slot:
+ *   [w13 packed (w1 rows then w3 rows) | w2 packed | w13 scales | w2 scales]
+ * with the scales re-tiled into 512-byte atoms (128 rows x 4 scale bytes,
+ * row r at (r%32)*16 + (r/32)*4) that the tensor cores read directly.
+ * Replaces the six per-expert host tensors of ExpertBank.register
+ * (offload.py:59-68) and their per-call stacking (deepseek_v4.py:218-223).
+ * ------------------------------------------------------------------------ */
+int64_t dsv4_expert_slot_bytes(int32_t hidden, int32_t inter);
+/* host-side pack of the checkpoint tensors into one slot (CPU memory) */
+int dsv4_pack_expert_host(const uint8_t* w1p, const uint8_t* w1s, const uint8_t* w2p, const uint8_t* w2s,
+                          const uint8_t* w3p, const uint8_t* w3s, int32_t hidden, int32_t inter,
+                          uint8_t* slot_out);
+/* inverse of dsv4_pack_expert_host (CPU memory); used by get_packed views */
+int dsv4_unpack_expert_host(const uint8_t* slot, int32_t hidden, int32_t inter, uint8_t* w1p, uint8_t* w1s,
+                            uint8_t* w2p, uint8_t* w2s, uint8_t* w3p, uint8_t* w3s);
+
+/* ------------------------------------------------------------------------ *
+ * Element-wise ops.
+ * ------------------------------------------------------------------------ */
+/* dequant_fp4_weight (npu_ops.py:142-158): [rows, k/2] packed E2M1 +
+ * [rows, k/32] E8M0 -> [rows, k] bf16, bit-exact. */
+int dsv4_dequant_mxfp4(const uint8_t* w_packed, const uint8_t* scale, void* out_bf16, int64_t rows, int64_t k,
+                       void* stream);
+/* ExpertBank._dequant_on_device (offload.py:77-84) from a packed slot:
+ * w1/w3 -> [I, H] bf16, w2 -> [H, I] bf16. */
+int dsv4_slot_dequant(const uint8_t* slot, int32_t hidden, int32_t inter, void* w1_bf16, void* w2_bf16,
+                      void* w3_bf16, void* stream);
+/* act_quant(x, 128, "ue8m0", None, inplace=True) (npu_ops.py:73-98):
+ * in-place FP8-E4M3 round trip of bf16 [rows, cols], bit-exact. */
+int dsv4_act_quant_fp8_rt(void* x_bf16, int64_t rows, int64_t cols, void* stream);
+/* npu_dynamic_mx_quant(x, dst_type=F4) (deepseek_v4.py:212, 240): bf16
+ * [rows, cols] -> packed E2M1 [rows, cols/2] + E8M0 [rows, cols/32];
+ * scale = floor(log2(amax/6)), elements round-to-nearest-even, saturating. */
+int dsv4_act_quant_mxfp4(const void* x_bf16, int64_t rows, int64_t cols, uint8_t* q_packed, uint8_t* scale,
+                         void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
+ * logits = float(x) @ gate_w^T; scores by score_func; experts = top-k of
+ * scores + bias (or tid2eid[input_ids] when tid2eid != NULL); weights =
+ * unbiased scores, renormalised when renormalize != 0, times route_scale.
+ * Indices come out in descending biased-score order (ties: lower id first).
+ * ------------------------------------------------------------------------ */
+int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts);
+int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
+                    const int64_t* input_ids, int64_t n_tokens, int32_t hidden, int32_t n_experts, int32_t topk,
+                    int32_t score_func, int32_t renormalize, float route_scale, float* weights_out,
+                    int32_t* indices_out, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * moe_align (deepseek_v4.py:154-164): stable counting sort of the T*k
+ * (token, slot) assignments by expert id.  sorted_flat[pos] = t*k + j,
+ * inv[t*k + j] = pos, offsets = exclusive prefix of counts (E+1 entries),
+ * active = ascending ids with count > 0, *n_active their number.  An index
+ * outside [0, n_experts) sets DSV4_EINVAL in *status (device word).
+ * ------------------------------------------------------------------------ */
+int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t topk, int32_t n_experts, int32_t* counts,
+                   int32_t* offsets, int32_t* sorted_flat, int32_t* inv, int32_t* active, int32_t* n_active,
+                   int* status, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Routed-expert layer: _routed / _routed_mxfp4 (deepseek_v4.py:150-245).
+ * A plan binds the layer dims, the HBM slot arena (n_slots packed slots of
+ * dsv4_expert_slot_bytes each, 256-byte aligned) and a workspace, and builds
+ * the TMA descriptors once.  dsv4_moe_forward then runs, on `stream`:
+ * align -> activation quant + gather -> fused gate/up GEMM with SwiGLU,
+ * route weight and activation re-quant -> down GEMM -> deterministic
+ * combine (ascending expert order per token, fp32) -> y bf16 [T, H].
+ * route_weights/route_indices are the router outputs [T, k];
+ * slot_of_expert[e] is the arena slot holding expert e (or -1).
+ * ------------------------------------------------------------------------ */
+typedef struct dsv4_moe_plan dsv4_moe_plan;
+int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                                 int64_t max_tokens);
+int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                         int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena, int64_t n_slots,
+                         void* workspace, int64_t workspace_bytes);
+int dsv4_moe_plan_destroy(dsv4_moe_plan* plan);
+int dsv4_moe_forward(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                     const float* route_weights, const int32_t* route_indices, const int32_t* slot_of_expert,
+                     void* y_bf16, void* stream);
+/* Synchronises `stream`, returns the plan's device status word (0 or a
+ * DSV4_E* code recorded by a kernel) and clears it. */
+int dsv4_moe_status(dsv4_moe_plan* plan, void* stream);
+/* Device pointers of the plan's align outputs (valid after a forward):
+ * counts[E], offsets[E+1], sorted_flat[P], inv[P], active[E], n_active[1]. */
+int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,
+                         int32_t** inv, int32_t** active, int32_t** n_active);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSV4MOE_H */

@@ -88,7 +88,8 @@ def e4m3_round(x: np.ndarray) -> np.ndarray:
     q = np.ldexp(np.float32(1.0), e - 3)       # 3 mantissa bits
     r = np.rint(a / q) * q                     # np.rint = ties to even
     r = np.minimum(r, np.float32(FP8_MAX))
-    return (np.sign(x) * r).astype(np.float32)
+    # the cast keeps the sign of zero (and of values that round to zero)
+    return np.copysign(r, x).astype(np.float32)
 
 
 def e2m1_round(x: np.ndarray) -> np.ndarray:
@@ -153,7 +154,8 @@ def act_quant_rt(x: np.ndarray, block: int = 128) -> np.ndarray:
     xb = xf.reshape(-1, shp[-1] // block, block)
     k = fp8_block_scale_exp(np.abs(xb).max(axis=-1, keepdims=True))
     y = e4m3_round(np.clip(np.ldexp(xb, -k), -FP8_MAX, FP8_MAX))
-    return bf16_round(np.ldexp(y, k)).reshape(shp)
+    with np.errstate(over="ignore"):      # y * 2**k may overflow to inf, as in float32 torch
+        return bf16_round(np.ldexp(y, k)).reshape(shp)
 
 
 def act_quant_fp8(x: np.ndarray, block: int = 128):

@@ -195,6 +195,15 @@ def main():
     ya = O.act_quant(xa.clone(), 128, "ue8m0", None, True)
     ops["aq_x"], ops["aq_y"] = bf16_bits(xa), bf16_bits(ya)
 
+    # every finite bf16 value, shuffled into 128-blocks, through act_quant
+    allv = (np.arange(0, 0x10000, dtype=np.uint32) << 16).view(np.float32)
+    allv = allv[np.isfinite(allv)]
+    allv = np.random.default_rng(0).permutation(allv)
+    allv = allv[: (allv.size // 128) * 128].reshape(-1, 128)
+    xall = torch.from_numpy(allv.copy()).to(torch.bfloat16)
+    ops["aq_all_x"] = bf16_bits(xall)
+    ops["aq_all_y"] = bf16_bits(O.act_quant(xall.clone(), 128, "ue8m0", None, True))
+
     # exhaustive: pow2 scale exponent for every positive finite bf16 amax
     pats = np.arange(1, 0x7F80, dtype=np.uint16)
     amax = torch.from_numpy((pats.astype(np.uint32) << 16).view(np.float32))

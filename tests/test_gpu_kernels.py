@@ -1,0 +1,147 @@
+"""GPU parity of the element-wise kernels, router and align against the
+oracle and the reference's golden fixtures.  Bit-exact where the reference
+is integer / byte / exactly-rounded work."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from dsv4_plugin import synthetic as S
+
+from helpers import bf16_tensor, bf16_to_np
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from dsv4_plugin import ops as _ops
+    return _ops
+
+
+def _gold(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_dequant_golden(ops, tag):
+    g = _gold("ops.npz")
+    wp = torch.from_numpy(g[f"deq_{tag}_wp"]).cuda()
+    ws = torch.from_numpy(g[f"deq_{tag}_ws"]).cuda()
+    out = ops.dequant_fp4_weight(wp, ws)
+    got = out.cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, g[f"deq_{tag}_out"])
+
+
+def test_dequant_full_size_bit_exact(ops):
+    ex = S.make_expert(S.CFG1, 3, 0)
+    for w in ("w1", "w2"):
+        out = ops.dequant_fp4_weight(torch.from_numpy(ex[w + "p"]).cuda(), torch.from_numpy(ex[w + "s"]).cuda())
+        ref = O.bf16_bits(O.dequant_fp4_weight(ex[w + "p"], ex[w + "s"]))
+        assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+
+
+def test_slot_dequant_matches_checkpoint_dequant(ops):
+    cfg = S.CFG0
+    ex = S.make_expert(cfg, 5, 2)
+    slot = ops.pack_expert(*[torch.from_numpy(ex[k]) for k in ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")],
+                           cfg.hidden, cfg.inter).cuda()
+    d = ops.slot_dequant(slot, cfg.hidden, cfg.inter)
+    for w in ("w1", "w2", "w3"):
+        ref = O.bf16_bits(O.dequant_fp4_weight(ex[w + "p"], ex[w + "s"]))
+        assert np.array_equal(d[w].cpu().view(torch.int16).numpy().view(np.uint16), ref)
+
+
+def test_act_quant_golden_and_exhaustive(ops):
+    g = _gold("ops.npz")
+    x = torch.from_numpy(g["aq_x"].view(np.int16)).view(torch.bfloat16).cuda()
+    ops.act_quant(x, 128, "ue8m0", None, True)
+    assert np.array_equal(x.cpu().view(torch.int16).numpy().view(np.uint16), g["aq_y"])
+    # every finite bf16 value, shuffled into 128-blocks, against the reference
+    xt = torch.from_numpy(g["aq_all_x"].view(np.int16)).view(torch.bfloat16).cuda()
+    ops.act_quant(xt, 128, "ue8m0", None, True)
+    assert np.array_equal(xt.cpu().view(torch.int16).numpy().view(np.uint16), g["aq_all_y"])
+
+
+def test_mx_quant_bit_exact(ops):
+    rng = np.random.default_rng(1)
+    x = S.bf16_exact(rng.standard_normal((64, 1024)).astype(np.float32) * np.float32(3.0))
+    x[3, :32] = 0.0
+    x[4, 32:64] = 1e-30
+    x[5, 64:96] = 6.0 * 2.0 ** np.arange(32)
+    q, s = ops.dynamic_mx_quant(bf16_tensor(x))
+    vals, k, _ = O.mx_quant_fp4(x)
+    assert np.array_equal(q.cpu().numpy(), O.pack_fp4(vals))
+    assert np.array_equal(s.cpu().numpy(), (k + 127).astype(np.uint8))
+
+
+def _sets(a):
+    return np.sort(np.asarray(a), axis=-1)
+
+
+def test_route_golden_cfg0(ops):
+    g = _gold("layer_cfg0.npz")
+    x = bf16_tensor(O.bf16_from_bits(g["x"]))
+    cfg = S.CFG0
+    w, i = ops.route_topk(x, torch.from_numpy(g["gate_w"]).cuda(), torch.zeros(cfg.n_experts).cuda(), cfg.topk,
+                          "softmax", False)
+    assert np.array_equal(_sets(i.cpu().numpy()), _sets(g["oracle_idx"]))
+    ow = np.take_along_axis(g["oracle_w"], np.argsort(g["oracle_idx"], -1), -1)
+    gw = np.take_along_axis(w.cpu().numpy(), np.argsort(i.cpu().numpy(), -1), -1)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5, atol=1e-7)
+    for func, wk, ik in (("sqrtsoftplus", "sq_w", "sq_idx"), ("sigmoid", "sig_w", "sig_idx")):
+        w, i = ops.route_topk(x, torch.from_numpy(g["sq_gate_w"]).cuda(), torch.from_numpy(g["sq_bias"]).cuda(),
+                              cfg.topk, func, True)
+        assert np.array_equal(_sets(i.cpu().numpy()), _sets(g[ik]))
+        np.testing.assert_allclose(np.take_along_axis(w.cpu().numpy(), np.argsort(i.cpu().numpy(), -1), -1),
+                                   np.take_along_axis(g[wk], np.argsort(g[ik], -1), -1), rtol=1e-5, atol=1e-7)
+    w, i = ops.route_topk(x, torch.from_numpy(g["sq_gate_w"]).cuda(), None, cfg.topk, "sqrtsoftplus", True,
+                          tid2eid=torch.from_numpy(g["hash_tid2eid"]).cuda(),
+                          input_ids=torch.from_numpy(g["hash_ids"]).cuda())
+    assert np.array_equal(i.cpu().numpy(), g["hash_idx"])
+    np.testing.assert_allclose(w.cpu().numpy(), g["hash_w"], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 300])
+def test_route_cfg1_matches_oracle(ops, T):
+    cfg = S.CFG1
+    gw, bias = S.make_gate(cfg, 0)
+    x = S.make_tokens(cfg, 0, T)
+    w, i = ops.route_topk(bf16_tensor(x), torch.from_numpy(gw).cuda(), torch.from_numpy(bias).cuda(), cfg.topk,
+                          cfg.score_func, cfg.renormalize)
+    ow, oi = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+    assert np.array_equal(_sets(i.cpu().numpy()), _sets(oi))
+    np.testing.assert_allclose(np.take_along_axis(w.cpu().numpy(), np.argsort(i.cpu().numpy(), -1), -1),
+                               np.take_along_axis(ow, np.argsort(oi, -1), -1), rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("T,k,E", [(0, 8, 256), (1, 8, 256), (64, 8, 256), (2048, 8, 256), (8192, 8, 256),
+                                   (16, 4, 16), (33, 6, 1024)])
+def test_align_bit_exact(ops, T, k, E):
+    rng = np.random.default_rng(T * 31 + E)
+    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]) if T else np.zeros((0, k), np.int64)
+    if T:
+        # skew: token-majority on a few experts
+        idx[: T // 2, 0] = 3
+    res = ops.moe_align(torch.from_numpy(idx.astype(np.int32)).cuda(), E)
+    ref = O.moe_align(idx.reshape(T, k), E)
+    assert int(res["status"].item()) == 0
+    assert np.array_equal(res["counts"].cpu().numpy(), ref["counts"])
+    assert np.array_equal(res["offsets"].cpu().numpy(), ref["offsets"])
+    assert np.array_equal(res["sorted_flat"].cpu().numpy(), ref["order"])
+    assert np.array_equal(res["inv"].cpu().numpy(), ref["inv"])
+    na = int(res["n_active"].item())
+    assert na == ref["active"].size
+    assert np.array_equal(res["active"].cpu().numpy()[:na], ref["active"])
+
+
+def test_align_rejects_out_of_range_expert(ops):
+    idx = torch.tensor([[0, 1], [2, 99]], dtype=torch.int32).cuda()
+    res = ops.moe_align(idx, 16)
+    assert int(res["status"].item()) == -1

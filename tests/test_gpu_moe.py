@@ -1,0 +1,131 @@
+"""GPU parity of the fused routed-expert layer (tcgen05 grouped GEMMs).
+
+Tolerance (bf16 profile, from the task contract): max |gpu - oracle| <=
+1e-2 * max |oracle|, the oracle accumulating in fp32.  The a4w4 profile is
+held to the same bound against the oracle's a4w4 restatement (same MXFP4
+rule), and to the reference's a4w4 fixture."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from dsv4_plugin import synthetic as S
+
+from helpers import SyntheticLayer, bf16_tensor, bf16_to_np, rel_err
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from dsv4_plugin import ops as _ops
+    return _ops
+
+
+@pytest.fixture(scope="module")
+def layer0(ops):
+    return SyntheticLayer(S.CFG0, seed=0)
+
+
+def _plan(ops, L, max_tokens):
+    c = L.cfg
+    return ops.MoEPlan(c.hidden, c.inter, L.n, c.topk, max_tokens, c.swiglu_limit, L.arena)
+
+
+@pytest.mark.parametrize("profile", ["bf16", "a4w4"])
+def test_cfg0_matches_oracle_and_reference(ops, layer0, profile):
+    g = np.load(os.path.join(GOLD, "layer_cfg0.npz"))
+    L = layer0
+    x = O.bf16_from_bits(g["x"])
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, 64)
+    y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
+                     L.slot_of, profile)
+    plan.status()
+    got = bf16_to_np(y)
+    ref = L.oracle(x, w, idx, profile)
+    assert rel_err(got, ref) <= TOL
+    gold = O.bf16_from_bits(g["oracle_y"] if profile == "bf16" else g["plugin_a4w4_y"])
+    assert rel_err(got, gold) <= TOL
+
+
+def test_cfg0_alignment_outputs(ops, layer0):
+    L = layer0
+    x = S.make_tokens(L.cfg, 9, 40)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, 40)
+    plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
+                 L.slot_of)
+    plan.status()
+    d = plan.debug_align(40)
+    ref = O.moe_align(idx, L.n)
+    assert np.array_equal(d["sorted_flat"].numpy(), ref["order"])
+    assert np.array_equal(d["counts"].numpy(), ref["counts"])
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 513])
+def test_cfg0_token_counts_and_multi_chunk(ops, layer0, T):
+    """Ragged counts, single token, and experts with >64 rows (several
+    64-row chunks per expert)."""
+    L = layer0
+    x = S.make_tokens(L.cfg, 100 + T, T)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, max(T, 1))
+    for profile in ("bf16", "a4w4"):
+        y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
+                         L.slot_of, profile)
+        plan.status()
+        assert rel_err(bf16_to_np(y), L.oracle(x, w, idx, profile)) <= TOL, profile
+
+
+def test_deterministic_reruns(ops, layer0):
+    L = layer0
+    x = S.make_tokens(L.cfg, 5, 200)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, 200)
+    args = (bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(), L.slot_of)
+    a = plan.forward(*args).clone()
+    b = plan.forward(*args).clone()
+    plan.status()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_missing_expert_reports_status(ops, layer0):
+    L = layer0
+    x = S.make_tokens(L.cfg, 6, 8)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, 8)
+    slot_of = L.slot_of.clone()
+    slot_of[int(idx[0, 0])] = -1
+    plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(), slot_of)
+    with pytest.raises(Exception) as ei:
+        plan.status()
+    assert "-6" in str(ei.value)
+    plan.status()  # cleared
+
+
+@pytest.fixture(scope="module")
+def layer1(ops):
+    return SyntheticLayer(S.CFG1, seed=0)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_cfg1_decode_matches_oracle(ops, layer1, T):
+    L = layer1
+    c = L.cfg
+    x = S.make_tokens(c, 0, T)
+    xt = bf16_tensor(x)
+    w, idx = ops.route_topk(xt, torch.from_numpy(L.gate_w).cuda(), torch.from_numpy(L.bias).cuda(), c.topk,
+                            c.score_func, c.renormalize)
+    plan = _plan(ops, L, 64)
+    y = plan.forward(xt, w, idx, L.slot_of, "bf16")
+    plan.status()
+    ref = L.oracle(x, w.cpu().numpy(), idx.cpu().numpy().astype(np.int64), "bf16")
+    assert rel_err(bf16_to_np(y), ref) <= TOL

@@ -49,6 +49,12 @@ def test_act_quant_roundtrip_matches_reference():
     assert np.array_equal(O.bf16_bits(y), g["aq_y"])
 
 
+def test_act_quant_exhaustive_matches_reference():
+    g = _load("ops.npz")
+    y = O.act_quant_rt(_bf16(g["aq_all_x"]))
+    assert np.array_equal(O.bf16_bits(y), g["aq_all_y"])     # incl. the sign of zero and overflow to inf
+
+
 def test_pow2_scale_exhaustive_over_bf16_amax():
     g = _load("ops.npz")
     amax = O.bf16_from_bits(g["scale_pats"])
