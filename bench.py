@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark of the routed-expert MoE hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (N=1): BASELINE config 1, decode, bf16 profile -- one DeepSeek-V4
+MoE layer (H=4096, I=2048, E=256, top-8, sqrtsoftplus router with a
+Zipf-skewed selection bias) on T=64 tokens with every expert resident in the
+HBM slot arena, synthetic seeded inputs.  A step is one layer forward.
+  value : tokens/s with inputs already in HBM (device time, CUDA events);
+  e2e   : tokens/s through the plugin's public forward with the tokens copied
+          H2D from pinned host memory and the output read back D2H inside the
+          timed region;
+  roofline : the gate/up GEMM kernel (the dominant launch), algorithmic
+          bytes / its event-timed duration against the measured HBM copy peak.
+L2 is flushed (256 MiB write) before every timed step; steps rotate over
+several token batches so routing changes.  With N>1 (torchrun) every rank
+runs the layer expert-parallel: E/N experts per rank, T=64 tokens per rank,
+all-to-all dispatch and combine (weak scaling).
+``--impl reference`` times the CPU restatement of the reference's
+per-expert path (oracle/moe_oracle.py) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "deepseek-v4-flash-offload_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE tok/s (bf16 & a4w4, LRU offload) at 1/2/4/8 B200; GEMM % of roofline"
+UNIT = "tok/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-detail", action="store_true")
+    a = ap.parse_args(argv)
+    a.warmup = max(a.warmup, 3)
+    a.steps = max(a.steps, 1)
+    return a
+
+
+def _dist():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9 and p[1].replace(".", "").isdigit():
+                    rows.append(p)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = max(float(r[2]) for r in rows)
+        load = [s for s in sm if s > 0.5 * mx] or sm
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic layer through the plugin's public API
+# ---------------------------------------------------------------------------
+def _cfg():
+    from dsv4_plugin import synthetic as S
+    return S.CFG1
+
+
+def build_layer(device, rank: int, world: int, seed: int = 0, layer_idx: int = 3):
+    """Engine + OffloadDeepseekV4MoE for one synthetic layer; the experts
+    owned by this rank (all of them at world=1) are resident."""
+    import types
+
+    import torch
+
+    from dsv4_plugin import synthetic as S
+    from dsv4_plugin.core import engine as ENG
+    from dsv4_plugin.models import deepseek_v4 as DV4
+
+    cfg = _cfg()
+    e_loc = cfg.n_experts // world
+    lo = rank * e_loc
+    eng = ENG.ExpertOffloadEngine(slot_capacity=e_loc, device=device, packed_capacity=e_loc)
+    eng.bank.pin = True
+    for e in range(lo, lo + e_loc):
+        ex = S.make_expert(cfg, seed, e, layer_idx)
+        eng.bank.register(layer_idx, e, *[torch.from_numpy(ex[k]) for k in
+                                          ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
+    ENG.reset_engine(eng)
+    hf = types.SimpleNamespace(
+        n_routed_experts=cfg.n_experts, n_shared_experts=None, num_experts_per_tok=cfg.topk,
+        norm_topk_prob=cfg.renormalize, scoring_func=cfg.score_func, routed_scaling_factor=cfg.route_scale,
+        swiglu_limit=cfg.swiglu_limit, num_hash_layers=0, vocab_size=129280, hidden_size=cfg.hidden,
+        moe_intermediate_size=cfg.inter, hidden_act="silu")
+    pc = types.SimpleNamespace(use_sequence_parallel_moe=False, eplb_config=None, enable_eplb=False)
+    moe = DV4.OffloadDeepseekV4MoE(hf, pc, prefix=f"model.layers.{layer_idx}.mlp").to(device)
+    gw, bias = S.make_gate(cfg, seed, layer_idx)
+    moe.gate.weight.data.copy_(torch.from_numpy(gw))
+    moe.gate.e_score_correction_bias.data.copy_(torch.from_numpy(bias))
+    if world == 1:
+        eng.bank.preload_all(layer_idx)
+    torch.cuda.synchronize(device)
+    return moe, eng
+
+
+def _token_batches(n: int, tokens: int, device, rank: int):
+    import torch
+
+    from dsv4_plugin import synthetic as S
+    cfg = _cfg()
+    host, dev = [], []
+    for r in range(n):
+        x = S.make_tokens(cfg, 7 + 1000 * rank, tokens, step=r)
+        h = torch.from_numpy(S.to_bf16_bits(x).astype("int16")).view(torch.bfloat16).pin_memory()
+        host.append(h)
+        dev.append(h.to(device))
+    return host, dev
+
+
+def _gemm_bytes(d: int, p: int, which: str) -> float:
+    """Algorithmic HBM bytes of one launch: weights of the d active experts
+    (packed E2M1 + E8M0 scales) plus the activations in and out."""
+    c = _cfg()
+    h, i = c.hidden, c.inter
+    if which == "gate_up":
+        return d * (2 * i * h // 2 + 2 * i * h // 32) + p * (h + h // 32) + p * (i + i // 32)
+    return d * (h * i // 2 + h * i // 32) + p * (i + i // 32) + p * h * 2
+
+
+def _layer_bytes(d: int, t: int) -> float:
+    c = _cfg()
+    return d * c.packed_expert_bytes() + c.n_experts * c.hidden * 4 + 2 * t * c.hidden * 2
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _traffic():
+    """Per-launch DRAM bytes of the gate/up GEMM from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_gate_up_gemm_cfg1_t64.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(a):
+    import torch
+
+    rank, world, local = _dist()
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    if world > 1:
+        return run_ep(a, rank, world, device)
+    from dsv4_plugin.models import deepseek_v4 as DV4
+
+    moe, eng = build_layer(device, 0, 1)
+    T = a.tokens
+    R = 8
+    host, dev = _token_batches(R, T, device, 0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    y_host = torch.empty((T, _cfg().hidden), dtype=torch.bfloat16).pin_memory()
+    plan = eng.plan_for(_cfg().n_experts, _cfg().topk, T, _cfg().swiglu_limit)
+    plan.enable_timing(True)
+    stream = torch.cuda.current_stream(device)
+
+    def device_steps(n, tokens_dev, record=True):
+        tot, stages, ds = 0.0, [], []
+        for s in range(n):
+            x = tokens_dev[s % len(tokens_dev)]
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            moe.forward(x)
+            e1.record(stream)
+            e1.synchronize()
+            if record:
+                tot += e0.elapsed_time(e1)
+                stages.append(plan.stage_times())
+                ds.append(plan.n_active())
+        return tot, stages, ds
+
+    # warm-up, then the timed device-resident region
+    device_steps(a.warmup, dev, record=False)
+    clk = Clocks(local)
+    torch.cuda.synchronize(device)
+    clk.start()
+    tot_ms, stages, ds = device_steps(a.steps, dev)
+    torch.cuda.synchronize(device)
+    clocks = clk.stop()
+    ms_step = tot_ms / a.steps
+    value = T * a.steps / (tot_ms / 1e3)
+
+    # roofline of the gate/up GEMM and of the whole layer
+    hbm, peak_kind = _peaks()
+    P = T * _cfg().topk
+    g1_ms = sum(s["gate_up_gemm"] for s in stages)
+    g2_ms = sum(s["down_gemm"] for s in stages)
+    g1_bytes = sum(_gemm_bytes(d, P, "gate_up") for d in ds)
+    g2_bytes = sum(_gemm_bytes(d, P, "down") for d in ds)
+    ach1 = g1_bytes / (g1_ms / 1e3) / 1e9
+    ach2 = g2_bytes / (g2_ms / 1e3) / 1e9
+    lay = sum(_layer_bytes(d, T) for d in ds) / (tot_ms / 1e3) / 1e9
+    traffic = _traffic()
+    roofline = {"bound": "hbm", "kernel": "moe_gemm_kernel<2,false,0> (gate/up, bf16 profile)",
+                "achieved": round(ach1, 1), "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
+                "unit": "GB/s", "frac": round(ach1 / hbm, 4),
+                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "algorithmic_bytes_per_launch": round(g1_bytes / len(ds)),
+                "launch_ms": round(g1_ms / len(ds), 5)}
+    detail = {"active_experts_mean": round(statistics.mean(ds), 2),
+              "stage_ms_mean": {k: round(statistics.mean(s[k] for s in stages), 5) for k in stages[0]},
+              "down_gemm_roofline": {"achieved": round(ach2, 1), "frac": round(ach2 / hbm, 4)},
+              "layer_roofline": {"achieved": round(lay, 1), "frac": round(lay / hbm, 4),
+                                 "bytes": "D*13369344 + gate fp32 + x/y"}}
+
+    # e2e through the public forward with host buffers
+    def e2e_steps(n, record=True):
+        tot = 0.0
+        xd = torch.empty_like(dev[0])
+        for s in range(n):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            xd.copy_(host[s % R], non_blocking=True)
+            y = moe.forward(xd)
+            y_host.copy_(y, non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+            if record:
+                tot += e0.elapsed_time(e1)
+        return tot
+
+    e2e_steps(a.warmup, record=False)
+    e2e_ms = e2e_steps(a.steps)
+    e2e = {"value": round(T * a.steps / (e2e_ms / 1e3), 1), "unit": UNIT,
+           "h2d_bytes_per_step": T * _cfg().hidden * 2, "d2h_bytes_per_step": T * _cfg().hidden * 2,
+           "ms_per_step": round(e2e_ms / a.steps, 5), "api": "OffloadDeepseekV4MoE.forward"}
+
+    if not a.no_detail:
+        # a4w4 profile on the same workload, and the other decode batch sizes
+        DV4._MXFP4_GMM = True
+        try:
+            device_steps(2, dev, record=False)
+            t4, _, _ = device_steps(a.steps, dev)
+        finally:
+            DV4._MXFP4_GMM = False
+        detail["a4w4_value"] = round(T * a.steps / (t4 / 1e3), 1)
+        per_t = {}
+        for t in (1, 8, 32):
+            _, dv = _token_batches(4, t, device, 0)
+            device_steps(2, dv, record=False)
+            tt, st, dd = device_steps(max(4, a.steps // 2), dv)
+            n = max(4, a.steps // 2)
+            per_t[str(t)] = {"tok_s": round(t * n / (tt / 1e3), 1), "ms": round(tt / n, 5),
+                             "active_experts": round(statistics.mean(dd), 1),
+                             "gate_up_frac": round(sum(_gemm_bytes(d, t * 8, "gate_up") for d in dd) /
+                                                   (sum(x["gate_up_gemm"] for x in st) / 1e3) / 1e9 / hbm, 4)}
+        detail["decode_T"] = per_t
+    moe.engine.bank  # keep alive
+    plan.status()
+
+    cpu = None if a.no_cpu_baseline else cpu_baseline(T, budget_s=12.0)
+    line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": 1, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1 x e4m3 block-scaled (bf16 profile), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded; BASELINE config 1 distributions)",
+            "config": {"workload": f"cfg1 decode bf16 profile: T={T} tokens, H=4096, I=2048, E=256, top-8, "
+                                   "all experts resident", "tokens_per_step": T, "global_batch": T,
+                       "parallelism": "single GPU",
+                       "l2": "256 MiB flush before every timed step; 8 rotating token batches"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": 7 * a.steps, "detail": detail}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(tokens: int, budget_s: float = 12.0):
+    """Oracle per-expert path (reference semantics) on the host cores, experts
+    resident dequantised (the reference's hot ExpertBank), bounded sample."""
+    import numpy as np
+
+    from dsv4_plugin import synthetic as S
+    from oracle import moe_oracle as O
+    cfg = _cfg()
+    gw, bias = S.make_gate(cfg, 0, 3)
+    x = S.make_tokens(cfg, 7, tokens, step=0)
+    w, idx = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+    need = sorted(set(idx.reshape(-1).tolist()))
+    experts = {e: S.make_expert(cfg, 0, e, 3) for e in need}
+    cache = {e: O.expert_weights_f32(experts[e]) for e in need}
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=cache)
+        n += 1
+        if time.perf_counter() - t0 > budget_s or n >= 50:
+            break
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": round(tokens * n / dt, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} layer forwards of cfg1 decode T={tokens} (oracle per-expert loop, numpy fp32 BLAS, "
+                      f"{len(need)} active experts resident dequantised), {dt:.1f} s"}
+
+
+def run_reference(a):
+    rank, world, _ = _dist()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from dsv4_plugin import synthetic as S
+    from oracle import moe_oracle as O
+    cfg = _cfg()
+    T = a.tokens
+    gw, bias = S.make_gate(cfg, 0, 3)
+    x = S.make_tokens(cfg, 7, T, step=0)
+    w, idx = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+    need = sorted(set(idx.reshape(-1).tolist()))
+    experts = {e: S.make_expert(cfg, 0, e, 3) for e in need}
+    cache = {e: O.expert_weights_f32(experts[e]) for e in need}
+
+    def step():
+        ww, ii = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+        O.moe_routed(x, ww, ii, experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=cache)
+
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    value = T * a.steps / dt
+    line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16-rounded like the reference)",
+            "data": "synthetic (seeded; BASELINE config 1 distributions)", "impl": "reference",
+            "config": {"workload": f"cfg1 decode bf16 profile: T={T} tokens, H=4096, I=2048, E=256, top-8, "
+                                   "all experts resident", "tokens_per_step": T, "global_batch": T,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{a.steps} layer forwards (router + per-expert loop) of cfg1 T={T}; "
+                                       f"{len(need)} experts resident dequantised"},
+            "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ep(a, rank, world, device):
+    from dsv4_plugin.parallel_ep import run_ep_bench
+    line = run_ep_bench(a, rank, world, device, METRIC, UNIT, build_layer, _token_batches, Clocks,
+                        L2_FLUSH_BYTES)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    a = _args(argv)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -61,6 +61,27 @@ static void untile_scales(const uint8_t* src, int64_t rows, int64_t k, uint8_t* 
   }
 }
 
+// Packed weights [rows, k/2] (row-major, two E2M1 per byte) -> 8 KiB blocks of
+// 128 rows x 128 elements: block (r/128, k/128) at ((r/128)*(k/128) + k/128)*8192,
+// row r%128 of the block at (r%128)*64.  One TMA box = one contiguous block.
+static void tile_weights(const uint8_t* w, int64_t rows, int64_t k, uint8_t* dst, int64_t row_base) {
+  const int64_t kt_n = k / 128, row_bytes = k / 2;
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t R = row_base + r;
+    for (int64_t kt = 0; kt < kt_n; ++kt)
+      memcpy(dst + ((R / 128) * kt_n + kt) * 8192 + (R % 128) * 64, w + r * row_bytes + kt * 64, 64);
+  }
+}
+
+static void untile_weights(const uint8_t* src, int64_t rows, int64_t k, uint8_t* w, int64_t row_base) {
+  const int64_t kt_n = k / 128, row_bytes = k / 2;
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t R = row_base + r;
+    for (int64_t kt = 0; kt < kt_n; ++kt)
+      memcpy(w + r * row_bytes + kt * 64, src + ((R / 128) * kt_n + kt) * 8192 + (R % 128) * 64, 64);
+  }
+}
+
 }  // namespace dsv4
 
 using namespace dsv4;
@@ -83,9 +104,9 @@ extern "C" int dsv4_pack_expert_host(const uint8_t* w1p, const uint8_t* w1s, con
                  "hidden and inter must be positive multiples of 128");
   const SlotLayout L = slot_layout(hidden, inter);
   const int64_t H = hidden, I = inter;
-  memcpy(slot + L.w13p, w1p, (size_t)(I * H / 2));
-  memcpy(slot + L.w13p + I * H / 2, w3p, (size_t)(I * H / 2));
-  memcpy(slot + L.w2p, w2p, (size_t)(H * I / 2));
+  tile_weights(w1p, I, H, slot + L.w13p, 0);
+  tile_weights(w3p, I, H, slot + L.w13p, I);
+  tile_weights(w2p, H, I, slot + L.w2p, 0);
   tile_scales(w1s, I, H, slot + L.sf13, 0);
   tile_scales(w3s, I, H, slot + L.sf13, I);
   tile_scales(w2s, H, I, slot + L.sf2, 0);
@@ -100,9 +121,9 @@ extern "C" int dsv4_unpack_expert_host(const uint8_t* slot, int32_t hidden, int3
                  "hidden and inter must be positive multiples of 128");
   const SlotLayout L = slot_layout(hidden, inter);
   const int64_t H = hidden, I = inter;
-  memcpy(w1p, slot + L.w13p, (size_t)(I * H / 2));
-  memcpy(w3p, slot + L.w13p + I * H / 2, (size_t)(I * H / 2));
-  memcpy(w2p, slot + L.w2p, (size_t)(H * I / 2));
+  untile_weights(slot + L.w13p, I, H, w1p, 0);
+  untile_weights(slot + L.w13p, I, H, w3p, I);
+  untile_weights(slot + L.w2p, H, I, w2p, 0);
   untile_scales(slot + L.sf13, I, H, w1s, 0);
   untile_scales(slot + L.sf13, I, H, w3s, I);
   untile_scales(slot + L.sf2, H, I, w2s, 0);

@@ -4,19 +4,24 @@
 // (128 rows per tile), the tokens routed to that expert are the N side
 // (64 per tile), K runs along the hidden (or intermediate) dimension:
 //     D[w_row, token] = sum_k W[w_row, k] * X[token, k]
-// A = packed E2M1 weights straight from the expert slot (TMA type
-// 16U4_ALIGN16B expands them to the one-byte-per-element shared-memory form
-// the f8f6f4 tensor-core path reads), with their E8M0 per-32 scales;
+// A = packed E2M1 weights straight from the expert slot, one contiguous 8 KiB
+// block per 128x128 tile (TMA type 16U4_ALIGN16B expands them to the
+// one-byte-per-element shared-memory form the f8f6f4 tensor-core path
+// reads), with their E8M0 per-32 scales;
 // B = E4M3 activations (bf16 profile) or E2M1 activations (a4w4), with E8M0
 // per-32 scales.  One tcgen05.mma.kind::mxf8f6f4.block_scale per 32 of K.
 // The products equal those of bf16(dequant(W)) x bf16(fp8_roundtrip(X)) of
 // the reference exactly, so only accumulation order differs.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over tiles):
-//   warp 0     producer: TMA for A and B, bulk copy of A scales, gather of
-//              B scales into the tensor-core order, one mbarrier per stage;
+// Warp roles (320 threads, one CTA per SM, persistent over tiles):
+//   warp 0     producer: TMA for A and B, bulk copies of the A and B scale
+//              atoms, one mbarrier per stage;
 //   warp 1     TMEM owner and MMA issuer (one thread);
-//   warps 2-5  epilogue: TMEM -> registers -> fused math -> global.
+//   warps 2-9  epilogue: TMEM -> registers -> fused math -> global; two
+//              warps per TMEM lane quarter, each taking half the columns.
+// Every role walks the same tile sequence and loads the next tile's
+// metadata (chunk, slot) one tile ahead, so tile boundaries cost no
+// dependent global-memory round trip.
 // NUM_A = 2 runs the gate (w1) and up (w3) projections of the same 128
 // intermediate rows into two accumulators; NUM_A = 1 runs the down
 // projection.  Accumulators are double-buffered in TMEM so the epilogue of
@@ -30,7 +35,8 @@ namespace dsv4 {
 constexpr int G_BM = 128;
 constexpr int G_BN = 64;
 constexpr int G_BK = 128;
-constexpr int G_THREADS = 192;
+constexpr int G_EPI_WARPS = 8;
+constexpr int G_THREADS = 64 + 32 * G_EPI_WARPS;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint32_t G_SF_COL = 256;   // TMEM columns 256..267 hold scale factors
 
@@ -46,6 +52,7 @@ struct GemmCfg {
   static constexpr int STAGES = NUM_A == 2 ? 5 : 8;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * G_BN * 4 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 struct GemmParams {
@@ -55,15 +62,15 @@ struct GemmParams {
   int k_tiles;               // K / 128
   int a_row_tiles;           // tiles of 128 rows per A matrix (= tiles per chunk)
   int a1_row_offset;         // row offset of the second A matrix (w3) in the map
-  const uint32_t* b_sf;      // activation scales [k_tiles][p_cap], 4 bytes per row
-  int64_t p_cap;
+  const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, 64-row block)
+  int64_t rb_cap;            // 64-row blocks per k-tile in b_sf / out_sf
   const int4* chunks;        // {expert, row0, nrows, 0}
   const int* n_chunks;
   const int* slot_of;        // expert -> slot
   int n_slots;               // slots in the arena; other values are rejected
   const float* sorted_w;     // route weight per sorted row (gate/up epilogue)
   uint8_t* out_q;            // gate/up: next activation (E4M3 [p_cap][I] or E2M1 [p_cap][I/2])
-  uint32_t* out_sf;          // gate/up: its scales [I/128][p_cap]
+  uint8_t* out_sf;           // gate/up: its scale atoms, same layout as b_sf
   uint16_t* out_bf16;        // down: [p_cap][H] bf16
   int out_ld;                // elements per output row (I or H)
   float swiglu_limit;
@@ -76,7 +83,36 @@ __device__ __forceinline__ float warp_max_f(float v) {
   return v;
 }
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+// SiLU with the fast exponential and division intrinsics: relative error
+// ~1e-6, far inside the layer's tolerance; v -> -inf gives -0.
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
+// max over the warp of non-negative floats (their bit patterns order like
+// unsigned integers): one redux instruction.
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+}
+
+struct TileInfo {
+  int slot;   // < 0: skip (expert not resident)
+  int row0;   // first row of the 64-row chunk
+  int nrows;  // valid rows in the chunk
+  int mt;     // 128-row tile of the weight matrix
+};
+
+__device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_tiles) {
+  TileInfo ti{-1, 0, 0, 0};
+  if (t < n_tiles) {
+    const int c = t / p.a_row_tiles;
+    const int4 ch = p.chunks[c];
+    const int s = p.slot_of[ch.x];
+    ti.slot = (s >= 0 && s < p.n_slots) ? s : -1;
+    ti.row0 = ch.y;
+    ti.nrows = ch.z;
+    ti.mt = t - c * p.a_row_tiles;
+  }
+  return ti;
+}
 
 template <int NUM_A, bool B_FP4, int EPI>
 __global__ void __launch_bounds__(G_THREADS, 1)
@@ -104,7 +140,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 4);
+      mbar_init(&accempty[b], G_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *epi_fail = 0;
@@ -125,81 +161,77 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
   const int n_tiles = (*p.n_chunks) * p.a_row_tiles;
   const int k_tiles = p.k_tiles;
+  const int step = gridDim.x;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    const uint64_t pol_w = policy_evict_first();
-    const uint64_t pol_x = policy_evict_last();
-    int stage = 0;
-    uint32_t phase = 0;
-    int issued = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-      const int c = t / p.a_row_tiles, mt = t - c * p.a_row_tiles;
-      const int4 ch = p.chunks[c];
-      const int slot = p.slot_of[ch.x];
-      if (slot < 0 || slot >= p.n_slots) {
-        set_status(p.status, DSV4_ENOTFOUND);
-        continue;
-      }
-      const uint8_t* sf_base = p.arena + (int64_t)slot * p.slot_bytes + p.sfa_off;
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
-          ok = false;
-          break;
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+      for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
+        const TileInfo nxt = load_tile(p, t + step, n_tiles);
+        if (cur.slot < 0) {
+          set_status(p.status, DSV4_ENOTFOUND);
+          cur = nxt;
+          continue;
         }
-        uint8_t* st = smem + stage * C::STAGE_BYTES;
-        uint8_t* sA0 = st;
-        uint8_t* sA1 = st + C::A_BYTES;
-        uint8_t* sB = st + NUM_A * C::A_BYTES;
-        uint8_t* sSFA = sB + C::B_BYTES;
-        uint8_t* sSFB = sSFA + NUM_A * C::SF_BYTES;
-        // B scales: row n of the tile -> byte (n%32)*16 + (n/32)*4
-        const uint32_t* bsf = p.b_sf + (int64_t)kt * p.p_cap + ch.y;
-#pragma unroll
-        for (int h = 0; h < G_BN / 32; ++h) {
-          const int n = lane + 32 * h;
-          *reinterpret_cast<uint32_t*>(sSFB + (n & 31) * 16 + (n >> 5) * 4) = bsf[n];
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
+        const uint8_t* sf_base = p.arena + (int64_t)cur.slot * p.slot_bytes + p.sfa_off;
+        const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / G_BN) * C::SF_BYTES;
+        const int rt1 = p.a1_row_offset / G_BM + cur.mt;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + stage * C::STAGE_BYTES;
+          uint8_t* sA0 = st;
+          uint8_t* sA1 = st + C::A_BYTES;
+          uint8_t* sB = st + NUM_A * C::A_BYTES;
+          uint8_t* sSFA = sB + C::B_BYTES;
+          uint8_t* sSFB = sSFA + NUM_A * C::SF_BYTES;
           constexpr uint32_t a_tx = G_BM * G_BK / 2;  // packed bytes of one A box
           constexpr uint32_t b_tx = B_FP4 ? G_BN * G_BK / 2 : G_BN * G_BK;
-          mbar_expect_tx(&full[stage], NUM_A * (a_tx + C::SF_BYTES) + b_tx);
-          tma_load_3d(sA0, &tmA, &full[stage], kt * G_BK, mt * G_BM, slot, pol_w);
-          bulk_load(sSFA, sf_base + ((int64_t)mt * k_tiles + kt) * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_w);
+          mbar_expect_tx(&full[stage], NUM_A * (a_tx + C::SF_BYTES) + b_tx + C::SF_BYTES);
+          tma_load_5d(sA0, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
+          bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_w);
           if (NUM_A == 2) {
-            tma_load_3d(sA1, &tmA, &full[stage], kt * G_BK, p.a1_row_offset + mt * G_BM, slot, pol_w);
-            const int rt1 = p.a1_row_offset / G_BM + mt;
+            tma_load_5d(sA1, &tmA, &full[stage], 0, 0, kt, rt1, cur.slot, pol_w);
             bulk_load(sSFA + C::SF_BYTES, sf_base + ((int64_t)rt1 * k_tiles + kt) * C::SF_BYTES, C::SF_BYTES,
                       &full[stage], pol_w);
           }
-          tma_load_2d(sB, &tmB, &full[stage], kt * G_BK, ch.y, pol_x);
+          tma_load_2d(sB, &tmB, &full[stage], kt * G_BK, cur.row0, pol_x);
+          // B scales: the atom of (k-tile kt, this 64-row chunk), already in tensor-core order
+          bulk_load(sSFB, sfb_base + (int64_t)kt * p.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
           mbar_arrive(&full[stage]);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        ++issued;
-        if (++stage == C::STAGES) {
-          stage = 0;
-          phase ^= 1u;
+        cur = nxt;
+      }
+      if (!ok) {
+        // let copies already in flight land before the CTA can exit
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < C::STAGES && i < issued; ++i) {
+          if (--s < 0) {
+            s = C::STAGES - 1;
+            ph ^= 1u;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], ph) && globaltimer_ns() - t0 < DSV4_WAIT_NS) {
+          }
         }
       }
     }
-    if (!ok && lane == 0) {
-      // let copies already in flight land before the CTA can exit
-      int s = stage;
-      uint32_t ph = phase;
-      for (int i = 0; i < C::STAGES && i < issued; ++i) {
-        if (--s < 0) {
-          s = C::STAGES - 1;
-          ph ^= 1u;
-        }
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[s], ph) && globaltimer_ns() - t0 < DSV4_WAIT_NS) {
-        }
-      }
-    }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -209,10 +241,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t aphase = 0;
       bool ok = true;
       const uint32_t sfa0 = tmem + G_SF_COL, sfa1 = tmem + G_SF_COL + 4, sfb = tmem + G_SF_COL + 8;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-        const int c = t / p.a_row_tiles;
-        const int slot = p.slot_of[p.chunks[c].x];
-        if (slot < 0 || slot >= p.n_slots) continue;
+      TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+      for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
+        const TileInfo nxt = load_tile(p, t + step, n_tiles);
+        if (cur.slot < 0) {
+          cur = nxt;
+          continue;
+        }
+        cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)abuf * (NUM_A * G_BN);
@@ -263,32 +299,50 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    constexpr int HALF = G_BN / 2;     // columns per epilogue warp
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int ew = warp - 2;           // 0..3
+    const int half = (warp - 2) >> 2;  // which half of the 64 columns
     const int i = q * 32 + lane;       // row inside the 128-row tile
+    const int c0 = half * HALF;        // first column of this warp
     int abuf = 0;
     uint32_t aphase = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-      const int c = t / p.a_row_tiles, mt = t - c * p.a_row_tiles;
-      const int4 ch = p.chunks[c];
-      const int slot = p.slot_of[ch.x];
-      if (slot < 0 || slot >= p.n_slots) continue;
-      const int row0 = ch.y, nrows = ch.z;
-      // all four epilogue warps take the same decision: a failed wait in any
-      // of them ends the loop for all (the named barriers below need all 4)
+    TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+    for (int t = blockIdx.x; t < n_tiles; t += step) {
+      const TileInfo nxt = load_tile(p, t + step, n_tiles);
+      if (cur.slot < 0) {
+        cur = nxt;
+        continue;
+      }
+      const int row0 = cur.row0, nrows = cur.nrows, mt = cur.mt;
+      cur = nxt;
+      float w[HALF];
+      if constexpr (EPI != EPI_STORE_BF16) {
+        // route weights of this warp's 32 rows (row0 is a multiple of 64)
+        const float4* wp = reinterpret_cast<const float4*>(p.sorted_w + row0 + c0);
+#pragma unroll
+        for (int j = 0; j < HALF / 4; ++j) {
+          const float4 v = wp[j];
+          w[4 * j] = v.x;
+          w[4 * j + 1] = v.y;
+          w[4 * j + 2] = v.z;
+          w[4 * j + 3] = v.w;
+        }
+      }
+      // all epilogue warps take the same decision: a failed wait in any of
+      // them ends the loop for all (the named barriers below need all 8)
       if (!mbar_wait(&accfull[abuf], aphase, p.status) && lane == 0) atomicOr(epi_fail, 1);
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * G_EPI_WARPS);
       if (*reinterpret_cast<volatile int*>(epi_fail) != 0) break;
       tc_fence_after();
-      float acc0[G_BN];
-      float acc1[NUM_A == 2 ? G_BN : 1];
+      float acc0[HALF];
+      float acc1[NUM_A == 2 ? HALF : 1];
       (void)acc1;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)abuf * (NUM_A * G_BN);
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)abuf * (NUM_A * G_BN) + c0;
 #pragma unroll
-      for (int j = 0; j < G_BN / 16; ++j) tmem_ld16(tbase + j * 16, acc0 + j * 16);
+      for (int j = 0; j < HALF / 16; ++j) tmem_ld16(tbase + j * 16, acc0 + j * 16);
       if constexpr (NUM_A == 2) {
 #pragma unroll
-        for (int j = 0; j < G_BN / 16; ++j) tmem_ld16(tbase + G_BN + j * 16, acc1 + j * 16);
+        for (int j = 0; j < HALF / 16; ++j) tmem_ld16(tbase + G_BN + j * 16, acc1 + j * 16);
       }
       tc_wait_ld();
       tc_fence_before();
@@ -300,58 +354,67 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
 
       if constexpr (EPI == EPI_STORE_BF16) {
-        uint16_t* dst = p.out_bf16 + (int64_t)row0 * p.out_ld + mt * G_BM + i;
+        uint16_t* dst = p.out_bf16 + (int64_t)(row0 + c0) * p.out_ld + mt * G_BM + i;
 #pragma unroll
-        for (int n = 0; n < G_BN; ++n)
-          if (n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+        for (int n = 0; n < HALF; ++n)
+          if (c0 + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
       } else {
         // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
         // bf16(h) is the input of the activation re-quantisation.
         const float lim = p.swiglu_limit;
 #pragma unroll
-        for (int n = 0; n < G_BN; ++n) {
+        for (int n = 0; n < HALF; ++n) {
           float g = bf16r(acc0[n]);
           float u = bf16r(acc1[n]);
           if (lim > 0.f) {
             u = fminf(fmaxf(u, -lim), lim);
             g = fminf(g, lim);
           }
-          const float w = (n < nrows) ? p.sorted_w[row0 + n] : 0.f;
-          acc0[n] = bf16r(silu_f(g) * u * w);
+          acc0[n] = bf16r(silu_f(g) * u * w[n]);
         }
         if constexpr (EPI == EPI_SWIGLU_FP8) {
-          // per-token amax over the 128 rows of this tile = one 128-block of I
+          // per-token amax over the 128 rows of this tile = one 128-block of I:
+          // redux over the warp's 32 rows, then across the 4 lane quarters
+          float mine = 0.f;
 #pragma unroll
-          for (int n = 0; n < G_BN; ++n) {
-            const float m = warp_max_f(fabsf(acc0[n]));
-            if (lane == 0) red[ew * G_BN + n] = m;
+          for (int n = 0; n < HALF; ++n) {
+            const float m = warp_max_nonneg(fabsf(acc0[n]));
+            if (lane == n) mine = m;
           }
-          named_bar_sync(1, 128);
-          uint8_t* dst = p.out_q + (int64_t)row0 * p.out_ld + mt * G_BM + i;
+          red[q * G_BN + c0 + lane] = mine;
+          named_bar_sync(1, 32 * G_EPI_WARPS);
+          const float amax_l = fmaxf(fmaxf(red[c0 + lane], red[G_BN + c0 + lane]),
+                                     fmaxf(red[2 * G_BN + c0 + lane], red[3 * G_BN + c0 + lane]));
+          const int e_l = fp8_scale_exp(amax_l);
+          uint8_t* dst = p.out_q + (int64_t)(row0 + c0) * p.out_ld + mt * G_BM + i;
 #pragma unroll
-          for (int n = 0; n < G_BN; ++n) {
-            if (n < nrows) {
-              const float amax = fmaxf(fmaxf(red[n], red[G_BN + n]), fmaxf(red[2 * G_BN + n], red[3 * G_BN + n]));
-              const int e = fp8_scale_exp(amax);
+          for (int n = 0; n < HALF; ++n) {
+            const int e = __shfl_sync(0xffffffffu, e_l, n);
+            if (c0 + n < nrows) {
               const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
               dst[(int64_t)n * p.out_ld] = (uint8_t)e4m3_byte(v);
-              if (i == 0) p.out_sf[(int64_t)mt * p.p_cap + row0 + n] = (uint32_t)(e + 127) * 0x01010101u;
             }
           }
-          named_bar_sync(1, 128);
+          if (q == 0 && c0 + lane < nrows) {
+            const int n = c0 + lane;
+            *reinterpret_cast<uint32_t*>(p.out_sf + ((int64_t)mt * p.rb_cap + row0 / G_BN) * 512 + (n & 31) * 16 +
+                                         (n >> 5) * 4) = (uint32_t)(e_l + 127) * 0x01010101u;
+          }
+          named_bar_sync(1, 32 * G_EPI_WARPS);
         } else {
           // per-token amax over the 32 rows of this warp = one 32-block of I
-          uint8_t* dst = p.out_q + (int64_t)row0 * (p.out_ld / 2) + (mt * G_BM + i) / 2;
-          uint8_t* sfd = reinterpret_cast<uint8_t*>(p.out_sf) + ((int64_t)mt * p.p_cap + row0) * 4 + q;
+          uint8_t* dst = p.out_q + (int64_t)(row0 + c0) * (p.out_ld / 2) + (mt * G_BM + i) / 2;
+          uint8_t* sfd = p.out_sf + ((int64_t)mt * p.rb_cap + row0 / G_BN) * 512 + q;
 #pragma unroll
-          for (int n = 0; n < G_BN; ++n) {
-            if (n < nrows) {
-              const float amax = warp_max_f(fabsf(acc0[n]));
+          for (int n = 0; n < HALF; ++n) {
+            if (c0 + n < nrows) {
+              const float amax = warp_max_nonneg(fabsf(acc0[n]));
               const int e = mx_scale_exp(amax);
               const uint32_t code = e2m1_code(acc0[n] * pow2_any(-e));
               const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
               if ((lane & 1) == 0) dst[(int64_t)n * (p.out_ld / 2)] = (uint8_t)(code | (hi << 4));
-              if (lane == 0) sfd[(int64_t)n * 4] = (uint8_t)(e + 127);
+              const int cn = c0 + n;
+              if (lane == 0) sfd[(cn & 31) * 16 + (cn >> 5) * 4] = (uint8_t)(e + 127);
             }
           }
         }

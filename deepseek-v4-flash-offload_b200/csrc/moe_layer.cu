@@ -17,7 +17,9 @@ namespace dsv4 {
 // exclusive scan, then a stable scatter in chunks of 1024 assignments: rank
 // inside a warp from __match_any_sync, rank across warps from a per-warp,
 // per-expert count table.  Also emits the active-expert list and the GEMM
-// work chunks (<= 64 rows of one expert each).
+// work chunks.  With pad > 1 every expert's group starts at a multiple of
+// pad rows (the GEMM tile height); padding positions get sorted_flat = -1
+// and each chunk is one pad-row block of one expert.
 // ---------------------------------------------------------------------------
 constexpr int AL_THREADS = 1024;
 
@@ -53,7 +55,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                      int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
                      float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
-                     int chunk_rows, int* status) {
+                     int pad, int* status) {
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
@@ -74,14 +76,19 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  // exclusive scan of counts (E <= 1024: one expert per thread)
+  // exclusive scan of the (padded) group sizes (E <= 1024: one expert per thread)
   int total = 0;
   const int c = tid < E ? cnt[tid] : 0;
-  const int off = block_exclusive_scan(c, scratch, &total);
+  const int cpad = (c + pad - 1) / pad * pad;
+  const int off = block_exclusive_scan(cpad, scratch, &total);
   if (tid < E) {
     run[tid] = off;
     counts[tid] = c;
     offsets[tid] = off;
+    for (int r = off + c; r < off + cpad; ++r) {
+      sorted_flat[r] = -1;
+      if (sorted_w) sorted_w[r] = 0.f;
+    }
   }
   if (tid == 0) offsets[E] = total;
   __syncthreads();
@@ -126,14 +133,14 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   const int apos = block_exclusive_scan(flag, scratch, &nact);
   if (flag) active[apos] = tid;
   if (tid == 0) *n_active = nact;
-  // work chunks of <= chunk_rows rows
+  // work chunks: one pad-row block of one expert each
   if (chunks) {
-    const int nch = tid < E ? (cnt[tid] + chunk_rows - 1) / chunk_rows : 0;
+    const int nch = cpad / pad;
     int nchunk_total = 0;
     const int cpos = block_exclusive_scan(nch, scratch, &nchunk_total);
     for (int j = 0; j < nch; ++j) {
-      const int r0 = off + j * chunk_rows;
-      chunks[cpos + j] = make_int4(tid, r0, min(chunk_rows, c - j * chunk_rows), 0);
+      const int r0 = off + j * pad;
+      chunks[cpos + j] = make_int4(tid, r0, min(pad, c - j * pad), 0);
     }
     if (tid == 0) *n_chunks = nchunk_total;
   }
@@ -141,12 +148,19 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 
 // ---------------------------------------------------------------------------
 // activation quant + gather into the GEMM B operand.  Sorted row p reads token
-// sorted_flat[p] / topk.  Scales go to [K/128][p_cap] words, one byte per
-// 32-block (FP8: the per-128 exponent replicated four times).
+// sorted_flat[p] / topk (padding rows, sorted_flat < 0, are skipped).  Scales
+// go to 512-byte atoms, one per (128-column k-tile kt, 64-row block rb) at
+// (kt * rb_cap + rb) * 512, row n of the block at (n%32)*16 + (n/32)*4, one
+// byte per 32-block (FP8: the per-128 exponent replicated four times): the
+// order the tensor cores read after a 32x128b.warpx4 copy.
 // ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, int64_t rb_cap) {
+  return ((int64_t)kt * rb_cap + row / 64) * 512 + (row % 32) * 16 + ((row % 64) / 32) * 4;
+}
+
 __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
-                                        const int* __restrict__ n_rows, int topk, int K, int64_t p_cap,
-                                        uint8_t* __restrict__ q, uint32_t* __restrict__ sf) {
+                                        const int* __restrict__ n_rows, int topk, int K, int64_t rb_cap,
+                                        uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
   const int64_t nblk = (int64_t)(*n_rows) * kblk;
@@ -155,7 +169,9 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
   for (int64_t b = warp0; b < nblk; b += nwarps) {
     const int64_t p = b / kblk;
     const int kb = (int)(b - p * kblk);
-    const int64_t tok = sorted_flat[p] / topk;
+    const int src = sorted_flat[p];
+    if (src < 0) continue;
+    const int64_t tok = src / topk;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -167,13 +183,13 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
 #pragma unroll
     for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv, -448.f), 448.f)) << (8 * i);
     *reinterpret_cast<uint32_t*>(q + p * K + kb * 128 + lane * 4) = o;
-    if (lane == 0) sf[(int64_t)kb * p_cap + p] = (uint32_t)(e + 127) * 0x01010101u;
+    if (lane == 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(p, kb, rb_cap)) = (uint32_t)(e + 127) * 0x01010101u;
   }
 }
 
 __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
-                                          const int* __restrict__ n_rows, int topk, int K, int64_t p_cap,
-                                          uint8_t* __restrict__ q, uint32_t* __restrict__ sf) {
+                                          const int* __restrict__ n_rows, int topk, int K, int64_t rb_cap,
+                                          uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
   const int64_t nblk = (int64_t)(*n_rows) * kblk;
@@ -182,7 +198,9 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
   for (int64_t b = warp0; b < nblk; b += nwarps) {
     const int64_t p = b / kblk;
     const int kb = (int)(b - p * kblk);
-    const int64_t tok = sorted_flat[p] / topk;
+    const int src = sorted_flat[p];
+    if (src < 0) continue;
+    const int64_t tok = src / topk;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -194,8 +212,7 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
     const uint32_t packed = e2m1_code(v[0] * inv) | (e2m1_code(v[1] * inv) << 4) | (e2m1_code(v[2] * inv) << 8) |
                             (e2m1_code(v[3] * inv) << 12);
     *reinterpret_cast<uint16_t*>(q + p * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
-    if ((lane & 7) == 0)
-      reinterpret_cast<uint8_t*>(sf)[((int64_t)kb * p_cap + p) * 4 + (lane >> 3)] = (uint8_t)(e + 127);
+    if ((lane & 7) == 0) sf[act_sf_offset(p, kb, rb_cap) + (lane >> 3)] = (uint8_t)(e + 127);
   }
 }
 
@@ -224,6 +241,31 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
       const uint4 r = *reinterpret_cast<const uint4*>(out + (int64_t)pos[j] * H + c);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16_from_bits(w[q] & 0xffffu);
+        acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = (uint32_t)bf16_bits(acc[2 * q]) | ((uint32_t)bf16_bits(acc[2 * q + 1]) << 16);
+    *reinterpret_cast<uint4*>(y + t * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Same sum, rows taken in the caller's order (no sorting).
+__global__ void combine_ordered_kernel(const uint16_t* __restrict__ rows, const int32_t* __restrict__ order,
+                                       int topk, int H, uint16_t* __restrict__ y, int64_t T) {
+  const int64_t t = blockIdx.x;
+  if (t >= T) return;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < topk; ++j) {
+      const int pos = order[t * topk + j];
+      if (pos < 0) continue;
+      const uint4 r = *reinterpret_cast<const uint4*>(rows + (int64_t)pos * H + c);
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -287,8 +329,9 @@ static int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
 static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens) {
   WsLayout w;
   w.p_max = max_tokens * topk;
-  w.p_cap = (w.p_max + 127) / 128 * 128 + 128;
-  w.max_chunks = w.p_max / G_BN + E + 1;
+  // every expert group is padded to a multiple of G_BN rows
+  w.p_cap = (w.p_max + (G_BN - 1) * std::min<int64_t>(E, w.p_max) + G_BN - 1) / G_BN * G_BN + G_BN;
+  w.max_chunks = w.p_cap / G_BN + 1;
   int64_t o = 0;
   auto take = [&](int64_t bytes) {
     const int64_t at = o;
@@ -301,14 +344,14 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   w.active = take(4 * E);
   w.n_active = take(4);
   w.n_chunks = take(4);
-  w.sorted_flat = take(4 * std::max<int64_t>(w.p_max, 1));
+  w.sorted_flat = take(4 * w.p_cap);  // indexed by padded row position
   w.inv = take(4 * std::max<int64_t>(w.p_max, 1));
-  w.sorted_w = take(4 * std::max<int64_t>(w.p_max, 1));
+  w.sorted_w = take(4 * w.p_cap);
   w.chunks = take(16 * w.max_chunks);
   w.xq = take(w.p_cap * H);
-  w.xsf = take(4 * (H / 128) * w.p_cap);
+  w.xsf = take((H / 128) * (w.p_cap / G_BN) * 512);
   w.hq = take(w.p_cap * I);
-  w.hsf = take(4 * (I / 128) * w.p_cap);
+  w.hsf = take((I / 128) * (w.p_cap / G_BN) * 512);
   w.out = take(2 * w.p_cap * H);
   w.bytes = o;
   return w;
@@ -328,6 +371,12 @@ struct dsv4_moe_plan {
   uint8_t* ws = nullptr;
   dsv4::WsLayout wl;
   CUtensorMap tmA13, tmA2, tmB1_fp8, tmB1_fp4, tmB2_fp8, tmB2_fp4;
+  bool timing = false;
+  cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  ~dsv4_moe_plan() {
+    for (auto& e : ev)
+      if (e) cudaEventDestroy(e);
+  }
 };
 
 using namespace dsv4;
@@ -385,15 +434,19 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   const uint64_t H = hidden, I = inter, SB = (uint64_t)p->slot.bytes, PC = (uint64_t)wl.p_cap;
   const CUtensorMapDataType U4 = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   int rc;
-  {  // w13: [slots][2I rows][H] E2M1
-    const uint64_t dims[3] = {H, 2 * I, (uint64_t)n_slots}, str[2] = {H / 2, SB};
-    const uint32_t box[3] = {G_BK, G_BM, 1};
-    if ((rc = make_map(&p->tmA13, U4, 3, slot_arena + p->slot.w13p, dims, str, box, "w13")) != 0) return rc;
+  // weights are stored as contiguous 8 KiB blocks of 128 rows x 128 E2M1
+  // elements: dims (element in block row, row in block, k tile, row tile, slot)
+  {  // w13: 2I rows, K = H
+    const uint64_t kt = H / 128, rt = 2 * I / 128;
+    const uint64_t dims[5] = {128, 128, kt, rt, (uint64_t)n_slots}, str[4] = {64, 8192, kt * 8192, SB};
+    const uint32_t box[5] = {G_BK, G_BM, 1, 1, 1};
+    if ((rc = make_map(&p->tmA13, U4, 5, slot_arena + p->slot.w13p, dims, str, box, "w13")) != 0) return rc;
   }
-  {  // w2: [slots][H rows][I]
-    const uint64_t dims[3] = {I, H, (uint64_t)n_slots}, str[2] = {I / 2, SB};
-    const uint32_t box[3] = {G_BK, G_BM, 1};
-    if ((rc = make_map(&p->tmA2, U4, 3, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
+  {  // w2: H rows, K = I
+    const uint64_t kt = I / 128, rt = H / 128;
+    const uint64_t dims[5] = {128, 128, kt, rt, (uint64_t)n_slots}, str[4] = {64, 8192, kt * 8192, SB};
+    const uint32_t box[5] = {G_BK, G_BM, 1, 1, 1};
+    if ((rc = make_map(&p->tmA2, U4, 5, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
   }
   const uint32_t bbox[2] = {G_BK, G_BN};
   {
@@ -441,26 +494,34 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   int32_t* n_active = wsp<int32_t>(p, w.n_active);
   int* n_chunks = wsp<int>(p, w.n_chunks);
   const size_t al_smem = (size_t)(3 * p->E + 32) * 4 + (size_t)32 * p->E * 2;
+  auto mark = [&](int i) {
+    if (p->timing) cudaEventRecord(p->ev[i], st);
+  };
+  mark(0);
   moe_align_kernel<<<1, AL_THREADS, al_smem, st>>>(
       route_indices, P, p->topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
       sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w), wsp<int4>(p, w.chunks),
       n_chunks, G_BN, status);
+  mark(1);
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
-  // the gather reads the valid row count from the align output (offsets[E])
+  // the gather reads the padded row count from the align output (offsets[E])
   const int* n_rows = wsp<int>(p, w.offsets) + p->E;
+  const int64_t rb_cap = w.p_cap / G_BN;
   {
-    const int64_t warps = (int64_t)P * (p->H / 128);
+    const int64_t rows_max = std::min<int64_t>(w.p_cap, (int64_t)P + (int64_t)(G_BN - 1) * std::min(P, p->E));
+    const int64_t warps = rows_max * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
     if (fp4)
       quant_gather_mxfp4_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
-                                                                  p->topk, p->H, w.p_cap, p->ws + w.xq,
-                                                                  wsp<uint32_t>(p, w.xsf));
+                                                                  p->topk, p->H, rb_cap, p->ws + w.xq,
+                                                                  p->ws + w.xsf);
     else
       quant_gather_fp8_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
-                                                                p->topk, p->H, w.p_cap, p->ws + w.xq,
-                                                                wsp<uint32_t>(p, w.xsf));
+                                                                p->topk, p->H, rb_cap, p->ws + w.xq,
+                                                                p->ws + w.xsf);
   }
+  mark(2);
   GemmParams g1{};
   g1.arena = p->arena;
   g1.slot_bytes = p->slot.bytes;
@@ -468,15 +529,15 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g1.k_tiles = p->H / 128;
   g1.a_row_tiles = p->I / 128;
   g1.a1_row_offset = p->I;
-  g1.b_sf = wsp<uint32_t>(p, w.xsf);
-  g1.p_cap = w.p_cap;
+  g1.b_sf = p->ws + w.xsf;
+  g1.rb_cap = rb_cap;
   g1.chunks = wsp<int4>(p, w.chunks);
   g1.n_chunks = n_chunks;
   g1.slot_of = slot_of_expert;
   g1.n_slots = (int)p->n_slots;
   g1.sorted_w = wsp<float>(p, w.sorted_w);
   g1.out_q = p->ws + w.hq;
-  g1.out_sf = wsp<uint32_t>(p, w.hsf);
+  g1.out_sf = p->ws + w.hsf;
   g1.out_ld = p->I;
   g1.swiglu_limit = p->swiglu_limit;
   g1.status = status;
@@ -485,22 +546,47 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g2.k_tiles = p->I / 128;
   g2.a_row_tiles = p->H / 128;
   g2.a1_row_offset = 0;
-  g2.b_sf = wsp<uint32_t>(p, w.hsf);
+  g2.b_sf = p->ws + w.hsf;
   g2.out_q = nullptr;
   g2.out_sf = nullptr;
   g2.out_bf16 = wsp<uint16_t>(p, w.out);
   g2.out_ld = p->H;
   const dim3 grid(p->num_sms), block(G_THREADS);
-  if (fp4) {
+  if (fp4)
     moe_gemm_kernel<2, true, EPI_SWIGLU_MXFP4><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp4, g1);
-    moe_gemm_kernel<1, true, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp4, g2);
-  } else {
+  else
     moe_gemm_kernel<2, false, EPI_SWIGLU_FP8><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp8, g1);
+  mark(3);
+  if (fp4)
+    moe_gemm_kernel<1, true, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp4, g2);
+  else
     moe_gemm_kernel<1, false, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp8, g2);
-  }
+  mark(4);
   combine_kernel<<<(unsigned)n_tokens, std::min(1024, p->H / 8), 0, st>>>(wsp<uint16_t>(p, w.out), inv, p->topk,
                                                                           p->H, (uint16_t*)y_bf16, n_tokens);
+  mark(5);
   DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_enable_timing(dsv4_moe_plan* p, int32_t enable) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p, "null plan");
+  DSV4_CUDA_CHECK(cudaSetDevice(p->device));
+  if (enable)
+    for (auto& e : p->ev)
+      if (!e) DSV4_CUDA_CHECK(cudaEventCreate(&e));
+  p->timing = enable != 0;
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_stage_times(dsv4_moe_plan* p, float* ms, int32_t n) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p && ms, "null pointer");
+  DSV4_CHECK_ARG(p->timing, "timing is not enabled on this plan");
+  DSV4_CUDA_CHECK(cudaSetDevice(p->device));
+  DSV4_CUDA_CHECK(cudaEventSynchronize(p->ev[5]));
+  for (int i = 0; i < 5 && i < n; ++i) DSV4_CUDA_CHECK(cudaEventElapsedTime(&ms[i], p->ev[i], p->ev[i + 1]));
   DSV4_API_END
 }
 
@@ -547,7 +633,21 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
       indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-      nullptr, nullptr, nullptr, 64, status);
+      nullptr, nullptr, nullptr, 1, status);
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_combine_ordered(const void* rows_bf16, const int32_t* order, int64_t n_tokens, int32_t topk,
+                                        int32_t hidden, void* y_bf16, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(n_tokens >= 0 && topk > 0 && hidden > 0 && hidden % 8 == 0, "bad sizes");
+  if (n_tokens == 0) return DSV4_OK;
+  DSV4_CHECK_ARG(rows_bf16 && order && y_bf16, "null pointer");
+  DSV4_CHECK_ARG(((uintptr_t)rows_bf16 % 16) == 0 && ((uintptr_t)y_bf16 % 16) == 0, "rows and y must be 16-byte aligned");
+  if (int rc = bind_device_of(y_bf16, nullptr)) return rc;
+  combine_ordered_kernel<<<(unsigned)n_tokens, std::min(1024, hidden / 8), 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)rows_bf16, order, topk, hidden, (uint16_t*)y_bf16, n_tokens);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

@@ -46,13 +46,20 @@ __host__ __device__ __forceinline__ int64_t sf_atom_offset(int64_t r, int64_t kb
   return ((r / 128) * ktiles + kb / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (kb % 4);
 }
 
+// Byte offset of packed element pair (row r, element k0) in the 8 KiB tiled
+// weight blocks of a [rows, k] matrix.
+__host__ __device__ __forceinline__ int64_t w_tile_offset(int64_t r, int64_t k0, int64_t k) {
+  return ((r / 128) * (k / 128) + k0 / 128) * 8192 + (r % 128) * 64 + (k0 % 128) / 2;
+}
+
 __global__ void slot_dequant_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf,
                                     uint16_t* __restrict__ out, int64_t rows, int64_t k, int64_t row_base) {
   const int64_t kb = k / 32;
   const int64_t n = rows * kb;
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n; c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = c / kb, b = c - r * kb;
-    dequant_block32(w + r * (k / 2) + b * 16, sf[sf_atom_offset(row_base + r, b, k)], out + r * k + b * 32);
+    dequant_block32(w + w_tile_offset(row_base + r, b * 32, k), sf[sf_atom_offset(row_base + r, b, k)],
+                    out + r * k + b * 32);
   }
 }
 
@@ -156,8 +163,8 @@ extern "C" int dsv4_slot_dequant(const uint8_t* slot, int32_t hidden, int32_t in
   const int64_t items13 = (int64_t)inter * (hidden / 32), items2 = (int64_t)hidden * (inter / 32);
   slot_dequant_kernel<<<grid_for(items13, 256), 256, 0, st>>>(slot + L.w13p, slot + L.sf13, (uint16_t*)w1, inter,
                                                               hidden, 0);
-  slot_dequant_kernel<<<grid_for(items13, 256), 256, 0, st>>>(slot + L.w13p + (int64_t)inter * hidden / 2,
-                                                              slot + L.sf13, (uint16_t*)w3, inter, hidden, inter);
+  slot_dequant_kernel<<<grid_for(items13, 256), 256, 0, st>>>(slot + L.w13p, slot + L.sf13, (uint16_t*)w3, inter,
+                                                              hidden, inter);
   slot_dequant_kernel<<<grid_for(items2, 256), 256, 0, st>>>(slot + L.w2p, slot + L.sf2, (uint16_t*)w2, hidden,
                                                              inter, 0);
   DSV4_CUDA_CHECK(cudaGetLastError());

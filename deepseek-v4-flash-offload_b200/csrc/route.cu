@@ -1,7 +1,7 @@
 // Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
-//   phase 1: fp32 logits = float(x) @ gate_w^T, tiled through shared memory,
-//            split along H into fixed chunks (deterministic partial sums);
-//   phase 2: one warp per token: sum the chunks in order, score function,
+//   phase 1: fp32 logits = float(x) @ gate_w^T, gate rows staged in shared
+//            memory, one warp per dot product (deterministic);
+//   phase 2: one warp per token: score function,
 //            biased top-k (or hash table), unbiased weights, renormalise,
 //            scale.
 #include "capi_internal.h"
@@ -9,63 +9,59 @@
 
 namespace dsv4 {
 
-constexpr int RT_T = 16;    // tokens per tile
-constexpr int RT_E = 32;    // experts per tile
-constexpr int RT_H = 128;   // hidden chunk
-constexpr int RT_PAD = RT_H + 1;
 constexpr int RT_MAX_E = 256;
+constexpr int RT_TOK = 256;   // tokens per CTA (grid y)
 
+// logits[t, e] = sum_h float(x[t, h]) * w[e, h].  A CTA keeps EPB gate rows in
+// shared memory; each warp takes whole (token, expert-group) dot products,
+// lanes stride H in 4-element steps, then a fixed butterfly reduction: one
+// writer per logit, so the result is deterministic.
+template <int EPB>
 __global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __restrict__ x,
-                                                           const float* __restrict__ w, float* __restrict__ part,
+                                                           const float* __restrict__ w, float* __restrict__ logits,
                                                            int64_t T, int H, int E) {
-  __shared__ float xs[RT_T][RT_PAD];
-  __shared__ float ws[RT_E][RT_PAD];
-  const int e0 = blockIdx.x * RT_E;
-  const int64_t t0 = (int64_t)blockIdx.y * RT_T;
-  const int h0 = blockIdx.z * RT_H;
-  const int tid = threadIdx.x;
-  // x tile: 16 x 256 bf16 -> f32
-  for (int i = tid; i < RT_T * RT_H / 2; i += 256) {
-    const int r = i / (RT_H / 2), c = (i % (RT_H / 2)) * 2;
-    float a = 0.f, b = 0.f;
-    if (t0 + r < T) {
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(x + (t0 + r) * H + h0 + c);
-      a = bf16_from_bits(v & 0xffffu);
-      b = bf16_from_bits(v >> 16);
-    }
-    xs[r][c] = a;
-    xs[r][c + 1] = b;
-  }
-  // gate tile: 32 x 256 f32
-  for (int i = tid; i < RT_E * RT_H / 4; i += 256) {
-    const int r = i / (RT_H / 4), c = (i % (RT_H / 4)) * 4;
+  extern __shared__ float ws[];  // [EPB][H]
+  const int e0 = blockIdx.x * EPB;
+  for (int i = threadIdx.x * 4; i < EPB * H; i += blockDim.x * 4) {
+    const int r = i / H, c = i - r * H;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (e0 + r < E) v = *reinterpret_cast<const float4*>(w + (int64_t)(e0 + r) * H + h0 + c);
-    ws[r][c] = v.x;
-    ws[r][c + 1] = v.y;
-    ws[r][c + 2] = v.z;
-    ws[r][c + 3] = v.w;
+    if (e0 + r < E) v = *reinterpret_cast<const float4*>(w + (int64_t)(e0 + r) * H + c);
+    *reinterpret_cast<float4*>(ws + i) = v;
   }
   __syncthreads();
-  const int el = tid >> 3, tp = (tid & 7) * 2;
-  float a0 = 0.f, a1 = 0.f;
-#pragma unroll 8
-  for (int h = 0; h < RT_H; ++h) {
-    const float wv = ws[el][h];
-    a0 = fmaf(xs[tp][h], wv, a0);
-    a1 = fmaf(xs[tp + 1][h], wv, a1);
-  }
-  const int e = e0 + el;
-  if (e < E) {
-    float* dst = part + ((int64_t)blockIdx.z * T) * E;
-    if (t0 + tp < T) dst[(t0 + tp) * E + e] = a0;
-    if (t0 + tp + 1 < T) dst[(t0 + tp + 1) * E + e] = a1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t_end = min(T, (int64_t)(blockIdx.y + 1) * RT_TOK);
+  for (int64_t t = (int64_t)blockIdx.y * RT_TOK + warp; t < t_end; t += blockDim.x >> 5) {
+    float acc[EPB];
+#pragma unroll
+    for (int j = 0; j < EPB; ++j) acc[j] = 0.f;
+    const uint16_t* xr = x + t * H;
+    for (int h = lane * 4; h < H; h += 128) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(xr + h);
+      const float a0 = bf16_from_bits(raw.x & 0xffffu), a1 = bf16_from_bits(raw.x >> 16);
+      const float a2 = bf16_from_bits(raw.y & 0xffffu), a3 = bf16_from_bits(raw.y >> 16);
+#pragma unroll
+      for (int j = 0; j < EPB; ++j) {
+        const float4 g = *reinterpret_cast<const float4*>(ws + j * H + h);
+        acc[j] = fmaf(a0, g.x, acc[j]);
+        acc[j] = fmaf(a1, g.y, acc[j]);
+        acc[j] = fmaf(a2, g.z, acc[j]);
+        acc[j] = fmaf(a3, g.w, acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < EPB; ++j) {
+      float v = acc[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && e0 + j < E) logits[t * E + e0 + j] = v;
+    }
   }
 }
 
 __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log1pf(expf(v)); }
 
-__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ part, int nchunks, int64_t T,
+__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int64_t T,
                                                          int E, int K, int score_func, int renorm, float scale,
                                                          const float* __restrict__ bias,
                                                          const int32_t* __restrict__ tid2eid,
@@ -79,10 +75,7 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    float l = 0.f;
-    if (e < E)
-      for (int c = 0; c < nchunks; ++c) l += part[((int64_t)c * T + t) * E + e];
-    sc[j] = (e < E) ? l : -INFINITY;
+    sc[j] = (e < E) ? logits[t * E + e] : -INFINITY;
   }
   if (score_func == DSV4_SCORE_SOFTMAX) {
     float m = -INFINITY;
@@ -171,7 +164,7 @@ using namespace dsv4;
 
 extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts) {
   if (n_tokens < 0 || hidden <= 0 || n_experts <= 0) return DSV4_EINVAL;
-  return (int64_t)(hidden / RT_H) * n_tokens * n_experts * (int64_t)sizeof(float);
+  return n_tokens * n_experts * (int64_t)sizeof(float);
 }
 
 extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
@@ -181,7 +174,7 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
                                void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out && workspace, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && hidden % RT_H == 0, "hidden must be a positive multiple of 128");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % 128 == 0 && hidden <= 6144, "hidden must be a multiple of 128, <= 6144");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
@@ -191,14 +184,22 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   if (n_tokens == 0) return DSV4_OK;
   if (int rc = bind_device_of(x_bf16, nullptr)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const int nchunks = hidden / RT_H;
-  dim3 g1((n_experts + RT_E - 1) / RT_E, (unsigned)((n_tokens + RT_T - 1) / RT_T), nchunks);
-  route_logits_kernel<<<g1, 256, 0, st>>>((const uint16_t*)x_bf16, gate_w, (float*)workspace, n_tokens, hidden,
-                                          n_experts);
+  const unsigned gy = (unsigned)((n_tokens + RT_TOK - 1) / RT_TOK);
+  if (n_tokens <= 512) {  // decode: 2 gate rows per CTA, E/2 CTAs
+    const size_t smem = (size_t)2 * hidden * sizeof(float);
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    route_logits_kernel<2><<<dim3((n_experts + 1) / 2, gy), 256, smem, st>>>(
+        (const uint16_t*)x_bf16, gate_w, (float*)workspace, n_tokens, hidden, n_experts);
+  } else {  // prefill: 8 gate rows per CTA so x is re-read E/8 times
+    const size_t smem = (size_t)8 * hidden * sizeof(float);
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    route_logits_kernel<8><<<dim3((n_experts + 7) / 8, gy), 256, smem, st>>>(
+        (const uint16_t*)x_bf16, gate_w, (float*)workspace, n_tokens, hidden, n_experts);
+  }
   const int64_t threads = n_tokens * 32;
   route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      (const float*)workspace, nchunks, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias,
-      tid2eid, input_ids, weights_out, indices_out);
+      (const float*)workspace, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid,
+      input_ids, weights_out, indices_out);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

@@ -115,6 +115,7 @@ class ExpertBank:
         self.h2d_copies = 0
         self._tables = {}               # layer -> (epoch, device slot table)
         self._epoch = 0
+        self._all_event = None
 
     # -- host pool ----------------------------------------------------------
     @property
@@ -198,6 +199,8 @@ class ExpertBank:
         slots, misses = self._lru.lookup(keys)
         if misses:
             cs = self._stream()
+            if self._all_event is not None:
+                cs.wait_event(self._all_event)   # kernels that read every slot
             for k, s in misses:
                 ev = self._slot_events.get(s)
                 if ev is not None:
@@ -228,9 +231,13 @@ class ExpertBank:
         return t
 
     def mark_used(self, slots, stream=None):
-        """Record that kernels enqueued so far on ``stream`` read ``slots``."""
+        """Record that kernels enqueued so far on ``stream`` read ``slots``
+        (``None``: possibly any slot)."""
         ev = torch.cuda.Event()
         ev.record(stream or torch.cuda.current_stream(self.device))
+        if slots is None:
+            self._all_event = ev
+            return
         for s in slots:
             self._slot_events[int(s)] = ev
 
@@ -269,24 +276,23 @@ class ExpertBank:
 
     def get_packed(self, layer, eid):
         """Packed expert on the device (offload.py:103-129 semantics):
-        ``w{1,2,3}p`` views of the resident slot ([N, K//2] uint8) and
-        ``w{1,2,3}s`` E8M0 scales [N, K//32] in checkpoint order, plus
-        ``slot`` (the whole slot) and ``slot_index``."""
+        ``w{1,2,3}p`` ([N, K//2] uint8) and ``w{1,2,3}s`` ([N, K//32] E8M0)
+        in checkpoint order, plus ``slot`` (the resident slot, kernel layout)
+        and ``slot_index``.  The checkpoint-order tensors are copies made
+        from the host pool; the kernels read the slot."""
         from dsv4_plugin import ops
         s = self.ensure_resident(layer, [eid])[0]
-        h, i = self.hidden, self.inter
-        row = self.arena[s]
-        w13 = row[: 2 * i * (h // 2)].view(2 * i, h // 2)
-        w2 = row[2 * i * (h // 2): 2 * i * (h // 2) + h * (i // 2)].view(h, i // 2)
-        sc = ops.unpack_expert(self._host[(int(layer), int(eid))], h, i)
-        return {"w1p": w13[:i], "w3p": w13[i:], "w2p": w2,
-                "w1s": sc["w1s"].to(self.device), "w2s": sc["w2s"].to(self.device),
-                "w3s": sc["w3s"].to(self.device), "slot": row, "slot_index": s}
+        parts = ops.unpack_expert(self._host[(int(layer), int(eid))], self.hidden, self.inter)
+        out = {k: v.to(self.device) for k, v in parts.items()}
+        out["slot"] = self.arena[s]
+        out["slot_index"] = s
+        return out
 
     def invalidate(self):
         self._cache.clear()
         self._lru.clear()
         self._slot_events.clear()
+        self._all_event = None
         self._tables.clear()
         self._epoch += 1
 

@@ -139,6 +139,18 @@ def moe_align(indices: torch.Tensor, n_experts: int) -> dict:
     return out
 
 
+def combine_ordered(rows: torch.Tensor, order: torch.Tensor) -> torch.Tensor:
+    """y[t] = bf16(sum_j rows[order[t, j]]) in float32, j ascending; -1 skips."""
+    _need_cuda(rows, order)
+    rows = rows.contiguous()
+    o = order.to(torch.int32).contiguous()
+    t, k = o.shape
+    y = torch.empty((t, rows.shape[1]), dtype=torch.bfloat16, device=rows.device)
+    check(lib().dsv4_moe_combine_ordered(rows.data_ptr(), o.data_ptr(), t, k, rows.shape[1], y.data_ptr(),
+                                         _stream(rows.device)))
+    return y
+
+
 def expert_slot_bytes(hidden: int, inter: int) -> int:
     n = lib().dsv4_expert_slot_bytes(hidden, inter)
     if n < 0:
@@ -233,6 +245,26 @@ class MoEPlan:
                                      so.data_ptr(), out.data_ptr(), _stream(x.device)))
         return out
 
+    STAGES = ("align", "quant_gather", "gate_up_gemm", "down_gemm", "combine")
+
+    def enable_timing(self, enable: bool = True) -> None:
+        check(lib().dsv4_moe_enable_timing(self._h, int(bool(enable))))
+
+    def stage_times(self) -> dict:
+        """ms per stage of the last forward (waits for it)."""
+        buf = (C.c_float * 5)()
+        check(lib().dsv4_moe_stage_times(self._h, buf, 5))
+        return dict(zip(self.STAGES, [float(v) for v in buf]))
+
+    def n_active(self) -> int:
+        """Active experts of the last forward (synchronises)."""
+        ptrs = [C.c_void_p() for _ in range(6)]
+        check(lib().dsv4_moe_debug_align(self._h, *[C.byref(p) for p in ptrs]))
+        buf = (C.c_int32 * 1)()
+        torch.cuda.synchronize(self.device)
+        _memcpy_d2h(buf, ptrs[5].value, 4)
+        return int(buf[0])
+
     def status(self) -> None:
         """Synchronise and raise if a kernel recorded an error."""
         check(lib().dsv4_moe_status(self._h, _stream(self.device)))
@@ -246,6 +278,9 @@ class MoEPlan:
         sizes = (e, e + 1, p, p, e, 1)
         out = {}
         for name, ptr, n in zip(names, ptrs, sizes):
+            if n == 0:
+                out[name] = torch.zeros(0, dtype=torch.int32)
+                continue
             buf = (C.c_int32 * n)()
             torch.cuda.synchronize(self.device)
             _memcpy_d2h(buf, ptr.value, 4 * n)

@@ -50,8 +50,10 @@ int dsv4_abi_version(void);
  * One expert = w1/w3 [I, H/2] + w2 [H, I/2] packed E2M1 (low nibble = even k)
  * and E8M0 per-32 scales, stored as ONE contiguous slot:
  *   [w13 packed (w1 rows then w3 rows) | w2 packed | w13 scales | w2 scales]
- * with the scales re-tiled into 512-byte atoms (128 rows x 4 scale bytes,
- * row r at (r%32)*16 + (r/32)*4) that the tensor cores read directly.
+ * The packed weights are tiled into contiguous 8 KiB blocks of 128 rows x
+ * 128 elements (one TMA box each); the scales are re-tiled into 512-byte
+ * atoms (128 rows x 4 scale bytes, row r at (r%32)*16 + (r/32)*4) that the
+ * tensor cores read directly.
  * Replaces the six per-expert host tensors of ExpertBank.register
  * (offload.py:59-68) and their per-call stacking (deepseek_v4.py:218-223).
  * ------------------------------------------------------------------------ */
@@ -132,6 +134,21 @@ int dsv4_moe_forward(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, i
 /* Synchronises `stream`, returns the plan's device status word (0 or a
  * DSV4_E* code recorded by a kernel) and clears it. */
 int dsv4_moe_status(dsv4_moe_plan* plan, void* stream);
+/* Combine in a given order (deepseek_v4.py:195-197 index_add_, ascending
+ * expert id per token): y[t] = bf16(sum_j rows[order[t*k + j]]) summed in
+ * float32 from zero in j order; order < 0 skips.  Used by the expert-
+ * parallel path, whose received rows are not grouped by expert. */
+int dsv4_moe_combine_ordered(const void* rows_bf16, const int32_t* order, int64_t n_tokens, int32_t topk,
+                             int32_t hidden, void* y_bf16, void* stream);
+
+/* Per-stage device timing (no counterpart in the reference, which has no
+ * timing hooks).  When enabled, dsv4_moe_forward records CUDA events on its
+ * stream between its stages; dsv4_moe_stage_times waits for the last
+ * forward's events and writes up to n elapsed times in ms: [0] align,
+ * [1] activation quant + gather, [2] gate/up GEMM, [3] down GEMM,
+ * [4] combine. */
+int dsv4_moe_enable_timing(dsv4_moe_plan* plan, int32_t enable);
+int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
 /* Device pointers of the plan's align outputs (valid after a forward):
  * counts[E], offsets[E+1], sorted_flat[P], inv[P], active[E], n_active[1]. */
 int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,

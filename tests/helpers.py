@@ -47,3 +47,35 @@ class SyntheticLayer:
     def oracle(self, x: np.ndarray, weights: np.ndarray, idx: np.ndarray, profile="bf16") -> np.ndarray:
         return O.moe_routed(x, weights, idx, self.experts, self.n, self.cfg.swiglu_limit, profile,
                             deq_cache=self.deq_cache)
+
+
+def make_plugin_layer(cfg: S.MoEConfig, experts: dict, device, layer_idx: int = 3, seed: int = 0,
+                      slots: int | None = None):
+    """OffloadDeepseekV4MoE for a synthetic layer built through the plugin's
+    public API, with ``experts`` {eid: six tensors} registered in a fresh
+    engine (which becomes the process-wide one)."""
+    import types
+
+    from dsv4_plugin.core import engine as ENG
+    from dsv4_plugin.models import deepseek_v4 as DV4
+
+    n = slots or len(experts)
+    eng = ENG.ExpertOffloadEngine(slot_capacity=n, device=device, packed_capacity=n)
+    for e, ex in experts.items():
+        eng.bank.register(layer_idx, e, *[torch.from_numpy(ex[k]) for k in
+                                          ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
+    ENG.reset_engine(eng)
+    hf = types.SimpleNamespace(
+        n_routed_experts=cfg.n_experts, n_shared_experts=None, num_experts_per_tok=cfg.topk,
+        norm_topk_prob=cfg.renormalize, scoring_func=cfg.score_func, routed_scaling_factor=cfg.route_scale,
+        swiglu_limit=cfg.swiglu_limit, num_hash_layers=0, vocab_size=1000, hidden_size=cfg.hidden,
+        moe_intermediate_size=cfg.inter, hidden_act="silu")
+    pc = types.SimpleNamespace(use_sequence_parallel_moe=False, eplb_config=None, enable_eplb=False)
+    moe = DV4.OffloadDeepseekV4MoE(hf, pc, prefix=f"model.layers.{layer_idx}.mlp").to(device)
+    gw, bias = S.make_gate(cfg, seed, layer_idx)
+    moe.gate.weight.data.copy_(torch.from_numpy(gw))
+    if bias is not None:
+        moe.gate.e_score_correction_bias.data.copy_(torch.from_numpy(bias))
+    else:
+        moe.gate.e_score_correction_bias.data.zero_()
+    return moe, eng

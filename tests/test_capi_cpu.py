@@ -1,0 +1,109 @@
+"""C-ABI library checks that need no GPU: it builds, loads, exports every
+entry point of include/dsv4moe.h, and its host-only functions (slot packing)
+match a Python restatement of the slot layout."""
+
+import ctypes as C
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "deepseek-v4-flash-offload_b200")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    spec = importlib.util.spec_from_file_location("dsv4_build_ext", os.path.join(PKG, "build_ext.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
+    from dsv4_plugin import _lib
+    return _lib
+
+
+def test_exports_every_header_symbol(lib):
+    names = lib.header_symbols(os.path.join(ROOT, "include", "dsv4moe.h"))
+    assert len(names) >= 20
+    raw = C.CDLL(lib.LIB_PATH)
+    missing = [n for n in names if not hasattr(raw, n)]
+    assert not missing, missing
+    # the ctypes table covers the header exactly
+    assert sorted(lib.SIGNATURES) == names
+    assert lib.lib().dsv4_abi_version() == 1
+
+
+def test_slot_bytes(lib):
+    L = lib.lib()
+    assert L.dsv4_expert_slot_bytes(4096, 2048) == 13369344
+    assert L.dsv4_expert_slot_bytes(1024, 512) == 835584
+    assert L.dsv4_expert_slot_bytes(1000, 512) == lib.DSV4_EINVAL
+
+
+def _tile_py(s, row_base, k, atoms):
+    """Python restatement of the scale-atom layout."""
+    rows, kb_n = s.shape
+    for r in range(rows):
+        R = row_base + r
+        for kb in range(kb_n):
+            off = ((R // 128) * (k // 128) + kb // 4) * 512 + (R % 32) * 16 + ((R % 128) // 32) * 4 + kb % 4
+            atoms[off] = s[r, kb]
+
+
+def _tile_w_py(w, row_base, k, out):
+    """Python restatement of the 8 KiB weight blocks (128 rows x 128 elements)."""
+    rows = w.shape[0]
+    for r in range(rows):
+        R = row_base + r
+        for kt in range(k // 128):
+            off = ((R // 128) * (k // 128) + kt) * 8192 + (R % 128) * 64
+            out[off: off + 64] = w[r, kt * 64: kt * 64 + 64]
+
+
+def test_pack_unpack_round_trip(lib):
+    from dsv4_plugin import ops
+    from dsv4_plugin import synthetic as S
+    cfg = S.CFG0
+    ex = S.make_expert(cfg, 11, 3)
+    t = {k: torch.from_numpy(v) for k, v in ex.items()}
+    slot = ops.pack_expert(t["w1p"], t["w1s"], t["w2p"], t["w2s"], t["w3p"], t["w3s"], cfg.hidden, cfg.inter)
+    h, i = cfg.hidden, cfg.inter
+    sb = slot.numpy()
+    assert sb.size == 835584
+    w13 = np.zeros(i * h, np.uint8)
+    _tile_w_py(ex["w1p"], 0, h, w13)
+    _tile_w_py(ex["w3p"], i, h, w13)
+    assert np.array_equal(sb[: i * h], w13)
+    w2 = np.zeros(h * i // 2, np.uint8)
+    _tile_w_py(ex["w2p"], 0, i, w2)
+    assert np.array_equal(sb[i * h: i * h + h * i // 2], w2)
+    sf13 = np.zeros(2 * i * h // 32, np.uint8)
+    _tile_py(ex["w1s"], 0, h, sf13)
+    _tile_py(ex["w3s"], i, h, sf13)
+    o = i * h + h * i // 2
+    assert np.array_equal(sb[o: o + sf13.size], sf13)
+    sf2 = np.zeros(h * i // 32, np.uint8)
+    _tile_py(ex["w2s"], 0, i, sf2)
+    assert np.array_equal(sb[o + sf13.size:], sf2)
+    back = ops.unpack_expert(slot, h, i)
+    for k in ex:
+        assert np.array_equal(back[k].numpy(), ex[k]), k
+
+
+def test_errors_are_codes_not_crashes(lib):
+    L = lib.lib()
+    rc = L.dsv4_pack_expert_host(None, None, None, None, None, None, 1024, 512, None)
+    assert rc == lib.DSV4_EINVAL
+    assert b"null pointer" in L.dsv4_last_error_string()
+    with pytest.raises(lib.Dsv4Error):
+        lib.check(rc)
+
+
+def test_ops_refuse_cpu_tensors(lib):
+    from dsv4_plugin import ops
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.dequant_fp4_weight(torch.zeros(4, 16, dtype=torch.uint8), torch.zeros(4, 1, dtype=torch.uint8))
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.route_topk(torch.zeros(2, 256, dtype=torch.bfloat16), torch.zeros(16, 256), None, 4)

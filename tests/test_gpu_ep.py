@@ -1,0 +1,87 @@
+"""Expert-parallel layer on the GPU (NCCL).  The EP forward must equal the
+single-GPU layer bit for bit.  World 1 runs in every GPU session; world 2
+needs two GPUs and is skipped otherwise."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dsv4_plugin import synthetic as S
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(rank, world, port, tokens, out):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, root, os.path.join(root, "deepseek-v4-flash-offload_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from datetime import timedelta
+
+    from helpers import make_plugin_layer
+
+    from dsv4_plugin.parallel_ep import ExpertParallelMoE
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+    try:
+        cfg = S.CFG0
+        allx = {e: S.make_expert(cfg, 0, e, 3) for e in range(cfg.n_experts)}
+        full, _ = make_plugin_layer(cfg, allx, dev)
+        x = S.make_tokens(cfg, 50 + rank, tokens)
+        xt = torch.from_numpy(S.to_bf16_bits(x).astype(np.int16)).view(torch.bfloat16).to(dev)
+        full.engine.bank.preload_all(3)
+        ref = full.forward(xt).clone()
+        e_loc = cfg.n_experts // world
+        mine = {e: allx[e] for e in range(rank * e_loc, (rank + 1) * e_loc)}
+        part, _ = make_plugin_layer(cfg, mine, dev)
+        epm = ExpertParallelMoE(part, rank, world)
+        for profile in ("bf16", "a4w4"):
+            from dsv4_plugin.models import deepseek_v4 as DV4
+            DV4._MXFP4_GMM = profile == "a4w4"
+            try:
+                ref = full.forward(xt).clone()
+                got = epm.forward(xt, profile)
+            finally:
+                DV4._MXFP4_GMM = False
+            torch.cuda.synchronize(dev)
+            epm.plan.status()
+            out[(rank, profile)] = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        del epm
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tokens", [1, 24])
+def test_ep_world1_equals_single_gpu(tokens):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_run, args=(1, _port(), tokens, out), nprocs=1, join=True)
+    assert dict(out) == {(0, "bf16"): True, (0, "a4w4"): True}
+
+
+def test_ep_world2_equals_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_run, args=(2, _port(), 33, out), nprocs=2, join=True)
+    assert all(out.values()) and len(out) == 4

@@ -66,8 +66,14 @@ def test_cfg0_alignment_outputs(ops, layer0):
     plan.status()
     d = plan.debug_align(40)
     ref = O.moe_align(idx, L.n)
-    assert np.array_equal(d["sorted_flat"].numpy(), ref["order"])
+    # rows sit in per-expert groups padded to 64; the stable order is unchanged
+    assert np.array_equal(np.argsort(d["inv"].numpy(), kind="stable"), ref["order"])
     assert np.array_equal(d["counts"].numpy(), ref["counts"])
+    starts = d["offsets"].numpy()[:-1]
+    assert np.all(starts % 64 == 0)
+    inv = d["inv"].numpy()
+    e_of = idx.reshape(-1)
+    assert np.all(inv - starts[e_of] >= 0) and np.all(inv - starts[e_of] < ref["counts"][e_of])
 
 
 @pytest.mark.parametrize("T", [1, 7, 64, 513])
