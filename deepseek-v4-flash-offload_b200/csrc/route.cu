@@ -4,6 +4,9 @@
 //   phase 2: one warp per token: score function,
 //            biased top-k (or hash table), unbiased weights, renormalise,
 //            scale.
+#include <mutex>
+#include <string>
+
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -200,6 +203,86 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
       (const float*)workspace, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid,
       input_ids, weights_out, indices_out);
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+// ---------------------------------------------------------------------------
+// Router variant that allocates nothing.
+//
+// Some callers cannot allocate device memory when they route a batch: a
+// serving engine that has handed nearly all free HBM to its pre-sized cache
+// pool has no room left for a new cudaMalloc in the middle of a step, and a
+// plain C caller bound through an FFI may have no device allocator at all.
+// For them the logits scratch of the router lives in this fixed file-scope
+// device array instead of a caller workspace.  Limits and rules:
+//   * at most DSV4_ROUTE_NOALLOC_MAX_LOGITS (n_tokens * n_experts) logits,
+//     256 KiB of device memory that every GPU loading the library keeps
+//     until the process exits; larger calls are rejected with DSV4_EINVAL;
+//   * the first call on a device looks up the array's device address on
+//     that device (cudaGetSymbolAddress); make that first call before any
+//     stream capture;
+//   * all calls share the one array and it keeps the last call's logits;
+//     the logits kernel writes every element the top-k kernel then reads, so
+//     nothing needs clearing, but calls that overlap on the GPU (on different
+//     streams, or from several threads) race on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_route_noalloc_scratch[DSV4_ROUTE_NOALLOC_MAX_LOGITS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float* bias,
+                                       const int32_t* tid2eid, const int64_t* input_ids, int64_t n_tokens,
+                                       int32_t hidden, int32_t n_experts, int32_t topk, int32_t score_func,
+                                       int32_t renormalize, float route_scale, float* weights_out,
+                                       int32_t* indices_out, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out, "null pointer");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % 128 == 0 && hidden <= 6144, "hidden must be a multiple of 128, <= 6144");
+  DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
+  DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
+  DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
+  DSV4_CHECK_ARG(!tid2eid || input_ids, "hash routing needs input_ids");
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * (int64_t)n_experts <= DSV4_ROUTE_NOALLOC_MAX_LOGITS,
+                 "n_tokens * n_experts exceeds the fixed scratch of " +
+                     std::to_string(DSV4_ROUTE_NOALLOC_MAX_LOGITS) +
+                     " logits; use dsv4_route_topk with a caller workspace");
+  if (n_tokens == 0) return DSV4_OK;
+  int dev = 0;
+  if (int rc = bind_device_of(x_bf16, &dev)) return rc;
+  DSV4_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "device ordinal out of range");
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      // set-up, once per device, with that device current (bind_device_of)
+      void* p = nullptr;
+      DSV4_CUDA_CHECK(cudaGetSymbolAddress(&p, g_route_noalloc_scratch));
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned gy = (unsigned)((n_tokens + RT_TOK - 1) / RT_TOK);
+  if (n_tokens <= 512) {
+    const size_t smem = (size_t)2 * hidden * sizeof(float);
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    route_logits_kernel<2><<<dim3((n_experts + 1) / 2, gy), 256, smem, st>>>(
+        (const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts);
+  } else {
+    const size_t smem = (size_t)8 * hidden * sizeof(float);
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    route_logits_kernel<8><<<dim3((n_experts + 7) / 8, gy), 256, smem, st>>>(
+        (const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts);
+  }
+  const int64_t threads = n_tokens * 32;
+  route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      scratch, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
+      weights_out, indices_out);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

@@ -99,6 +99,22 @@ int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, 
                     int32_t score_func, int32_t renormalize, float route_scale, float* weights_out,
                     int32_t* indices_out, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Router that allocates nothing; it has no counterpart in the reference.
+ * For callers that cannot allocate device memory at routing time (a serving
+ * engine whose cache pool already holds nearly all free HBM, or a C caller
+ * without a device allocator).  Same arguments and results as
+ * dsv4_route_topk minus the workspace: the logits scratch is a fixed
+ * 256 KiB device array inside the library, so n_tokens * n_experts must not
+ * exceed DSV4_ROUTE_NOALLOC_MAX_LOGITS (larger calls return DSV4_EINVAL).
+ * The first call on a device resolves the array's address on that device;
+ * make it before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU race on it. */
+#define DSV4_ROUTE_NOALLOC_MAX_LOGITS 65536
+int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
+                            const int64_t* input_ids, int64_t n_tokens, int32_t hidden, int32_t n_experts,
+                            int32_t topk, int32_t score_func, int32_t renormalize, float route_scale,
+                            float* weights_out, int32_t* indices_out, void* stream);
+
 /* ------------------------------------------------------------------------ *
  * moe_align (deepseek_v4.py:154-164): stable counting sort of the T*k
  * (token, slot) assignments by expert id.  sorted_flat[pos] = t*k + j,
