@@ -14,7 +14,10 @@ HBM slot arena, synthetic seeded inputs.  A step is one layer forward.
   roofline : the gate/up GEMM kernel (the dominant launch), algorithmic
           bytes / its event-timed duration against the measured HBM copy peak.
 L2 is flushed (256 MiB write) before every timed step; steps rotate over
-several token batches so routing changes.  With N>1 (torchrun) every rank
+several token batches so routing changes.  The layer is captured once as a
+CUDA graph and replayed per step (the way vLLM runs decode); the per-kernel
+times behind the roofline come from an eager pass of the same steps with
+CUDA events between the stages.  With N>1 (torchrun) every rank
 runs the layer expert-parallel: E/N experts per rank, T=64 tokens per rank,
 all-to-all dispatch and combine (weak scaling).
 ``--impl reference`` times the CPU restatement of the reference's
@@ -224,7 +227,6 @@ def run_ours(a):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     y_host = torch.empty((T, _cfg().hidden), dtype=torch.bfloat16).pin_memory()
     plan = eng.plan_for(_cfg().n_experts, _cfg().topk, T, _cfg().swiglu_limit)
-    plan.enable_timing(True)
     stream = torch.cuda.current_stream(device)
 
     def device_steps(n, tokens_dev, record=True):
@@ -243,16 +245,57 @@ def run_ours(a):
                 ds.append(plan.n_active())
         return tot, stages, ds
 
-    # warm-up, then the timed device-resident region
-    device_steps(a.warmup, dev, record=False)
+    # the layer as a CUDA graph (how a serving engine replays decode steps):
+    # the step's token batch is copied into the graph's input buffer, then the
+    # whole layer (router, align, quant, two GEMMs, combine) replays.
+    def capture(tokens_dev, profile_a4w4=False):
+        DV4._MXFP4_GMM = profile_a4w4
+        try:
+            xs = torch.empty_like(tokens_dev[0])
+            xs.copy_(tokens_dev[0])
+            for _ in range(2):
+                moe.forward(xs)
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                ys = moe.forward(xs)
+            torch.cuda.synchronize(device)
+        finally:
+            DV4._MXFP4_GMM = False
+        return g, xs, ys
+
+    def graph_steps(g, xs, tokens_dev, n, record=True):
+        tot = 0.0
+        for s in range(n):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            xs.copy_(tokens_dev[s % len(tokens_dev)])
+            g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            if record:
+                tot += e0.elapsed_time(e1)
+        return tot
+
+    plan.enable_timing(False)
+    g, xs, ys = capture(dev)
+    graph_steps(g, xs, dev, a.warmup, record=False)
     clk = Clocks(local)
     torch.cuda.synchronize(device)
     clk.start()
-    tot_ms, stages, ds = device_steps(a.steps, dev)
+    tot_ms = graph_steps(g, xs, dev, a.steps)
     torch.cuda.synchronize(device)
     clocks = clk.stop()
     ms_step = tot_ms / a.steps
     value = T * a.steps / (tot_ms / 1e3)
+
+    # per-kernel device times of the same steps, run eagerly with CUDA events
+    # between the stages (on the launching stream)
+    plan.enable_timing(True)
+    device_steps(2, dev, record=False)
+    eager_ms, stages, ds = device_steps(a.steps, dev)
+    plan.enable_timing(False)
 
     # roofline of the gate/up GEMM and of the whole layer
     hbm, peak_kind = _peaks()
@@ -272,22 +315,22 @@ def run_ours(a):
                 "algorithmic_bytes_per_launch": round(g1_bytes / len(ds)),
                 "launch_ms": round(g1_ms / len(ds), 5)}
     detail = {"active_experts_mean": round(statistics.mean(ds), 2),
+              "eager_ms_per_step": round(eager_ms / a.steps, 5),
               "stage_ms_mean": {k: round(statistics.mean(s[k] for s in stages), 5) for k in stages[0]},
               "down_gemm_roofline": {"achieved": round(ach2, 1), "frac": round(ach2 / hbm, 4)},
               "layer_roofline": {"achieved": round(lay, 1), "frac": round(lay / hbm, 4),
                                  "bytes": "D*13369344 + gate fp32 + x/y"}}
 
-    # e2e through the public forward with host buffers
+    # e2e through the public forward (graph-replayed) with host buffers
     def e2e_steps(n, record=True):
         tot = 0.0
-        xd = torch.empty_like(dev[0])
         for s in range(n):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            xd.copy_(host[s % R], non_blocking=True)
-            y = moe.forward(xd)
-            y_host.copy_(y, non_blocking=True)
+            xs.copy_(host[s % R], non_blocking=True)
+            g.replay()
+            y_host.copy_(ys, non_blocking=True)
             e1.record(stream)
             e1.synchronize()
             if record:
@@ -298,29 +341,32 @@ def run_ours(a):
     e2e_ms = e2e_steps(a.steps)
     e2e = {"value": round(T * a.steps / (e2e_ms / 1e3), 1), "unit": UNIT,
            "h2d_bytes_per_step": T * _cfg().hidden * 2, "d2h_bytes_per_step": T * _cfg().hidden * 2,
-           "ms_per_step": round(e2e_ms / a.steps, 5), "api": "OffloadDeepseekV4MoE.forward"}
+           "ms_per_step": round(e2e_ms / a.steps, 5),
+           "api": "OffloadDeepseekV4MoE.forward replayed as a CUDA graph"}
 
     if not a.no_detail:
         # a4w4 profile on the same workload, and the other decode batch sizes
-        DV4._MXFP4_GMM = True
-        try:
-            device_steps(2, dev, record=False)
-            t4, _, _ = device_steps(a.steps, dev)
-        finally:
-            DV4._MXFP4_GMM = False
+        g4, xs4, _ = capture(dev, profile_a4w4=True)
+        graph_steps(g4, xs4, dev, 2, record=False)
+        t4 = graph_steps(g4, xs4, dev, a.steps)
         detail["a4w4_value"] = round(T * a.steps / (t4 / 1e3), 1)
+        del g4
         per_t = {}
         for t in (1, 8, 32):
             _, dv = _token_batches(4, t, device, 0)
-            device_steps(2, dv, record=False)
-            tt, st, dd = device_steps(max(4, a.steps // 2), dv)
+            gt, xst, _ = capture(dv)
             n = max(4, a.steps // 2)
+            graph_steps(gt, xst, dv, 2, record=False)
+            tt = graph_steps(gt, xst, dv, n)
+            plan.enable_timing(True)
+            _, st, dd = device_steps(n, dv)
+            plan.enable_timing(False)
             per_t[str(t)] = {"tok_s": round(t * n / (tt / 1e3), 1), "ms": round(tt / n, 5),
                              "active_experts": round(statistics.mean(dd), 1),
                              "gate_up_frac": round(sum(_gemm_bytes(d, t * 8, "gate_up") for d in dd) /
                                                    (sum(x["gate_up_gemm"] for x in st) / 1e3) / 1e9 / hbm, 4)}
+            del gt
         detail["decode_T"] = per_t
-    moe.engine.bank  # keep alive
     plan.status()
 
     cpu = None if a.no_cpu_baseline else cpu_baseline(T, budget_s=12.0)
@@ -333,7 +379,8 @@ def run_ours(a):
                        "parallelism": "single GPU",
                        "l2": "256 MiB flush before every timed step; 8 rotating token batches"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": 7 * a.steps, "detail": detail}
+            "gpu_launches": 7 * a.steps, "launch_mode": "CUDA graph replay per step (7 kernels)",
+            "detail": detail}
     print(json.dumps(line), flush=True)
 
 

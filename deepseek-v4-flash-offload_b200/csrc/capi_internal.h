@@ -19,6 +19,28 @@ int fail(int code, const std::string& msg);
 // cudaSetDevice).  Optionally returns the device ordinal.
 int bind_device_of(const void* ptr, int* device);
 
+// Launch with programmatic stream serialization (PDL) when `pdl`: the kernel
+// may start while its stream predecessor finishes; it must call
+// griddep_wait() before reading that predecessor's outputs.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Whether kernels are launched with PDL (env DSV4_PDL, default on).
+bool pdl_enabled();
+
 // Byte layout of one packed expert slot (see include/dsv4moe.h).
 struct SlotLayout {
   int64_t w13p;   // [2I, H/2] packed, w1 rows then w3 rows

@@ -60,8 +60,9 @@ struct GemmParams {
   int64_t slot_bytes;
   int64_t sfa_off;           // byte offset of the A scale atoms inside a slot
   int k_tiles;               // K / 128
-  int a_row_tiles;           // tiles of 128 rows per A matrix (= tiles per chunk)
-  int a1_row_offset;         // row offset of the second A matrix (w3) in the map
+  int a_row_tiles;           // tiles per chunk = 256-row weight pairs of the matrix
+  int out_tile_cols;         // output columns per tile (128: gate/up pair, 256: down pair)
+  int pf_dist;               // L2 prefetch distance in k-tiles (0: off)
   const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, 64-row block)
   int64_t rb_cap;            // 64-row blocks per k-tile in b_sf / out_sf
   const int4* chunks;        // {expert, row0, nrows, 0}
@@ -114,10 +115,16 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
   return ti;
 }
 
+// Activation rows loaded per tile: the chunk's valid rows rounded up to 16,
+// 32 or 64 (decode chunks are mostly short); also the MMA N.
+__device__ __forceinline__ int b_rows_for(int nrows) { return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : 64); }
+
 template <int NUM_A, bool B_FP4, int EPI>
 __global__ void __launch_bounds__(G_THREADS, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB16,
+                    const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
                     const GemmParams p) {
+  static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
   using C = GemmCfg<NUM_A>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -148,7 +155,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tmA);
-    prefetch_tensormap(&tmB);
+    prefetch_tensormap(&tmB16);
+    prefetch_tensormap(&tmB32);
+    prefetch_tensormap(&tmB64);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, G_TMEM_COLS);
@@ -159,9 +168,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
+  // The align outputs (chunks, counts) are two kernels back and complete;
+  // the activations come from the immediate predecessor: wait for it, then
+  // let the next kernel start its prologue.
   const int n_tiles = (*p.n_chunks) * p.a_row_tiles;
   const int k_tiles = p.k_tiles;
   const int step = gridDim.x;
+  griddep_wait();
+  griddep_launch();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -182,29 +196,39 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         const uint8_t* sf_base = p.arena + (int64_t)cur.slot * p.slot_bytes + p.sfa_off;
         const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / G_BN) * C::SF_BYTES;
-        const int rt1 = p.a1_row_offset / G_BM + cur.mt;
+        const int nb = b_rows_for(cur.nrows);
+        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : &tmB64);
+        if (p.pf_dist > 0 && nxt.slot >= 0)  // the next tile's weight scales
+          bulk_prefetch_l2(p.arena + (int64_t)nxt.slot * p.slot_bytes + p.sfa_off +
+                               (int64_t)nxt.mt * k_tiles * 2 * C::SF_BYTES, k_tiles * 2 * C::SF_BYTES);
+        if (p.pf_dist > 0 && t == (int)blockIdx.x) {  // first tile of this CTA
+          bulk_prefetch_l2(sf_base + (int64_t)cur.mt * k_tiles * 2 * C::SF_BYTES, k_tiles * 2 * C::SF_BYTES);
+          for (int j = 0; j < p.pf_dist && j < k_tiles; ++j) tma_prefetch_5d(&tmA, 0, 0, j, cur.mt, cur.slot);
+        }
         for (int kt = 0; kt < k_tiles; ++kt) {
+          if (p.pf_dist > 0) {  // keep pf_dist k-tiles of weights on their way into L2
+            const int kp = kt + p.pf_dist;
+            if (kp < k_tiles)
+              tma_prefetch_5d(&tmA, 0, 0, kp, cur.mt, cur.slot);
+            else if (nxt.slot >= 0 && kp - k_tiles < k_tiles)
+              tma_prefetch_5d(&tmA, 0, 0, kp - k_tiles, nxt.mt, nxt.slot);
+          }
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + stage * C::STAGE_BYTES;
-          uint8_t* sA0 = st;
-          uint8_t* sA1 = st + C::A_BYTES;
+          uint8_t* sA = st;                        // 256 rows: A0 then A1
           uint8_t* sB = st + NUM_A * C::A_BYTES;
-          uint8_t* sSFA = sB + C::B_BYTES;
+          uint8_t* sSFA = sB + C::B_BYTES;         // 2 x 512 B
           uint8_t* sSFB = sSFA + NUM_A * C::SF_BYTES;
-          constexpr uint32_t a_tx = G_BM * G_BK / 2;  // packed bytes of one A box
-          constexpr uint32_t b_tx = B_FP4 ? G_BN * G_BK / 2 : G_BN * G_BK;
-          mbar_expect_tx(&full[stage], NUM_A * (a_tx + C::SF_BYTES) + b_tx + C::SF_BYTES);
-          tma_load_5d(sA0, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
-          bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_w);
-          if (NUM_A == 2) {
-            tma_load_5d(sA1, &tmA, &full[stage], 0, 0, kt, rt1, cur.slot, pol_w);
-            bulk_load(sSFA + C::SF_BYTES, sf_base + ((int64_t)rt1 * k_tiles + kt) * C::SF_BYTES, C::SF_BYTES,
-                      &full[stage], pol_w);
-          }
-          tma_load_2d(sB, &tmB, &full[stage], kt * G_BK, cur.row0, pol_x);
+          constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;  // packed bytes of the 256-row A box
+          const uint32_t b_tx = (uint32_t)nb * (B_FP4 ? G_BK / 2 : G_BK);
+          mbar_expect_tx(&full[stage], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+          tma_load_5d(sA, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
+          bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES, &full[stage],
+                    pol_w);
+          tma_load_2d(sB, mB, &full[stage], kt * G_BK, cur.row0, pol_x);
           // B scales: the atom of (k-tile kt, this 64-row chunk), already in tensor-core order
           bulk_load(sSFB, sfb_base + (int64_t)kt * p.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
           mbar_arrive(&full[stage]);
@@ -248,6 +272,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           cur = nxt;
           continue;
         }
+        const int nb = b_rows_for(cur.nrows);
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
@@ -270,7 +295,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const uint64_t dA0 = desc_sw128(aA0), dA1 = desc_sw128(aA1), dB = desc_sw128(aB);
 #pragma unroll
           for (int kb = 0; kb < G_BK / 32; ++kb) {
-            const uint32_t idesc = idesc_mxf8f6f4(G_BN, B_FP4, (uint32_t)kb);
+            const uint32_t idesc = idesc_mxf8f6f4(nb, B_FP4, (uint32_t)kb);
             const uint32_t sel = (uint32_t)kb << 30;
             const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
             // +32 bytes of K per step inside the 128-byte swizzle row
@@ -354,10 +379,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
 
       if constexpr (EPI == EPI_STORE_BF16) {
-        uint16_t* dst = p.out_bf16 + (int64_t)(row0 + c0) * p.out_ld + mt * G_BM + i;
+        // rows 0..127 of the pair -> acc0, rows 128..255 -> acc1
+        uint16_t* dst = p.out_bf16 + (int64_t)(row0 + c0) * p.out_ld + mt * p.out_tile_cols + i;
 #pragma unroll
         for (int n = 0; n < HALF; ++n)
           if (c0 + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+        if constexpr (NUM_A == 2) {
+          uint16_t* dst1 = dst + G_BM;
+#pragma unroll
+          for (int n = 0; n < HALF; ++n)
+            if (c0 + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+        }
       } else {
         // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
         // bf16(h) is the input of the activation re-quantisation.

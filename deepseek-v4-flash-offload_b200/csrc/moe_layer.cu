@@ -2,6 +2,8 @@
 // GEMMs (moe_gemm.cuh) and the deterministic combine, bound together by a
 // plan that owns the TMA descriptors.  Mirrors _routed / _routed_mxfp4
 // (deepseek_v4.py:150-245) of the reference.
+#include <stdlib.h>
+
 #include <algorithm>
 #include <memory>
 #include <string>
@@ -61,19 +63,25 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   int* run = cnt + E;            // E
   int* tot = run + E;            // E
   int* scratch = tot + E;        // 32
-  uint16_t* wc = reinterpret_cast<uint16_t*>(scratch + 32);  // [32][E]
+  int* sidx = scratch + 32;      // AL_THREADS (decode-sized batches)
+  uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool small = P <= AL_THREADS;
+  griddep_wait();
+  griddep_launch();
 
   for (int e = tid; e < E; e += AL_THREADS) cnt[e] = 0;
   __syncthreads();
   for (int p = tid; p < P; p += AL_THREADS) {
-    const int e = idx[p];
+    int e = idx[p];
     if (e < 0 || e >= E) {
       set_status(status, DSV4_EINVAL);
       inv[p] = -1;
-      continue;
+      e = -1;
+    } else {
+      atomicAdd(&cnt[e], 1);
     }
-    atomicAdd(&cnt[e], 1);
+    if (small) sidx[p] = e;
   }
   __syncthreads();
   // exclusive scan of the (padded) group sizes (E <= 1024: one expert per thread)
@@ -93,7 +101,23 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   if (tid == 0) offsets[E] = total;
   __syncthreads();
 
-  for (int base = 0; base < P; base += AL_THREADS) {
+  if (small) {
+    // decode-sized batch: the stable rank of assignment p inside its expert
+    // is the number of earlier assignments with the same expert
+    if (tid < P) {
+      const int e = sidx[tid];
+      if (e >= 0) {
+        int rank = 0;
+        for (int q = 0; q < tid; ++q) rank += (sidx[q] == e) ? 1 : 0;
+        const int pos = run[e] + rank;
+        sorted_flat[pos] = tid;
+        inv[tid] = pos;
+        if (sorted_w) sorted_w[pos] = w_flat[tid];
+      }
+    }
+    __syncthreads();
+  }
+  for (int base = 0; !small && base < P; base += AL_THREADS) {
     for (int j = tid; j < 32 * E; j += AL_THREADS) wc[j] = 0;
     __syncthreads();
     const int p = base + tid;
@@ -147,8 +171,9 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// activation quant + gather into the GEMM B operand.  Sorted row p reads token
-// sorted_flat[p] / topk (padding rows, sorted_flat < 0, are skipped).  Scales
+// activation quant + gather into the GEMM B operand.  Assignment a = t*topk+j
+// writes token t's row to its sorted row inv[a] (padding rows are never
+// touched; invalid assignments, inv < 0, are skipped).  Scales
 // go to 512-byte atoms, one per (128-column k-tile kt, 64-row block rb) at
 // (kt * rb_cap + rb) * 512, row n of the block at (n%32)*16 + (n/32)*4, one
 // byte per 32-block (FP8: the per-128 exponent replicated four times): the
@@ -158,20 +183,22 @@ __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, i
   return ((int64_t)kt * rb_cap + row / 64) * 512 + (row % 32) * 16 + ((row % 64) / 32) * 4;
 }
 
-__global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
-                                        const int* __restrict__ n_rows, int topk, int K, int64_t rb_cap,
+__global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
+                                        int64_t n_assign, int topk, int K, int64_t rb_cap,
                                         uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  griddep_wait();
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
-  const int64_t nblk = (int64_t)(*n_rows) * kblk;
+  const int64_t nblk = n_assign * kblk;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t b = warp0; b < nblk; b += nwarps) {
-    const int64_t p = b / kblk;
-    const int kb = (int)(b - p * kblk);
-    const int src = sorted_flat[p];
-    if (src < 0) continue;
-    const int64_t tok = src / topk;
+    const int64_t asg = b / kblk;          // flat assignment t*topk + j
+    const int kb = (int)(b - asg * kblk);
+    const int64_t p = inv[asg];            // its (padded) sorted row
+    if (p < 0) continue;
+    const int64_t tok = asg / topk;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -187,20 +214,22 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
   }
 }
 
-__global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_flat,
-                                          const int* __restrict__ n_rows, int topk, int K, int64_t rb_cap,
+__global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
+                                          int64_t n_assign, int topk, int K, int64_t rb_cap,
                                           uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  griddep_wait();
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
-  const int64_t nblk = (int64_t)(*n_rows) * kblk;
+  const int64_t nblk = n_assign * kblk;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t b = warp0; b < nblk; b += nwarps) {
-    const int64_t p = b / kblk;
-    const int kb = (int)(b - p * kblk);
-    const int src = sorted_flat[p];
-    if (src < 0) continue;
-    const int64_t tok = src / topk;
+    const int64_t asg = b / kblk;          // flat assignment t*topk + j
+    const int kb = (int)(b - asg * kblk);
+    const int64_t p = inv[asg];            // its (padded) sorted row
+    if (p < 0) continue;
+    const int64_t tok = asg / topk;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -221,8 +250,11 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
 // in ascending sorted position = ascending expert id, fp32 from zero).
 // One block per token, eight columns per thread.
 // ---------------------------------------------------------------------------
+// grid (T, H / (8 * blockDim.x)): each CTA covers 8 * blockDim.x columns.
 __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* __restrict__ inv, int topk, int H,
                                uint16_t* __restrict__ y, int64_t T) {
+  griddep_wait();
+  griddep_launch();
   const int64_t t = blockIdx.x;
   if (t >= T) return;
   int pos[16];
@@ -237,7 +269,7 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
     }
     pos[i] = v;
   }
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+  for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < H; c += gridDim.y * blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
       const uint4 r = *reinterpret_cast<const uint4*>(out + (int64_t)pos[j] * H + c);
@@ -258,6 +290,8 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
 // Same sum, rows taken in the caller's order (no sorting).
 __global__ void combine_ordered_kernel(const uint16_t* __restrict__ rows, const int32_t* __restrict__ order,
                                        int topk, int H, uint16_t* __restrict__ y, int64_t T) {
+  griddep_wait();
+  griddep_launch();
   const int64_t t = blockIdx.x;
   if (t >= T) return;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
@@ -370,8 +404,10 @@ struct dsv4_moe_plan {
   dsv4::SlotLayout slot;
   uint8_t* ws = nullptr;
   dsv4::WsLayout wl;
-  CUtensorMap tmA13, tmA2, tmB1_fp8, tmB1_fp4, tmB2_fp8, tmB2_fp4;
+  CUtensorMap tmA13, tmA2;
+  CUtensorMap tmB1_fp8[3], tmB1_fp4[3], tmB2_fp8[3], tmB2_fp4[3];  // 16, 32, 64 activation rows per box
   bool timing = false;
+  int pf_dist = 0;  // L2 prefetch distance of the weight tiles, in k-tiles (0: off)
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -406,8 +442,8 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
                                     int64_t n_slots, void* workspace, int64_t workspace_bytes) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(out && slot_arena && workspace, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 128 == 0 && inter % 128 == 0,
-                 "hidden and inter must be positive multiples of 128");
+  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 256 == 0 && inter % 128 == 0,
+                 "hidden must be a positive multiple of 256 and inter of 128");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= 1024, "n_experts must be in [1, 1024]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16, "topk must be in [1, 16]");
   DSV4_CHECK_ARG(max_tokens > 0 && n_slots > 0, "max_tokens and n_slots must be positive");
@@ -430,40 +466,44 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   p->slot = slot_layout(hidden, inter);
   p->ws = (uint8_t*)workspace;
   p->wl = wl;
+  if (const char* e = getenv("DSV4_L2_PREFETCH")) p->pf_dist = atoi(e);
   DSV4_CUDA_CHECK(cudaMemset(workspace, 0, (size_t)wl.bytes));
   const uint64_t H = hidden, I = inter, SB = (uint64_t)p->slot.bytes, PC = (uint64_t)wl.p_cap;
   const CUtensorMapDataType U4 = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   int rc;
-  // weights are stored as contiguous 8 KiB blocks of 128 rows x 128 E2M1
-  // elements: dims (element in block row, row in block, k tile, row tile, slot)
-  {  // w13: 2I rows, K = H
-    const uint64_t kt = H / 128, rt = 2 * I / 128;
-    const uint64_t dims[5] = {128, 128, kt, rt, (uint64_t)n_slots}, str[4] = {64, 8192, kt * 8192, SB};
-    const uint32_t box[5] = {G_BK, G_BM, 1, 1, 1};
+  // weights are stored as contiguous 16 KiB blocks of a 256-row pair x 128 E2M1
+  // elements (slot_layout.h): dims (element, row in pair, k tile, pair, slot)
+  {  // w13: I/128 pairs (w1 tile, w3 tile), K = H
+    const uint64_t kt = H / 128, np = I / 128;
+    const uint64_t dims[5] = {128, 256, kt, np, (uint64_t)n_slots}, str[4] = {64, 16384, kt * 16384, SB};
+    const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA13, U4, 5, slot_arena + p->slot.w13p, dims, str, box, "w13")) != 0) return rc;
   }
-  {  // w2: H rows, K = I
-    const uint64_t kt = I / 128, rt = H / 128;
-    const uint64_t dims[5] = {128, 128, kt, rt, (uint64_t)n_slots}, str[4] = {64, 8192, kt * 8192, SB};
-    const uint32_t box[5] = {G_BK, G_BM, 1, 1, 1};
+  {  // w2: H/256 pairs of 128-row tiles, K = I
+    const uint64_t kt = I / 128, np = H / 256;
+    const uint64_t dims[5] = {128, 256, kt, np, (uint64_t)n_slots}, str[4] = {64, 16384, kt * 16384, SB};
+    const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA2, U4, 5, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
   }
-  const uint32_t bbox[2] = {G_BK, G_BN};
-  {
-    const uint64_t dims[2] = {H, PC}, s8[1] = {H}, s4[1] = {H / 2};
-    if ((rc = make_map(&p->tmB1_fp8, U8, 2, p->ws + wl.xq, dims, s8, bbox, "x fp8")) != 0) return rc;
-    if ((rc = make_map(&p->tmB1_fp4, U4, 2, p->ws + wl.xq, dims, s4, bbox, "x fp4")) != 0) return rc;
-  }
-  {
-    const uint64_t dims[2] = {I, PC}, s8[1] = {I}, s4[1] = {I / 2};
-    if ((rc = make_map(&p->tmB2_fp8, U8, 2, p->ws + wl.hq, dims, s8, bbox, "h fp8")) != 0) return rc;
-    if ((rc = make_map(&p->tmB2_fp4, U4, 2, p->ws + wl.hq, dims, s4, bbox, "h fp4")) != 0) return rc;
+  const uint32_t brows[3] = {16, 32, 64};
+  for (int j = 0; j < 3; ++j) {
+    const uint32_t bbox[2] = {G_BK, brows[j]};
+    {
+      const uint64_t dims[2] = {H, PC}, s8[1] = {H}, s4[1] = {H / 2};
+      if ((rc = make_map(&p->tmB1_fp8[j], U8, 2, p->ws + wl.xq, dims, s8, bbox, "x fp8")) != 0) return rc;
+      if ((rc = make_map(&p->tmB1_fp4[j], U4, 2, p->ws + wl.xq, dims, s4, bbox, "x fp4")) != 0) return rc;
+    }
+    {
+      const uint64_t dims[2] = {I, PC}, s8[1] = {I}, s4[1] = {I / 2};
+      if ((rc = make_map(&p->tmB2_fp8[j], U8, 2, p->ws + wl.hq, dims, s8, bbox, "h fp8")) != 0) return rc;
+      if ((rc = make_map(&p->tmB2_fp4[j], U4, 2, p->ws + wl.hq, dims, s4, bbox, "h fp4")) != 0) return rc;
+    }
   }
   if ((rc = prepare_gemm<2, false, EPI_SWIGLU_FP8>()) != 0) return rc;
   if ((rc = prepare_gemm<2, true, EPI_SWIGLU_MXFP4>()) != 0) return rc;
-  if ((rc = prepare_gemm<1, false, EPI_STORE_BF16>()) != 0) return rc;
-  if ((rc = prepare_gemm<1, true, EPI_STORE_BF16>()) != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32) * 4 + (size_t)32 * n_experts * 2;
+  if ((rc = prepare_gemm<2, false, EPI_STORE_BF16>()) != 0) return rc;
+  if ((rc = prepare_gemm<2, true, EPI_STORE_BF16>()) != 0) return rc;
+  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 2;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   *out = p.release();
@@ -493,33 +533,27 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   int32_t* inv = wsp<int32_t>(p, w.inv);
   int32_t* n_active = wsp<int32_t>(p, w.n_active);
   int* n_chunks = wsp<int>(p, w.n_chunks);
-  const size_t al_smem = (size_t)(3 * p->E + 32) * 4 + (size_t)32 * p->E * 2;
+  const size_t al_smem = (size_t)(3 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 2;
   auto mark = [&](int i) {
     if (p->timing) cudaEventRecord(p->ev[i], st);
   };
+  // events between stages break the programmatic overlap: no PDL while timing
+  const bool pdl = pdl_enabled() && !p->timing;
   mark(0);
-  moe_align_kernel<<<1, AL_THREADS, al_smem, st>>>(
-      route_indices, P, p->topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
-      sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w), wsp<int4>(p, w.chunks),
-      n_chunks, G_BN, status);
+  DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, p->topk,
+                           p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets), sorted_flat,
+                           inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
+                           wsp<int4>(p, w.chunks), n_chunks, (int)G_BN, status));
   mark(1);
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
-  // the gather reads the padded row count from the align output (offsets[E])
-  const int* n_rows = wsp<int>(p, w.offsets) + p->E;
   const int64_t rb_cap = w.p_cap / G_BN;
   {
-    const int64_t rows_max = std::min<int64_t>(w.p_cap, (int64_t)P + (int64_t)(G_BN - 1) * std::min(P, p->E));
-    const int64_t warps = rows_max * (p->H / 128);
+    const int64_t warps = (int64_t)P * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
-    if (fp4)
-      quant_gather_mxfp4_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
-                                                                  p->topk, p->H, rb_cap, p->ws + w.xq,
-                                                                  p->ws + w.xsf);
-    else
-      quant_gather_fp8_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint16_t*)x_bf16, sorted_flat, n_rows,
-                                                                p->topk, p->H, rb_cap, p->ws + w.xq,
-                                                                p->ws + w.xsf);
+    DSV4_CUDA_CHECK(launch_k(fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
+                             dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, (int64_t)P,
+                             p->topk, p->H, rb_cap, p->ws + w.xq, p->ws + w.xsf));
   }
   mark(2);
   GemmParams g1{};
@@ -527,8 +561,9 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g1.slot_bytes = p->slot.bytes;
   g1.sfa_off = p->slot.sf13;
   g1.k_tiles = p->H / 128;
-  g1.a_row_tiles = p->I / 128;
-  g1.a1_row_offset = p->I;
+  g1.a_row_tiles = p->I / 128;   // one (w1, w3) tile pair per work tile
+  g1.out_tile_cols = 128;
+  g1.pf_dist = p->pf_dist;
   g1.b_sf = p->ws + w.xsf;
   g1.rb_cap = rb_cap;
   g1.chunks = wsp<int4>(p, w.chunks);
@@ -544,8 +579,8 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   GemmParams g2 = g1;
   g2.sfa_off = p->slot.sf2;
   g2.k_tiles = p->I / 128;
-  g2.a_row_tiles = p->H / 128;
-  g2.a1_row_offset = 0;
+  g2.a_row_tiles = p->H / 256;   // two 128-row tiles of w2 per work tile
+  g2.out_tile_cols = 256;
   g2.b_sf = p->ws + w.hsf;
   g2.out_q = nullptr;
   g2.out_sf = nullptr;
@@ -553,17 +588,26 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g2.out_ld = p->H;
   const dim3 grid(p->num_sms), block(G_THREADS);
   if (fp4)
-    moe_gemm_kernel<2, true, EPI_SWIGLU_MXFP4><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp4, g1);
+    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, true, EPI_SWIGLU_MXFP4>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
+                             p->tmA13, p->tmB1_fp4[0], p->tmB1_fp4[1], p->tmB1_fp4[2], g1));
   else
-    moe_gemm_kernel<2, false, EPI_SWIGLU_FP8><<<grid, block, GemmCfg<2>::SMEM_BYTES, st>>>(p->tmA13, p->tmB1_fp8, g1);
+    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, false, EPI_SWIGLU_FP8>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
+                             p->tmA13, p->tmB1_fp8[0], p->tmB1_fp8[1], p->tmB1_fp8[2], g1));
   mark(3);
   if (fp4)
-    moe_gemm_kernel<1, true, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp4, g2);
+    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, true, EPI_STORE_BF16>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
+                             p->tmA2, p->tmB2_fp4[0], p->tmB2_fp4[1], p->tmB2_fp4[2], g2));
   else
-    moe_gemm_kernel<1, false, EPI_STORE_BF16><<<grid, block, GemmCfg<1>::SMEM_BYTES, st>>>(p->tmA2, p->tmB2_fp8, g2);
+    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, false, EPI_STORE_BF16>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
+                             p->tmA2, p->tmB2_fp8[0], p->tmB2_fp8[1], p->tmB2_fp8[2], g2));
   mark(4);
-  combine_kernel<<<(unsigned)n_tokens, std::min(1024, p->H / 8), 0, st>>>(wsp<uint16_t>(p, w.out), inv, p->topk,
-                                                                          p->H, (uint16_t*)y_bf16, n_tokens);
+  {
+    const int threads = std::min(128, p->H / 8);
+    const unsigned gy = (unsigned)std::max(1, p->H / (8 * threads));
+    DSV4_CUDA_CHECK(launch_k(combine_kernel, dim3((unsigned)n_tokens, gy), dim3(threads), 0, st, pdl,
+                             (const uint16_t*)wsp<uint16_t>(p, w.out), (const int32_t*)inv, p->topk, p->H,
+                             (uint16_t*)y_bf16, (int64_t)n_tokens));
+  }
   mark(5);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
@@ -628,7 +672,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * topk < (1LL << 31), "too many assignments");
   int rc = bind_device_of(counts, nullptr);
   if (rc != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32) * 4 + (size_t)32 * n_experts * 2;
+  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 2;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(

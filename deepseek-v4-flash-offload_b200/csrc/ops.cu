@@ -3,6 +3,7 @@
 // All are HBM-bound: 128-bit loads/stores, one warp per 128-element block.
 #include "capi_internal.h"
 #include "common.cuh"
+#include "slot_layout.h"
 
 namespace dsv4 {
 
@@ -38,28 +39,17 @@ __global__ void dequant_mxfp4_kernel(const uint8_t* __restrict__ w, const uint8_
   }
 }
 
-// Byte offset of scale (row r, 32-block kb) inside the tiled scale atoms of a
-// [rows, k] matrix: atom (r/128, kb/4) of 512 B, row r at (r%32)*16 +
-// ((r%128)/32)*4, block kb%4 in the low 2 bits.
-__host__ __device__ __forceinline__ int64_t sf_atom_offset(int64_t r, int64_t kb, int64_t k) {
-  const int64_t ktiles = k / 128;
-  return ((r / 128) * ktiles + kb / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (kb % 4);
-}
-
-// Byte offset of packed element pair (row r, element k0) in the 8 KiB tiled
-// weight blocks of a [rows, k] matrix.
-__host__ __device__ __forceinline__ int64_t w_tile_offset(int64_t r, int64_t k0, int64_t k) {
-  return ((r / 128) * (k / 128) + k0 / 128) * 8192 + (r % 128) * 64 + (k0 % 128) / 2;
-}
-
+// Dequant of one matrix of a packed slot (layout in slot_layout.h); row r of
+// the output is paired-matrix row (r/128)*pair_stride + pair_base + r%128.
 __global__ void slot_dequant_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf,
-                                    uint16_t* __restrict__ out, int64_t rows, int64_t k, int64_t row_base) {
+                                    uint16_t* __restrict__ out, int64_t rows, int64_t k, int pair_stride,
+                                    int pair_base) {
   const int64_t kb = k / 32;
   const int64_t n = rows * kb;
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n; c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = c / kb, b = c - r * kb;
-    dequant_block32(w + w_tile_offset(row_base + r, b * 32, k), sf[sf_atom_offset(row_base + r, b, k)],
-                    out + r * k + b * 32);
+    const int64_t R = (r / 128) * pair_stride + pair_base + r % 128;
+    dequant_block32(w + w_pair_offset(R, b * 32, k), sf[sf_pair_offset(R, b, k)], out + r * k + b * 32);
   }
 }
 
@@ -155,18 +145,19 @@ extern "C" int dsv4_slot_dequant(const uint8_t* slot, int32_t hidden, int32_t in
                                  void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(slot && w1 && w2 && w3, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 128 == 0 && inter % 128 == 0,
-                 "hidden and inter must be positive multiples of 128");
+  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 256 == 0 && inter % 128 == 0,
+                 "hidden must be a positive multiple of 256 and inter of 128");
   const SlotLayout L = slot_layout(hidden, inter);
   if (int rc = bind_device_of(slot, nullptr)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t items13 = (int64_t)inter * (hidden / 32), items2 = (int64_t)hidden * (inter / 32);
+  // w1 row r is paired row (r/128)*256 + r%128, w3 row r is (r/128)*256 + 128 + r%128, w2 row r is r
   slot_dequant_kernel<<<grid_for(items13, 256), 256, 0, st>>>(slot + L.w13p, slot + L.sf13, (uint16_t*)w1, inter,
-                                                              hidden, 0);
+                                                              hidden, 256, 0);
   slot_dequant_kernel<<<grid_for(items13, 256), 256, 0, st>>>(slot + L.w13p, slot + L.sf13, (uint16_t*)w3, inter,
-                                                              hidden, inter);
+                                                              hidden, 256, 128);
   slot_dequant_kernel<<<grid_for(items2, 256), 256, 0, st>>>(slot + L.w2p, slot + L.sf2, (uint16_t*)w2, hidden,
-                                                             inter, 0);
+                                                             inter, 128, 0);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

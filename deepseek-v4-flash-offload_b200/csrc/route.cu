@@ -13,64 +13,74 @@
 namespace dsv4 {
 
 constexpr int RT_MAX_E = 256;
-constexpr int RT_TOK = 256;   // tokens per CTA (grid y)
+constexpr int RT_EPB = 8;      // experts per CTA (one warp each)
+constexpr int RT_TT = 64;      // tokens per CTA (two per lane)
+constexpr int RT_KC = 64;      // K elements per shared-memory tile
+constexpr int RT_SPLIT = 16;   // split of H on the workspace path; partials summed in order by the top-k kernel
+constexpr int RT_SPLIT_NOALLOC = 4;  // split on the fixed-scratch path
 
-// logits[t, e] = sum_h float(x[t, h]) * w[e, h].  A CTA keeps EPB gate rows in
-// shared memory; each warp takes whole (token, expert-group) dot products,
-// lanes stride H in 4-element steps, then a fixed butterfly reduction: one
-// writer per logit, so the result is deterministic.
-template <int EPB>
+// partial[c, t, e] = sum over H-chunk c of float(x[t, h]) * w[e, h].  Tiles of
+// 64 tokens x 64 h (bf16 -> f32, padded rows) and 8 gate rows x 64 h are
+// staged in shared memory; warp w owns expert e0 + w, lane owns tokens lane
+// and lane + 32.  One writer per partial: deterministic.
 __global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __restrict__ x,
-                                                           const float* __restrict__ w, float* __restrict__ logits,
-                                                           int64_t T, int H, int E) {
-  extern __shared__ float ws[];  // [EPB][H]
-  const int e0 = blockIdx.x * EPB;
-  for (int i = threadIdx.x * 4; i < EPB * H; i += blockDim.x * 4) {
-    const int r = i / H, c = i - r * H;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (e0 + r < E) v = *reinterpret_cast<const float4*>(w + (int64_t)(e0 + r) * H + c);
-    *reinterpret_cast<float4*>(ws + i) = v;
-  }
-  __syncthreads();
+                                                           const float* __restrict__ w, float* __restrict__ part,
+                                                           int64_t T, int H, int E, int split) {
+  __shared__ float xs[RT_TT][RT_KC + 1];
+  __shared__ float ws[RT_EPB][RT_KC];
+  griddep_wait();
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t_end = min(T, (int64_t)(blockIdx.y + 1) * RT_TOK);
-  for (int64_t t = (int64_t)blockIdx.y * RT_TOK + warp; t < t_end; t += blockDim.x >> 5) {
-    float acc[EPB];
-#pragma unroll
-    for (int j = 0; j < EPB; ++j) acc[j] = 0.f;
-    const uint16_t* xr = x + t * H;
-    for (int h = lane * 4; h < H; h += 128) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(xr + h);
-      const float a0 = bf16_from_bits(raw.x & 0xffffu), a1 = bf16_from_bits(raw.x >> 16);
-      const float a2 = bf16_from_bits(raw.y & 0xffffu), a3 = bf16_from_bits(raw.y >> 16);
-#pragma unroll
-      for (int j = 0; j < EPB; ++j) {
-        const float4 g = *reinterpret_cast<const float4*>(ws + j * H + h);
-        acc[j] = fmaf(a0, g.x, acc[j]);
-        acc[j] = fmaf(a1, g.y, acc[j]);
-        acc[j] = fmaf(a2, g.z, acc[j]);
-        acc[j] = fmaf(a3, g.w, acc[j]);
+  const int e0 = blockIdx.x * RT_EPB;
+  const int chunk = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.z * RT_TT;
+  const int kc = H / split;
+  const int kbeg = chunk * kc;
+  float a0 = 0.f, a1 = 0.f;
+  for (int k0 = kbeg; k0 < kbeg + kc; k0 += RT_KC) {
+    for (int i = threadIdx.x; i < RT_TT * RT_KC / 2; i += 256) {
+      const int r = i / (RT_KC / 2), c = (i % (RT_KC / 2)) * 2;
+      float lo = 0.f, hi = 0.f;
+      if (t0 + r < T) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(x + (t0 + r) * H + k0 + c);
+        lo = bf16_from_bits(v & 0xffffu);
+        hi = bf16_from_bits(v >> 16);
       }
+      xs[r][c] = lo;
+      xs[r][c + 1] = hi;
     }
-#pragma unroll
-    for (int j = 0; j < EPB; ++j) {
-      float v = acc[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0 && e0 + j < E) logits[t * E + e0 + j] = v;
+    for (int i = threadIdx.x; i < RT_EPB * RT_KC; i += 256) {
+      const int r = i / RT_KC, c = i % RT_KC;
+      ws[r][c] = (e0 + r < E) ? w[(int64_t)(e0 + r) * H + k0 + c] : 0.f;
     }
+    __syncthreads();
+#pragma unroll 16
+    for (int k = 0; k < RT_KC; ++k) {
+      const float g = ws[warp][k];
+      a0 = fmaf(xs[lane][k], g, a0);
+      a1 = fmaf(xs[lane + 32][k], g, a1);
+    }
+    __syncthreads();
+  }
+  const int e = e0 + warp;
+  if (e < E) {
+    float* dst = part + (int64_t)chunk * T * E;
+    if (t0 + lane < T) dst[(t0 + lane) * E + e] = a0;
+    if (t0 + lane + 32 < T) dst[(t0 + lane + 32) * E + e] = a1;
   }
 }
 
 __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log1pf(expf(v)); }
 
-__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int64_t T,
+__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int split, int64_t T,
                                                          int E, int K, int score_func, int renorm, float scale,
                                                          const float* __restrict__ bias,
                                                          const int32_t* __restrict__ tid2eid,
                                                          const int64_t* __restrict__ ids, float* __restrict__ w_out,
                                                          int32_t* __restrict__ i_out) {
   constexpr int PER = RT_MAX_E / 32;
+  griddep_wait();
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (t >= T) return;
@@ -78,7 +88,17 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    sc[j] = (e < E) ? logits[t * E + e] : -INFINITY;
+    float l = 0.f;
+    if (e < E) {
+      // partial sums of the H chunks, loaded together, added in chunk order
+      float v[RT_SPLIT];
+#pragma unroll
+      for (int c = 0; c < RT_SPLIT; ++c) v[c] = c < split ? logits[((int64_t)c * T + t) * E + e] : 0.f;
+#pragma unroll
+      for (int c = 0; c < RT_SPLIT; ++c)
+        if (c < split) l += v[c];
+    }
+    sc[j] = (e < E) ? l : -INFINITY;
   }
   if (score_func == DSV4_SCORE_SOFTMAX) {
     float m = -INFINITY;
@@ -167,7 +187,7 @@ using namespace dsv4;
 
 extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts) {
   if (n_tokens < 0 || hidden <= 0 || n_experts <= 0) return DSV4_EINVAL;
-  return n_tokens * n_experts * (int64_t)sizeof(float);
+  return RT_SPLIT * n_tokens * n_experts * (int64_t)sizeof(float);
 }
 
 extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
@@ -177,7 +197,7 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
                                void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out && workspace, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && hidden % 128 == 0 && hidden <= 6144, "hidden must be a multiple of 128, <= 6144");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % (RT_SPLIT * RT_KC) == 0, "hidden must be a positive multiple of 1024");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
@@ -187,22 +207,14 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   if (n_tokens == 0) return DSV4_OK;
   if (int rc = bind_device_of(x_bf16, nullptr)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const unsigned gy = (unsigned)((n_tokens + RT_TOK - 1) / RT_TOK);
-  if (n_tokens <= 512) {  // decode: 2 gate rows per CTA, E/2 CTAs
-    const size_t smem = (size_t)2 * hidden * sizeof(float);
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    route_logits_kernel<2><<<dim3((n_experts + 1) / 2, gy), 256, smem, st>>>(
-        (const uint16_t*)x_bf16, gate_w, (float*)workspace, n_tokens, hidden, n_experts);
-  } else {  // prefill: 8 gate rows per CTA so x is re-read E/8 times
-    const size_t smem = (size_t)8 * hidden * sizeof(float);
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    route_logits_kernel<8><<<dim3((n_experts + 7) / 8, gy), 256, smem, st>>>(
-        (const uint16_t*)x_bf16, gate_w, (float*)workspace, n_tokens, hidden, n_experts);
-  }
+  const dim3 grid((n_experts + RT_EPB - 1) / RT_EPB, RT_SPLIT, (unsigned)((n_tokens + RT_TT - 1) / RT_TT));
+  const bool pdl = pdl_enabled();
+  DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
+                           (float*)workspace, n_tokens, hidden, n_experts, RT_SPLIT));
   const int64_t threads = n_tokens * 32;
-  route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      (const float*)workspace, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid,
-      input_ids, weights_out, indices_out);
+  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, pdl,
+                           (const float*)workspace, RT_SPLIT, n_tokens, n_experts, topk, score_func, renormalize,
+                           route_scale, bias, tid2eid, input_ids, weights_out, indices_out));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
@@ -216,9 +228,10 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
 // plain C caller bound through an FFI may have no device allocator at all.
 // For them the logits scratch of the router lives in this fixed file-scope
 // device array instead of a caller workspace.  Limits and rules:
-//   * at most DSV4_ROUTE_NOALLOC_MAX_LOGITS (n_tokens * n_experts) logits,
-//     256 KiB of device memory that every GPU loading the library keeps
-//     until the process exits; larger calls are rejected with DSV4_EINVAL;
+//   * at most DSV4_ROUTE_NOALLOC_MAX_LOGITS (n_tokens * n_experts) logits;
+//     the array holds the router's fixed split of partial sums for that many
+//     logits (1 MiB of device memory that every GPU loading the library keeps
+//     until the process exits); larger calls are rejected with DSV4_EINVAL;
 //   * the first call on a device looks up the array's device address on
 //     that device (cudaGetSymbolAddress); make that first call before any
 //     stream capture;
@@ -227,7 +240,7 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
 //     nothing needs clearing, but calls that overlap on the GPU (on different
 //     streams, or from several threads) race on it.
 // ---------------------------------------------------------------------------
-static __device__ __align__(256) float g_route_noalloc_scratch[DSV4_ROUTE_NOALLOC_MAX_LOGITS];
+static __device__ __align__(256) float g_route_noalloc_scratch[RT_SPLIT_NOALLOC * DSV4_ROUTE_NOALLOC_MAX_LOGITS];
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -242,7 +255,7 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
                                        int32_t* indices_out, void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && hidden % 128 == 0 && hidden <= 6144, "hidden must be a multiple of 128, <= 6144");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % (RT_SPLIT * RT_KC) == 0, "hidden must be a positive multiple of 1024");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
@@ -267,21 +280,12 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
     scratch = g_noalloc_ptr[dev];
   }
   cudaStream_t st = (cudaStream_t)stream;
-  const unsigned gy = (unsigned)((n_tokens + RT_TOK - 1) / RT_TOK);
-  if (n_tokens <= 512) {
-    const size_t smem = (size_t)2 * hidden * sizeof(float);
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    route_logits_kernel<2><<<dim3((n_experts + 1) / 2, gy), 256, smem, st>>>(
-        (const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts);
-  } else {
-    const size_t smem = (size_t)8 * hidden * sizeof(float);
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    route_logits_kernel<8><<<dim3((n_experts + 7) / 8, gy), 256, smem, st>>>(
-        (const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts);
-  }
+  const dim3 grid((n_experts + RT_EPB - 1) / RT_EPB, RT_SPLIT_NOALLOC, (unsigned)((n_tokens + RT_TT - 1) / RT_TT));
+  route_logits_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts,
+                                            RT_SPLIT_NOALLOC);
   const int64_t threads = n_tokens * 32;
   route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      scratch, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
+      scratch, RT_SPLIT_NOALLOC, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
       weights_out, indices_out);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END

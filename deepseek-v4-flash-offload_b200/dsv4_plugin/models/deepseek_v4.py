@@ -154,7 +154,8 @@ class OffloadDeepseekV4MoE(nn.Module):
         slot_of, slots = self._slot_table(indices)
         plan = self.engine.plan_for(self.n_routed_experts, self.topk, hs.shape[0], self.swiglu_limit or 0.0)
         y = plan.forward(hs, weights, indices, slot_of, profile)
-        self.engine.bank.mark_used(slots)
+        if not torch.cuda.is_current_stream_capturing():
+            self.engine.bank.mark_used(slots)
         return y
 
     def _routed(self, hs: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:

@@ -104,7 +104,7 @@ int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, 
  * engine whose cache pool already holds nearly all free HBM, or a C caller
  * without a device allocator).  Same arguments and results as
  * dsv4_route_topk minus the workspace: the logits scratch is a fixed
- * 256 KiB device array inside the library, so n_tokens * n_experts must not
+ * 1 MiB device array inside the library, so n_tokens * n_experts must not
  * exceed DSV4_ROUTE_NOALLOC_MAX_LOGITS (larger calls return DSV4_EINVAL).
  * The first call on a device resolves the array's address on that device;
  * make it before any stream capture.  All calls share the array: calls that

@@ -40,26 +40,22 @@ def test_slot_bytes(lib):
     assert L.dsv4_expert_slot_bytes(4096, 2048) == 13369344
     assert L.dsv4_expert_slot_bytes(1024, 512) == 835584
     assert L.dsv4_expert_slot_bytes(1000, 512) == lib.DSV4_EINVAL
+    assert L.dsv4_expert_slot_bytes(1152, 512) == lib.DSV4_EINVAL   # hidden must pair 128-row tiles
 
 
-def _tile_py(s, row_base, k, atoms):
-    """Python restatement of the scale-atom layout."""
-    rows, kb_n = s.shape
-    for r in range(rows):
-        R = row_base + r
-        for kb in range(kb_n):
-            off = ((R // 128) * (k // 128) + kb // 4) * 512 + (R % 32) * 16 + ((R % 128) // 32) * 4 + kb % 4
-            atoms[off] = s[r, kb]
-
-
-def _tile_w_py(w, row_base, k, out):
-    """Python restatement of the 8 KiB weight blocks (128 rows x 128 elements)."""
+def _pack_py(w, sc, k, row_of, wout, sout):
+    """Python restatement of the paired slot layout (256-row pairs x 128 K)."""
     rows = w.shape[0]
     for r in range(rows):
-        R = row_base + r
+        R = row_of(r)
         for kt in range(k // 128):
-            off = ((R // 128) * (k // 128) + kt) * 8192 + (R % 128) * 64
-            out[off: off + 64] = w[r, kt * 64: kt * 64 + 64]
+            off = ((R // 256) * (k // 128) + kt) * 16384 + (R % 256) * 64
+            wout[off: off + 64] = w[r, kt * 64: kt * 64 + 64]
+        rr = R % 128
+        for kb in range(k // 32):
+            off = ((R // 256) * (k // 128) + kb // 4) * 1024 + ((R % 256) // 128) * 512 + (rr % 32) * 16 + \
+                (rr // 32) * 4 + kb % 4
+            sout[off] = sc[r, kb]
 
 
 def test_pack_unpack_round_trip(lib):
@@ -72,21 +68,16 @@ def test_pack_unpack_round_trip(lib):
     h, i = cfg.hidden, cfg.inter
     sb = slot.numpy()
     assert sb.size == 835584
-    w13 = np.zeros(i * h, np.uint8)
-    _tile_w_py(ex["w1p"], 0, h, w13)
-    _tile_w_py(ex["w3p"], i, h, w13)
-    assert np.array_equal(sb[: i * h], w13)
-    w2 = np.zeros(h * i // 2, np.uint8)
-    _tile_w_py(ex["w2p"], 0, i, w2)
-    assert np.array_equal(sb[i * h: i * h + h * i // 2], w2)
-    sf13 = np.zeros(2 * i * h // 32, np.uint8)
-    _tile_py(ex["w1s"], 0, h, sf13)
-    _tile_py(ex["w3s"], i, h, sf13)
+    w13, s13 = np.zeros(i * h, np.uint8), np.zeros(2 * i * h // 32, np.uint8)
+    _pack_py(ex["w1p"], ex["w1s"], h, lambda r: (r // 128) * 256 + r % 128, w13, s13)
+    _pack_py(ex["w3p"], ex["w3s"], h, lambda r: (r // 128) * 256 + 128 + r % 128, w13, s13)
+    w2, s2 = np.zeros(h * i // 2, np.uint8), np.zeros(h * i // 32, np.uint8)
+    _pack_py(ex["w2p"], ex["w2s"], i, lambda r: r, w2, s2)
     o = i * h + h * i // 2
-    assert np.array_equal(sb[o: o + sf13.size], sf13)
-    sf2 = np.zeros(h * i // 32, np.uint8)
-    _tile_py(ex["w2s"], 0, i, sf2)
-    assert np.array_equal(sb[o + sf13.size:], sf2)
+    assert np.array_equal(sb[: i * h], w13)
+    assert np.array_equal(sb[i * h: o], w2)
+    assert np.array_equal(sb[o: o + s13.size], s13)
+    assert np.array_equal(sb[o + s13.size:], s2)
     back = ops.unpack_expert(slot, h, i)
     for k in ex:
         assert np.array_equal(back[k].numpy(), ex[k]), k
