@@ -199,12 +199,18 @@ def _peaks():
 
 
 def _traffic():
-    """Per-launch DRAM bytes of the gate/up GEMM from the committed ncu summary."""
+    """Per-launch DRAM bytes (read + write) of the gate/up GEMM from the
+    committed ncu summary, with the algorithmic bytes of that same launch."""
+    out = {}
     try:
-        with open(os.path.join(ROOT, "profiles", "ncu_gate_up_gemm_cfg1_t64.json")) as f:
-            return json.load(f)
+        with open(os.path.join(ROOT, "profiles", "moe_gemm_cfg1_t64_bf16.md")) as f:
+            for line in f:
+                k, sep, v = line.partition(":")
+                if sep and k.strip() in ("dram_bytes_per_launch", "algorithmic_bytes_per_launch"):
+                    out[k.strip()] = int(v.strip())
     except (OSError, ValueError):
         return None
+    return out if "dram_bytes_per_launch" in out else None
 
 
 # ---------------------------------------------------------------------------
@@ -311,7 +317,10 @@ def run_ours(a):
     roofline = {"bound": "hbm", "kernel": "moe_gemm_kernel<2,false,0> (gate/up, bf16 profile)",
                 "achieved": round(ach1, 1), "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
                 "unit": "GB/s", "frac": round(ach1 / hbm, 4),
-                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch "
+                                   "(token batch 0, profiles/moe_gemm_cfg1_t64_bf16.md); algorithmic bytes of "
+                                   f"that launch: {traffic.get('algorithmic_bytes_per_launch')}") if traffic else None,
                 "algorithmic_bytes_per_launch": round(g1_bytes / len(ds)),
                 "launch_ms": round(g1_ms / len(ds), 5)}
     detail = {"active_experts_mean": round(statistics.mean(ds), 2),
