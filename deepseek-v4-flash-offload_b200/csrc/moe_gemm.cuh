@@ -1,31 +1,40 @@
 // Grouped expert GEMM on the sm_100a tensor cores (tcgen05, TMEM, TMA).
 //
 // Swap-AB formulation: the weight rows of one expert are the MMA M side
-// (128 rows per tile), the tokens routed to that expert are the N side
-// (64 per tile), K runs along the hidden (or intermediate) dimension:
+// (128 rows per MMA, two MMAs per 256-row weight pair), the tokens routed to
+// that expert are the N side (up to 64 per tile), K runs along the hidden (or
+// intermediate) dimension:
 //     D[w_row, token] = sum_k W[w_row, k] * X[token, k]
-// A = packed E2M1 weights straight from the expert slot, one contiguous 8 KiB
-// block per 128x128 tile (TMA type 16U4_ALIGN16B expands them to the
-// one-byte-per-element shared-memory form the f8f6f4 tensor-core path
-// reads), with their E8M0 per-32 scales;
+// A = packed E2M1 weights straight from the expert slot, one contiguous
+// 16 KiB block per (256-row pair, 128 of K) (TMA type 16U4_ALIGN16B expands
+// them to the one-byte-per-element shared-memory form the f8f6f4 tensor-core
+// path reads), with their E8M0 per-32 scales;
 // B = E4M3 activations (bf16 profile) or E2M1 activations (a4w4), with E8M0
 // per-32 scales.  One tcgen05.mma.kind::mxf8f6f4.block_scale per 32 of K.
 // The products equal those of bf16(dequant(W)) x bf16(fp8_roundtrip(X)) of
 // the reference exactly, so only accumulation order differs.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over tiles):
+// Decode MMAs are tiny (N = 16 tokens).  A tcgen05 instruction costs the
+// thread that issues it about 60-70 cycles whatever N is (up to 128), while
+// the tensor pipe itself stays mostly idle, so one issuing thread per CTA
+// caps the weight stream well below HBM speed.  Each 128-row half of the
+// weight pair therefore has its own issuing thread, scale copies and
+// accumulator; the two run in parallel on every stage.
+//
+// Warp roles (352 threads, one CTA per SM, persistent over tiles):
 //   warp 0     producer: TMA for A and B, bulk copies of the A and B scale
 //              atoms, one mbarrier per stage;
-//   warp 1     TMEM owner and MMA issuer (one thread);
+//   warp 1     TMEM owner, MMA issuer for weight rows 0-127 of the pair;
 //   warps 2-9  epilogue: TMEM -> registers -> fused math -> global; two
-//              warps per TMEM lane quarter, each taking half the columns.
+//              warps per TMEM lane quarter, each taking half the columns;
+//   warp 10    MMA issuer for weight rows 128-255 of the pair.
 // Every role walks the same tile sequence and loads the next tile's
 // metadata (chunk, slot) one tile ahead, so tile boundaries cost no
 // dependent global-memory round trip.
-// NUM_A = 2 runs the gate (w1) and up (w3) projections of the same 128
-// intermediate rows into two accumulators; NUM_A = 1 runs the down
-// projection.  Accumulators are double-buffered in TMEM so the epilogue of
-// one tile overlaps the main loop of the next.
+// Gate/up runs the gate (w1) and up (w3) rows of the same 128 intermediate
+// rows into two accumulators; down runs two consecutive 128-row tiles of w2.
+// Accumulators are double-buffered in TMEM so the epilogue of one tile
+// overlaps the main loop of the next.
 #pragma once
 
 #include "common.cuh"
@@ -36,9 +45,10 @@ constexpr int G_BM = 128;
 constexpr int G_BN = 64;
 constexpr int G_BK = 128;
 constexpr int G_EPI_WARPS = 8;
-constexpr int G_THREADS = 64 + 32 * G_EPI_WARPS;
+constexpr int G_MMA2_WARP = 2 + G_EPI_WARPS;   // MMA issuer of weight rows 128-255
+constexpr int G_THREADS = 32 * (G_MMA2_WARP + 1);
 constexpr uint32_t G_TMEM_COLS = 512;
-constexpr uint32_t G_SF_COL = 256;   // TMEM columns 256..267 hold scale factors
+constexpr uint32_t G_SF_COL = 256;   // TMEM columns 256..271: A and B scales of each issuer
 
 enum : int { EPI_SWIGLU_FP8 = 0, EPI_SWIGLU_MXFP4 = 1, EPI_STORE_BF16 = 2 };
 
@@ -49,7 +59,7 @@ struct GemmCfg {
   static constexpr int SF_BYTES = 512;
   static constexpr int STAGE_RAW = NUM_A * A_BYTES + B_BYTES + (NUM_A + 1) * SF_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int STAGES = NUM_A == 2 ? 5 : 8;
+  static constexpr int STAGES = 5;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * G_BN * 4 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -62,7 +72,6 @@ struct GemmParams {
   int k_tiles;               // K / 128
   int a_row_tiles;           // tiles per chunk = 256-row weight pairs of the matrix
   int out_tile_cols;         // output columns per tile (128: gate/up pair, 256: down pair)
-  int pf_dist;               // L2 prefetch distance in k-tiles (0: off)
   const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, 64-row block)
   int64_t rb_cap;            // 64-row blocks per k-tile in b_sf / out_sf
   const int4* chunks;        // {expert, row0, nrows, 0}
@@ -143,13 +152,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 2);   // one commit from each MMA issuer
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&accfull[b], 1);
+      mbar_init(&accfull[b], 2);
       mbar_init(&accempty[b], G_EPI_WARPS);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     *epi_fail = 0;
     fence_barrier_init();
   }
@@ -198,21 +207,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / G_BN) * C::SF_BYTES;
         const int nb = b_rows_for(cur.nrows);
         const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : &tmB64);
-        if (p.pf_dist > 0 && nxt.slot >= 0)  // the next tile's weight scales
-          bulk_prefetch_l2(p.arena + (int64_t)nxt.slot * p.slot_bytes + p.sfa_off +
-                               (int64_t)nxt.mt * k_tiles * 2 * C::SF_BYTES, k_tiles * 2 * C::SF_BYTES);
-        if (p.pf_dist > 0 && t == (int)blockIdx.x) {  // first tile of this CTA
-          bulk_prefetch_l2(sf_base + (int64_t)cur.mt * k_tiles * 2 * C::SF_BYTES, k_tiles * 2 * C::SF_BYTES);
-          for (int j = 0; j < p.pf_dist && j < k_tiles; ++j) tma_prefetch_5d(&tmA, 0, 0, j, cur.mt, cur.slot);
-        }
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (p.pf_dist > 0) {  // keep pf_dist k-tiles of weights on their way into L2
-            const int kp = kt + p.pf_dist;
-            if (kp < k_tiles)
-              tma_prefetch_5d(&tmA, 0, 0, kp, cur.mt, cur.slot);
-            else if (nxt.slot >= 0 && kp - k_tiles < k_tiles)
-              tma_prefetch_5d(&tmA, 0, 0, kp - k_tiles, nxt.mt, nxt.slot);
-          }
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             ok = false;
             break;
@@ -256,15 +251,18 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == G_MMA2_WARP) {
+    // ----------------------------------------------------------- MMA issuers
     if (lane == 0) {
+      const int half = warp == 1 ? 0 : 1;   // weight rows 0-127 or 128-255 of the pair
       int stage = 0;
       uint32_t phase = 0;
       int abuf = 0;
       uint32_t aphase = 0;
       bool ok = true;
-      const uint32_t sfa0 = tmem + G_SF_COL, sfa1 = tmem + G_SF_COL + 4, sfb = tmem + G_SF_COL + 8;
+      // each issuer copies the scales it reads into its own TMEM columns:
+      // tcgen05 operations of different threads are not ordered
+      const uint32_t sfa = tmem + G_SF_COL + 8 * half, sfb = tmem + G_SF_COL + 8 * half + 4;
       TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
       for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
         const TileInfo nxt = load_tile(p, t + step, n_tiles);
@@ -276,8 +274,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
-        const uint32_t d0 = tmem + (uint32_t)abuf * (NUM_A * G_BN);
-        const uint32_t d1 = d0 + G_BN;
+        const uint32_t d = tmem + (uint32_t)abuf * (NUM_A * G_BN) + (uint32_t)half * G_BN;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&full[stage], phase, p.status)) {
             ok = false;
@@ -285,22 +282,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           tc_fence_after();
           uint8_t* st = smem + stage * C::STAGE_BYTES;
-          const uint32_t aA0 = smem_u32(st), aA1 = smem_u32(st + C::A_BYTES);
+          const uint32_t aA = smem_u32(st + half * C::A_BYTES);
           const uint32_t aB = smem_u32(st + NUM_A * C::A_BYTES);
-          const uint32_t aSFA = aB + C::B_BYTES;
-          const uint32_t aSFB = aSFA + NUM_A * C::SF_BYTES;
-          tc_cp_sf(sfa0, desc_sf(aSFA));
-          if (NUM_A == 2) tc_cp_sf(sfa1, desc_sf(aSFA + C::SF_BYTES));
+          const uint32_t aSFA = aB + C::B_BYTES + half * C::SF_BYTES;
+          const uint32_t aSFB = aB + C::B_BYTES + NUM_A * C::SF_BYTES;
+          tc_cp_sf(sfa, desc_sf(aSFA));
           tc_cp_sf(sfb, desc_sf(aSFB));
-          const uint64_t dA0 = desc_sw128(aA0), dA1 = desc_sw128(aA1), dB = desc_sw128(aB);
+          const uint64_t dA = desc_sw128(aA), dB = desc_sw128(aB);
 #pragma unroll
           for (int kb = 0; kb < G_BK / 32; ++kb) {
             const uint32_t idesc = idesc_mxf8f6f4(nb, B_FP4, (uint32_t)kb);
             const uint32_t sel = (uint32_t)kb << 30;
             const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
             // +32 bytes of K per step inside the 128-byte swizzle row
-            tc_mma_mxf8f6f4(d0, dA0 + 2u * kb, dB + 2u * kb, idesc, acc, sfa0 | sel, sfb | sel);
-            if (NUM_A == 2) tc_mma_mxf8f6f4(d1, dA1 + 2u * kb, dB + 2u * kb, idesc, acc, sfa1 | sel, sfb | sel);
+            tc_mma_mxf8f6f4(d, dA + 2u * kb, dB + 2u * kb, idesc, acc, sfa | sel, sfb | sel);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -322,7 +317,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + G_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     constexpr int HALF = G_BN / 2;     // columns per epilogue warp
     const int q = warp & 3;            // TMEM lane quarter of this warp

@@ -407,7 +407,6 @@ struct dsv4_moe_plan {
   CUtensorMap tmA13, tmA2;
   CUtensorMap tmB1_fp8[3], tmB1_fp4[3], tmB2_fp8[3], tmB2_fp4[3];  // 16, 32, 64 activation rows per box
   bool timing = false;
-  int pf_dist = 0;  // L2 prefetch distance of the weight tiles, in k-tiles (0: off)
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -466,7 +465,6 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   p->slot = slot_layout(hidden, inter);
   p->ws = (uint8_t*)workspace;
   p->wl = wl;
-  if (const char* e = getenv("DSV4_L2_PREFETCH")) p->pf_dist = atoi(e);
   DSV4_CUDA_CHECK(cudaMemset(workspace, 0, (size_t)wl.bytes));
   const uint64_t H = hidden, I = inter, SB = (uint64_t)p->slot.bytes, PC = (uint64_t)wl.p_cap;
   const CUtensorMapDataType U4 = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -563,7 +561,6 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g1.k_tiles = p->H / 128;
   g1.a_row_tiles = p->I / 128;   // one (w1, w3) tile pair per work tile
   g1.out_tile_cols = 128;
-  g1.pf_dist = p->pf_dist;
   g1.b_sf = p->ws + w.xsf;
   g1.rb_cap = rb_cap;
   g1.chunks = wsp<int4>(p, w.chunks);
