@@ -52,6 +52,44 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
   return excl;
 }
 
+// Exclusive scan of three values over the block (all AL_THREADS threads
+// call it); scratch: 96 ints.  Two barriers; the caller separates the next
+// use of scratch by another barrier.
+__device__ __forceinline__ int3 block_scan3(int a, int b, int c, int* scratch, int3* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int xa = a, xb = b, xc = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ya = __shfl_up_sync(0xffffffffu, xa, o);
+    const int yb = __shfl_up_sync(0xffffffffu, xb, o);
+    const int yc = __shfl_up_sync(0xffffffffu, xc, o);
+    if (lane >= o) {
+      xa += ya;
+      xb += yb;
+      xc += yc;
+    }
+  }
+  if (lane == 31) {
+    scratch[warp] = xa;
+    scratch[32 + warp] = xb;
+    scratch[64 + warp] = xc;
+  }
+  __syncthreads();
+  if (warp < 3) {
+    int v = scratch[32 * warp + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    scratch[32 * warp + lane] = v;
+  }
+  __syncthreads();
+  *total = make_int3(scratch[31], scratch[63], scratch[95]);
+  return make_int3(xa - a + (warp > 0 ? scratch[warp - 1] : 0), xb - b + (warp > 0 ? scratch[31 + warp] : 0),
+                   xc - c + (warp > 0 ? scratch[63 + warp] : 0));
+}
+
 __global__ void __launch_bounds__(AL_THREADS, 1)
     moe_align_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, const float* __restrict__ w_flat,
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
@@ -63,12 +101,84 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   int* run = cnt + E;            // E
   int* tot = run + E;            // E
   int* scratch = tot + E;        // 32
-  int* sidx = scratch + 32;      // AL_THREADS (decode-sized batches)
+  int* sidx = scratch + 32;      // AL_THREADS ints: scan scratch of the one-pass path
   uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool small = P <= AL_THREADS;
   griddep_wait();
   griddep_launch();
+
+  if (small) {
+    // Decode-sized batch, one assignment per thread, five barriers: the
+    // stable rank of assignment p in its expert is its rank among equal
+    // experts of its warp (match) plus the count of that expert in the
+    // warps before it (exclusive prefix over the per-warp count table).
+    uint32_t* wc32 = reinterpret_cast<uint32_t*>(wc);
+    for (int j = tid; j < 16 * E; j += AL_THREADS) wc32[j] = 0u;
+    int e = -1;
+    float wv = 0.f;
+    if (tid < P) {
+      e = idx[tid];
+      if (e < 0 || e >= E) {
+        set_status(status, DSV4_EINVAL);
+        inv[tid] = -1;
+        e = -1;
+      } else if (sorted_w) {
+        wv = w_flat[tid];
+      }
+    }
+    __syncthreads();
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wc[warp * E + e] = (uint16_t)__popc(same);
+    __syncthreads();
+    int c = 0;
+    if (tid < E) {
+      uint16_t v[32];
+#pragma unroll
+      for (int w = 0; w < 32; ++w) v[w] = wc[w * E + tid];
+#pragma unroll
+      for (int w = 0; w < 32; ++w) {
+        wc[w * E + tid] = (uint16_t)c;
+        c += v[w];
+      }
+    }
+    const int cpad = (c + pad - 1) / pad * pad;
+    const int nch = cpad / pad;
+    int3 tot3;
+    const int3 ex = block_scan3(cpad, c > 0 ? 1 : 0, nch, sidx, &tot3);
+    if (tid < E) {
+      run[tid] = ex.x;   // start row of the group
+      cnt[tid] = c;
+      counts[tid] = c;
+      offsets[tid] = ex.x;
+      if (c > 0) active[ex.y] = tid;
+      if (chunks)
+        for (int j = 0; j < nch; ++j) chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), 0);
+    }
+    if (tid == 0) {
+      offsets[E] = tot3.x;
+      *n_active = tot3.y;
+      if (chunks) *n_chunks = tot3.z;
+    }
+    __syncthreads();
+    if (e >= 0) {
+      const int pos = run[e] + wc[warp * E + e] + rank;
+      sorted_flat[pos] = tid;
+      inv[tid] = pos;
+      if (sorted_w) sorted_w[pos] = wv;
+    }
+    // padding rows of each group (fewer than `pad`), one warp per group so
+    // the stores of a warp are contiguous
+    for (int g = warp; g < E; g += AL_THREADS / 32) {
+      const int r0 = run[g] + cnt[g], r1 = run[g] + (cnt[g] + pad - 1) / pad * pad;
+      for (int r = r0 + lane; r < r1; r += 32) {
+        sorted_flat[r] = -1;
+        if (sorted_w) sorted_w[r] = 0.f;
+      }
+    }
+    return;
+  }
 
   for (int e = tid; e < E; e += AL_THREADS) cnt[e] = 0;
   __syncthreads();
@@ -81,7 +191,6 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     } else {
       atomicAdd(&cnt[e], 1);
     }
-    if (small) sidx[p] = e;
   }
   __syncthreads();
   // exclusive scan of the (padded) group sizes (E <= 1024: one expert per thread)
@@ -91,33 +200,23 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   const int off = block_exclusive_scan(cpad, scratch, &total);
   if (tid < E) {
     run[tid] = off;
+    tot[tid] = off + c;   // first padding row of the group
     counts[tid] = c;
     offsets[tid] = off;
-    for (int r = off + c; r < off + cpad; ++r) {
+  }
+  if (tid == 0) offsets[E] = total;
+  __syncthreads();
+  // padding rows of each group (fewer than `pad`), one warp per group so the
+  // stores of a warp are contiguous
+  for (int e = warp; e < E; e += AL_THREADS / 32) {
+    const int r0 = tot[e], r1 = run[e] + (cnt[e] + pad - 1) / pad * pad;
+    for (int r = r0 + lane; r < r1; r += 32) {
       sorted_flat[r] = -1;
       if (sorted_w) sorted_w[r] = 0.f;
     }
   }
-  if (tid == 0) offsets[E] = total;
-  __syncthreads();
 
-  if (small) {
-    // decode-sized batch: the stable rank of assignment p inside its expert
-    // is the number of earlier assignments with the same expert
-    if (tid < P) {
-      const int e = sidx[tid];
-      if (e >= 0) {
-        int rank = 0;
-        for (int q = 0; q < tid; ++q) rank += (sidx[q] == e) ? 1 : 0;
-        const int pos = run[e] + rank;
-        sorted_flat[pos] = tid;
-        inv[tid] = pos;
-        if (sorted_w) sorted_w[pos] = w_flat[tid];
-      }
-    }
-    __syncthreads();
-  }
-  for (int base = 0; !small && base < P; base += AL_THREADS) {
+  for (int base = 0; base < P; base += AL_THREADS) {
     for (int j = tid; j < 32 * E; j += AL_THREADS) wc[j] = 0;
     __syncthreads();
     const int p = base + tid;

@@ -1,9 +1,9 @@
 // Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
-//   phase 1: fp32 logits = float(x) @ gate_w^T, gate rows staged in shared
-//            memory, one warp per dot product (deterministic);
-//   phase 2: one warp per token: score function,
-//            biased top-k (or hash table), unbiased weights, renormalise,
-//            scale.
+//   phase 1: fp32 partial logits, split over 128-wide slices of H:
+//            part[s, t, e] = sum over slice s of float(x[t, k]) * w[e, k];
+//   phase 2: one CTA per token: add the slices in order (deterministic),
+//            then one warp applies the score function, the biased top-k (or
+//            the hash table), the unbiased weights, renormalisation, scale.
 #include <mutex>
 #include <string>
 
@@ -13,65 +13,106 @@
 namespace dsv4 {
 
 constexpr int RT_MAX_E = 256;
-constexpr int RT_EPB = 8;      // experts per CTA (one warp each)
-constexpr int RT_TT = 64;      // tokens per CTA (two per lane)
-constexpr int RT_KC = 64;      // K elements per shared-memory tile
-constexpr int RT_SPLIT = 16;   // split of H on the workspace path; partials summed in order by the top-k kernel
-constexpr int RT_SPLIT_NOALLOC = 4;  // split on the fixed-scratch path
+constexpr int RL_TOK = 64;    // tokens per CTA
+constexpr int RL_EXP = 64;    // experts per CTA
+constexpr int RL_KC = 64;     // K elements per shared-memory chunk
+constexpr int RL_SLICE = 128; // K elements per CTA on the workspace path (one partial per 128 of H)
+constexpr int RT_SPLIT_NOALLOC = 4;  // slices of H on the fixed-scratch path
 
-// partial[c, t, e] = sum over H-chunk c of float(x[t, h]) * w[e, h].  Tiles of
-// 64 tokens x 64 h (bf16 -> f32, padded rows) and 8 gate rows x 64 h are
-// staged in shared memory; warp w owns expert e0 + w, lane owns tokens lane
-// and lane + 32.  One writer per partial: deterministic.
+// One CTA: 64 tokens x 64 experts over kslice elements of H (a multiple of
+// 64).  Each 64-wide chunk is staged transposed in shared memory (xs[k][t],
+// ws[k][e], conflict-free stores); thread (tq, eq) accumulates tokens
+// 4tq..4tq+3 against experts 4eq..4eq+3, two 16-byte loads per 16 FMAs.  The
+// next chunk's global loads are issued before the current chunk is computed.
+// One writer per partial: deterministic.
 __global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __restrict__ x,
                                                            const float* __restrict__ w, float* __restrict__ part,
-                                                           int64_t T, int H, int E, int split) {
-  __shared__ float xs[RT_TT][RT_KC + 1];
-  __shared__ float ws[RT_EPB][RT_KC];
+                                                           int64_t T, int H, int E, int kslice) {
+  __shared__ __align__(16) float xs[RL_KC][RL_TOK];
+  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
   griddep_wait();
   griddep_launch();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * RT_EPB;
-  const int chunk = blockIdx.y;
-  const int64_t t0 = (int64_t)blockIdx.z * RT_TT;
-  const int kc = H / split;
-  const int kbeg = chunk * kc;
-  float a0 = 0.f, a1 = 0.f;
-  for (int k0 = kbeg; k0 < kbeg + kc; k0 += RT_KC) {
-    for (int i = threadIdx.x; i < RT_TT * RT_KC / 2; i += 256) {
-      const int r = i / (RT_KC / 2), c = (i % (RT_KC / 2)) * 2;
-      float lo = 0.f, hi = 0.f;
-      if (t0 + r < T) {
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(x + (t0 + r) * H + k0 + c);
-        lo = bf16_from_bits(v & 0xffffu);
-        hi = bf16_from_bits(v >> 16);
+  const int tid = threadIdx.x;
+  const int e0 = blockIdx.x * RL_EXP;
+  const int slice = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.z * RL_TOK;
+  const int kbeg = slice * kslice;
+  // chunk staging in registers, row index fastest across lanes so the
+  // transposed shared-memory stores of a warp hit consecutive banks
+  uint4 xr[2];
+  float4 wr[4];
+  auto load = [&](int kc) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = tid + 256 * j, t = i & (RL_TOK - 1), c = (i >> 6) * 8;
+      xr[j] = t0 + t < T ? *reinterpret_cast<const uint4*>(x + (t0 + t) * H + kc + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j, e = i & (RL_EXP - 1), c = (i >> 6) * 4;
+      wr[j] = e0 + e < E ? *reinterpret_cast<const float4*>(w + (int64_t)(e0 + e) * H + kc + c)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  load(kbeg);
+  const int tq = tid & 15, eq = tid >> 4;
+  float acc[4][4] = {};
+  for (int kc = kbeg; kc < kbeg + kslice; kc += RL_KC) {
+    __syncthreads();   // the previous chunk has been consumed
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = tid + 256 * j, t = i & (RL_TOK - 1), c = (i >> 6) * 8;
+      const uint32_t v[4] = {xr[j].x, xr[j].y, xr[j].z, xr[j].w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        xs[c + 2 * m][t] = bf16_from_bits(v[m] & 0xffffu);
+        xs[c + 2 * m + 1][t] = bf16_from_bits(v[m] >> 16);
       }
-      xs[r][c] = lo;
-      xs[r][c + 1] = hi;
     }
-    for (int i = threadIdx.x; i < RT_EPB * RT_KC; i += 256) {
-      const int r = i / RT_KC, c = i % RT_KC;
-      ws[r][c] = (e0 + r < E) ? w[(int64_t)(e0 + r) * H + k0 + c] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll 16
-    for (int k = 0; k < RT_KC; ++k) {
-      const float g = ws[warp][k];
-      a0 = fmaf(xs[lane][k], g, a0);
-      a1 = fmaf(xs[lane + 32][k], g, a1);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j, e = i & (RL_EXP - 1), c = (i >> 6) * 4;
+      ws[c][e] = wr[j].x;
+      ws[c + 1][e] = wr[j].y;
+      ws[c + 2][e] = wr[j].z;
+      ws[c + 3][e] = wr[j].w;
     }
     __syncthreads();
+    if (kc + RL_KC < kbeg + kslice) load(kc + RL_KC);
+#pragma unroll 8
+    for (int k = 0; k < RL_KC; ++k) {
+      const float4 xv = *reinterpret_cast<const float4*>(&xs[k][4 * tq]);
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * eq]);
+      const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(xa[a], wa[b], acc[a][b]);
+    }
   }
-  const int e = e0 + warp;
-  if (e < E) {
-    float* dst = part + (int64_t)chunk * T * E;
-    if (t0 + lane < T) dst[(t0 + lane) * E + e] = a0;
-    if (t0 + lane + 32 < T) dst[(t0 + lane + 32) * E + e] = a1;
+  float* dst = part + (int64_t)slice * T * E;
+  const int e = e0 + 4 * eq;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int64_t t = t0 + 4 * tq + a;
+    if (t >= T) break;
+    if (e + 3 < E && (E & 3) == 0) {   // 16-byte aligned quads
+      *reinterpret_cast<float4*>(dst + t * E + e) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    } else {
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        if (e + b < E) dst[t * E + e + b] = acc[a][b];
+    }
   }
 }
 
 __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log1pf(expf(v)); }
 
+// One CTA (256 threads) per token.  Thread e adds the slices of logit
+// (t, e) in slice order and applies the score function; warp 0 then takes
+// the biased top-k (ties to the lower expert id, as torch.topk on the
+// reference's CPU path), or reads the hash table, and writes the unbiased
+// weights, renormalised and scaled.
 __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int split, int64_t T,
                                                          int E, int K, int score_func, int renorm, float scale,
                                                          const float* __restrict__ bias,
@@ -79,57 +120,59 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
                                                          const int64_t* __restrict__ ids, float* __restrict__ w_out,
                                                          int32_t* __restrict__ i_out) {
   constexpr int PER = RT_MAX_E / 32;
+  __shared__ float sc_s[RT_MAX_E], ch_s[RT_MAX_E];
+  __shared__ float red[2][8];
   griddep_wait();
   griddep_launch();
-  const int lane = threadIdx.x & 31;
-  const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  if (t >= T) return;
-  float sc[PER], ch[PER];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e = tid;
+  float l = -INFINITY;
+  if (e < E) {
+    const float* src = logits + t * E + e;
+    const int64_t stride = T * E;
+    l = 0.f;
+    for (int s0 = 0; s0 < split; s0 += 32) {
+      float v[32];
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int e = lane + 32 * j;
-    float l = 0.f;
-    if (e < E) {
-      // partial sums of the H chunks, loaded together, added in chunk order
-      float v[RT_SPLIT];
+      for (int u = 0; u < 32; ++u) v[u] = s0 + u < split ? src[(s0 + u) * stride] : 0.f;
 #pragma unroll
-      for (int c = 0; c < RT_SPLIT; ++c) v[c] = c < split ? logits[((int64_t)c * T + t) * E + e] : 0.f;
-#pragma unroll
-      for (int c = 0; c < RT_SPLIT; ++c)
-        if (c < split) l += v[c];
+      for (int u = 0; u < 32; ++u)
+        if (s0 + u < split) l += v[u];
     }
-    sc[j] = (e < E) ? l : -INFINITY;
   }
+  float sc;
   if (score_func == DSV4_SCORE_SOFTMAX) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) m = fmaxf(m, sc[j]);
+    float m = l;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
+    if (lane == 0) red[0][warp] = m;
+    __syncthreads();
+    m = red[0][0];
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[0][i]);
+    const float ex = e < E ? expf(l - m) : 0.f;
+    float sum = ex;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      sc[j] = (lane + 32 * j < E) ? expf(sc[j] - m) : 0.f;
-      s += sc[j];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-#pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = sc[j] / s;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[1][warp] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int i = 0; i < 8; ++i) sum += red[1][i];
+    sc = ex / sum;
   } else if (score_func == DSV4_SCORE_SIGMOID) {
-#pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = 1.f / (1.f + expf(-sc[j]));
+    sc = 1.f / (1.f + expf(-l));
   } else {
-#pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = sqrtf(softplus_f(sc[j]));
+    sc = sqrtf(softplus_f(l));
   }
+  sc_s[e] = sc;
+  ch_s[e] = e < E ? (bias ? sc + bias[e] : sc) : -INFINITY;
+  __syncthreads();
+  if (warp != 0) return;
+  float ch[PER];
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int e = lane + 32 * j;
-    ch[j] = (e < E) ? (bias ? sc[j] + bias[e] : sc[j]) : -INFINITY;
-  }
-  float wsel[16];
-  int isel[16];
+  for (int j = 0; j < PER; ++j) ch[j] = ch_s[lane + 32 * j];
+  float wsel = 0.f;   // lane r keeps pick r
+  int isel = 0;
   for (int r = 0; r < K; ++r) {
     int pick;
     if (tid2eid) {
@@ -139,10 +182,10 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
       int bi = 0x7fffffff;
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E && (ch[j] > bv || (ch[j] == bv && e < bi))) {
+        const int ej = lane + 32 * j;
+        if (ej < E && (ch[j] > bv || (ch[j] == bv && ej < bi))) {
           bv = ch[j];
-          bi = e;
+          bi = ej;
         }
       }
 #pragma unroll
@@ -161,23 +204,18 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
           if (j == (pick >> 5)) ch[j] = -INFINITY;
       }
     }
-    // unbiased score of the pick lives in lane pick%32, slot pick/32
-    float v = 0.f;
-#pragma unroll
-    for (int j = 0; j < PER; ++j)
-      if (j == (pick >> 5)) v = sc[j];
-    v = __shfl_sync(0xffffffffu, v, pick & 31);
-    wsel[r] = v;
-    isel[r] = pick;
-  }
-  if (lane == 0) {
-    float s = 0.f;
-    for (int r = 0; r < K; ++r) s += wsel[r];
-    for (int r = 0; r < K; ++r) {
-      float v = renorm ? wsel[r] / s : wsel[r];
-      w_out[t * K + r] = v * scale;
-      i_out[t * K + r] = isel[r];
+    if (lane == r) {
+      wsel = (pick >= 0 && pick < E) ? sc_s[pick] : 0.f;   // unbiased score of the pick
+      isel = pick;
     }
+  }
+  // renormalise over the K picks in pick order (lane 0 adds them up)
+  float ssum = 0.f;
+  for (int r = 0; r < K; ++r) ssum += __shfl_sync(0xffffffffu, wsel, r);
+  if (lane < K) {
+    const float v = renorm ? wsel / ssum : wsel;
+    w_out[t * K + lane] = v * scale;
+    i_out[t * K + lane] = isel;
   }
 }
 
@@ -187,7 +225,7 @@ using namespace dsv4;
 
 extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts) {
   if (n_tokens < 0 || hidden <= 0 || n_experts <= 0) return DSV4_EINVAL;
-  return RT_SPLIT * n_tokens * n_experts * (int64_t)sizeof(float);
+  return (int64_t)(hidden / RL_SLICE) * n_tokens * n_experts * (int64_t)sizeof(float);
 }
 
 extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
@@ -197,7 +235,7 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
                                void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out && workspace, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && hidden % (RT_SPLIT * RT_KC) == 0, "hidden must be a positive multiple of 1024");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % 1024 == 0, "hidden must be a positive multiple of 1024");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
@@ -207,13 +245,13 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   if (n_tokens == 0) return DSV4_OK;
   if (int rc = bind_device_of(x_bf16, nullptr)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const dim3 grid((n_experts + RT_EPB - 1) / RT_EPB, RT_SPLIT, (unsigned)((n_tokens + RT_TT - 1) / RT_TT));
+  const int split = hidden / RL_SLICE;
+  const dim3 grid((n_experts + RL_EXP - 1) / RL_EXP, split, (unsigned)((n_tokens + RL_TOK - 1) / RL_TOK));
   const bool pdl = pdl_enabled();
   DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
-                           (float*)workspace, n_tokens, hidden, n_experts, RT_SPLIT));
-  const int64_t threads = n_tokens * 32;
-  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, pdl,
-                           (const float*)workspace, RT_SPLIT, n_tokens, n_experts, topk, score_func, renormalize,
+                           (float*)workspace, n_tokens, hidden, n_experts, (int)RL_SLICE));
+  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl,
+                           (const float*)workspace, split, n_tokens, n_experts, topk, score_func, renormalize,
                            route_scale, bias, tid2eid, input_ids, weights_out, indices_out));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
@@ -255,7 +293,7 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
                                        int32_t* indices_out, void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out, "null pointer");
-  DSV4_CHECK_ARG(hidden > 0 && hidden % (RT_SPLIT * RT_KC) == 0, "hidden must be a positive multiple of 1024");
+  DSV4_CHECK_ARG(hidden > 0 && hidden % 1024 == 0, "hidden must be a positive multiple of 1024");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
@@ -280,11 +318,10 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
     scratch = g_noalloc_ptr[dev];
   }
   cudaStream_t st = (cudaStream_t)stream;
-  const dim3 grid((n_experts + RT_EPB - 1) / RT_EPB, RT_SPLIT_NOALLOC, (unsigned)((n_tokens + RT_TT - 1) / RT_TT));
+  const dim3 grid((n_experts + RL_EXP - 1) / RL_EXP, RT_SPLIT_NOALLOC, (unsigned)((n_tokens + RL_TOK - 1) / RL_TOK));
   route_logits_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x_bf16, gate_w, scratch, n_tokens, hidden, n_experts,
-                                            RT_SPLIT_NOALLOC);
-  const int64_t threads = n_tokens * 32;
-  route_topk_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+                                            hidden / RT_SPLIT_NOALLOC);
+  route_topk_kernel<<<(unsigned)n_tokens, 256, 0, st>>>(
       scratch, RT_SPLIT_NOALLOC, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
       weights_out, indices_out);
   DSV4_CUDA_CHECK(cudaGetLastError());
