@@ -156,6 +156,22 @@ class ExpertBank:
         if key in self._lru:        # stale device copy
             self.invalidate()
 
+    def register_packed(self, layer, eid, slot: torch.Tensor):
+        """Store an expert that is already in the packed slot layout (for
+        example a slot written earlier by ``host_slot``), without repacking."""
+        if self.hidden is None:
+            raise RuntimeError("register_packed needs hidden/inter (pass them to the constructor)")
+        if slot.dtype != torch.uint8 or slot.numel() != self.slot_bytes:
+            raise ValueError(f"a packed slot is {self.slot_bytes} uint8 bytes")
+        key = (int(layer), int(eid))
+        dst = self._host.get(key)
+        if dst is None:
+            dst = self._new_host_slot()
+        dst.copy_(slot.reshape(-1))
+        self._host[key] = dst
+        if key in self._lru:
+            self.invalidate()
+
     def has(self, layer, eid):
         return (int(layer), int(eid)) in self._host
 
@@ -229,6 +245,21 @@ class ExpertBank:
         t = torch.tensor([self._lru.od[k] for k in keys], dtype=torch.int32).to(self.device)
         self._tables[layer] = (epoch, t)
         return t
+
+    def resize_slots(self, packed_capacity: int):
+        """Change the HBM budget to ``packed_capacity`` slots.  Drops every
+        resident expert (the host pool stays) and waits for the kernels
+        that read the old arena."""
+        self._need_cuda()
+        torch.cuda.synchronize(self.device)
+        self._arena = None
+        self.packed_capacity = int(packed_capacity)
+        self._lru = SlotLRU(self.packed_capacity)
+        self._slot_events.clear()
+        self._all_event = None
+        self._tables.clear()
+        self._epoch += 1
+        self.h2d_bytes = self.h2d_copies = 0
 
     def mark_used(self, slots, stream=None):
         """Record that kernels enqueued so far on ``stream`` read ``slots``

@@ -83,6 +83,11 @@ class ExpertOffloadEngine:
             self._plans[key] = plan
         return plan
 
+    def resize_slots(self, packed_capacity: int):
+        """New HBM budget of packed slots; plans bound to the old arena are dropped."""
+        self.bank.resize_slots(packed_capacity)
+        self._plans.clear()
+
     def stats(self):
         s = self.bank.stats()
         s["captured"] = self.captured
