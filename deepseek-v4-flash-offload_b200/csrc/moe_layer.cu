@@ -282,53 +282,58 @@ __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, i
   return ((int64_t)kt * rb_cap + row / 64) * 512 + (row % 32) * 16 + ((row % 64) / 32) * 4;
 }
 
+// One warp per (token, 128-column block): the token's row is read and
+// quantised once, then written to the sorted rows of its topk assignments
+// (inv[t*topk + j]), 4 bytes per lane per row; lanes 0..topk-1 store the
+// rows' scale words.
 __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                        int64_t n_assign, int topk, int K, int64_t rb_cap,
+                                        int64_t n_tokens, int topk, int K, int64_t rb_cap,
                                         uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   griddep_wait();
   griddep_launch();
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
-  const int64_t nblk = n_assign * kblk;
+  const int64_t ntask = n_tokens * kblk;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t b = warp0; b < nblk; b += nwarps) {
-    const int64_t asg = b / kblk;          // flat assignment t*topk + j
-    const int kb = (int)(b - asg * kblk);
-    const int64_t p = inv[asg];            // its (padded) sorted row
-    if (p < 0) continue;
-    const int64_t tok = asg / topk;
+  for (int64_t b = warp0; b < ntask; b += nwarps) {
+    const int64_t tok = b / kblk;
+    const int kb = (int)(b - tok * kblk);
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
     float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     a = warp_max_f(a);
     const int e = fp8_scale_exp(a);
-    const float inv = pow2i(-e);
+    const float inv_s = pow2i(-e);
     uint32_t o = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv, -448.f), 448.f)) << (8 * i);
-    *reinterpret_cast<uint32_t*>(q + p * K + kb * 128 + lane * 4) = o;
-    if (lane == 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(p, kb, rb_cap)) = (uint32_t)(e + 127) * 0x01010101u;
+    for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv_s, -448.f), 448.f)) << (8 * i);
+    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
+    for (int j = 0; j < topk; ++j) {
+      const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
+      if (row >= 0) *reinterpret_cast<uint32_t*>(q + row * K + kb * 128 + lane * 4) = o;
+    }
+    if (my_row >= 0)
+      *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap)) = (uint32_t)(e + 127) * 0x01010101u;
   }
 }
 
+// MXFP4 (a4w4): per 32 columns an E8M0 scale floor(log2(amax/6)) + 127 and
+// E2M1 codes, round to nearest even, saturating; lanes 8g..8g+7 own block g.
 __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                          int64_t n_assign, int topk, int K, int64_t rb_cap,
+                                          int64_t n_tokens, int topk, int K, int64_t rb_cap,
                                           uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   griddep_wait();
   griddep_launch();
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
-  const int64_t nblk = n_assign * kblk;
+  const int64_t ntask = n_tokens * kblk;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t b = warp0; b < nblk; b += nwarps) {
-    const int64_t asg = b / kblk;          // flat assignment t*topk + j
-    const int kb = (int)(b - asg * kblk);
-    const int64_t p = inv[asg];            // its (padded) sorted row
-    if (p < 0) continue;
-    const int64_t tok = asg / topk;
+  for (int64_t b = warp0; b < ntask; b += nwarps) {
+    const int64_t tok = b / kblk;
+    const int kb = (int)(b - tok * kblk);
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -336,11 +341,20 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
 #pragma unroll
     for (int o = 4; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     const int e = mx_scale_exp(a);
-    const float inv = pow2_any(-e);
-    const uint32_t packed = e2m1_code(v[0] * inv) | (e2m1_code(v[1] * inv) << 4) | (e2m1_code(v[2] * inv) << 8) |
-                            (e2m1_code(v[3] * inv) << 12);
-    *reinterpret_cast<uint16_t*>(q + p * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
-    if ((lane & 7) == 0) sf[act_sf_offset(p, kb, rb_cap) + (lane >> 3)] = (uint8_t)(e + 127);
+    const float inv_s = pow2_any(-e);
+    const uint32_t packed = e2m1_code(v[0] * inv_s) | (e2m1_code(v[1] * inv_s) << 4) |
+                            (e2m1_code(v[2] * inv_s) << 8) | (e2m1_code(v[3] * inv_s) << 12);
+    // the four block scales of this 128-column block as one word
+    const uint32_t sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
+                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
+                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
+                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
+    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
+    for (int j = 0; j < topk; ++j) {
+      const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
+      if (row >= 0) *reinterpret_cast<uint16_t*>(q + row * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
+    }
+    if (my_row >= 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap)) = sword;
   }
 }
 
@@ -645,11 +659,11 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
   const int64_t rb_cap = w.p_cap / G_BN;
   {
-    const int64_t warps = (int64_t)P * (p->H / 128);
+    const int64_t warps = n_tokens * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
     DSV4_CUDA_CHECK(launch_k(fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
-                             dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, (int64_t)P,
+                             dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, n_tokens,
                              p->topk, p->H, rb_cap, p->ws + w.xq, p->ws + w.xsf));
   }
   mark(2);
