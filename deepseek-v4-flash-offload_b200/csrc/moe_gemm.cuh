@@ -42,7 +42,7 @@
 namespace dsv4 {
 
 constexpr int G_BM = 128;
-constexpr int G_BN = 64;
+constexpr int G_BN = 64;    // decode tile: up to 64 tokens of one expert
 constexpr int G_BK = 128;
 constexpr int G_EPI_WARPS = 8;
 constexpr int G_MMA2_WARP = 2 + G_EPI_WARPS;   // MMA issuer of weight rows 128-255
@@ -52,17 +52,24 @@ constexpr uint32_t G_SF_COL = 256;   // TMEM columns 256..271: A and B scales of
 
 enum : int { EPI_SWIGLU_FP8 = 0, EPI_SWIGLU_MXFP4 = 1, EPI_STORE_BF16 = 2 };
 
-template <int NUM_A>
+// BN = tokens per tile: 64 (decode) or 128 (prefill: twice the work per
+// MMA instruction, whose issue cost does not grow with N up to 128).  With
+// BN = 128 the accumulators (2 halves x 128 columns) fill half of TMEM, so
+// they are single-buffered and the ring has 4 stages.
+template <int NUM_A, int BN = G_BN>
 struct GemmCfg {
+  static_assert(BN == 64 || BN == 128, "tile of 64 or 128 tokens");
   static constexpr int A_BYTES = G_BM * G_BK;  // 16 KB (E2M1 expanded to 1 B / element)
-  static constexpr int B_BYTES = G_BN * G_BK;  // 8 KB
+  static constexpr int B_BYTES = BN * G_BK;    // 8 or 16 KB
   static constexpr int SF_BYTES = 512;
   static constexpr int STAGE_RAW = NUM_A * A_BYTES + B_BYTES + (NUM_A + 1) * SF_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int STAGES = 5;
+  static constexpr int STAGES = BN == 64 ? 5 : 4;
+  static constexpr int ACC_BUFS = BN == 64 ? 2 : 1;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * G_BN * 4 + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * BN * 4 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(ACC_BUFS * NUM_A * BN <= (int)G_SF_COL, "accumulators below the scale columns");
 };
 
 struct GemmParams {
@@ -72,8 +79,8 @@ struct GemmParams {
   int k_tiles;               // K / 128
   int a_row_tiles;           // tiles per chunk = 256-row weight pairs of the matrix
   int out_tile_cols;         // output columns per tile (128: gate/up pair, 256: down pair)
-  const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, 64-row block)
-  int64_t rb_cap;            // 64-row blocks per k-tile in b_sf / out_sf
+  const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, BN-row block)
+  int64_t rb_cap;            // BN-row blocks per k-tile in b_sf / out_sf
   const int4* chunks;        // {expert, row0, nrows, 0}
   const int* n_chunks;
   const int* slot_of;        // expert -> slot
@@ -125,16 +132,18 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
 }
 
 // Activation rows loaded per tile: the chunk's valid rows rounded up to 16,
-// 32 or 64 (decode chunks are mostly short); also the MMA N.
-__device__ __forceinline__ int b_rows_for(int nrows) { return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : 64); }
+// 32, 64 or 128 (decode chunks are mostly short); also the MMA N.
+__device__ __forceinline__ int b_rows_for(int nrows) {
+  return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : (nrows <= 64 ? 64 : 128));
+}
 
-template <int NUM_A, bool B_FP4, int EPI>
+template <int NUM_A, bool B_FP4, int EPI, int BN>
 __global__ void __launch_bounds__(G_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB16,
                     const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB128, const GemmParams p) {
   static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
-  using C = GemmCfg<NUM_A>;
+  using C = GemmCfg<NUM_A, BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -145,7 +154,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   int* epi_fail = reinterpret_cast<int*>(tmem_holder + 1);
-  float* red = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);  // [4][G_BN]
+  float* red = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);  // [4][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -154,7 +163,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);   // one commit from each MMA issuer
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::ACC_BUFS; ++b) {
       mbar_init(&accfull[b], 2);
       mbar_init(&accempty[b], G_EPI_WARPS);
     }
@@ -167,6 +176,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     prefetch_tensormap(&tmB16);
     prefetch_tensormap(&tmB32);
     prefetch_tensormap(&tmB64);
+    if (BN == 128) prefetch_tensormap(&tmB128);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, G_TMEM_COLS);
@@ -204,9 +214,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           continue;
         }
         const uint8_t* sf_base = p.arena + (int64_t)cur.slot * p.slot_bytes + p.sfa_off;
-        const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / G_BN) * C::SF_BYTES;
+        const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
         const int nb = b_rows_for(cur.nrows);
-        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : &tmB64);
+        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmB128));
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             ok = false;
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)abuf * (NUM_A * G_BN) + (uint32_t)half * G_BN;
+        const uint32_t d = tmem + (uint32_t)abuf * (NUM_A * BN) + (uint32_t)half * BN;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&full[stage], phase, p.status)) {
             ok = false;
@@ -305,7 +315,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         if (!ok) break;
         tc_commit(&accfull[abuf]);
-        if (++abuf == 2) {
+        if (++abuf == C::ACC_BUFS) {
           abuf = 0;
           aphase ^= 1u;
         }
@@ -319,13 +329,29 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     __syncwarp();
   } else if (warp < 2 + G_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
-    constexpr int HALF = G_BN / 2;     // columns per epilogue warp
+    constexpr int HALF = BN / 2;       // columns per epilogue warp
+    constexpr int SUB = 32;            // columns per pass (registers)
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int half = (warp - 2) >> 2;  // which half of the 64 columns
+    const int half = (warp - 2) >> 2;  // which half of the BN columns
     const int i = q * 32 + lane;       // row inside the 128-row tile
     const int c0 = half * HALF;        // first column of this warp
     int abuf = 0;
     uint32_t aphase = 0;
+    float w[SUB];
+    // route weights of 32 rows starting at cs (row0 + cs is a multiple of 32)
+    auto load_w = [&](int row0, int cs) {
+      if constexpr (EPI != EPI_STORE_BF16) {
+        const float4* wp = reinterpret_cast<const float4*>(p.sorted_w + row0 + cs);
+#pragma unroll
+        for (int j = 0; j < SUB / 4; ++j) {
+          const float4 v = wp[j];
+          w[4 * j] = v.x;
+          w[4 * j + 1] = v.y;
+          w[4 * j + 2] = v.z;
+          w[4 * j + 3] = v.w;
+        }
+      }
+    };
     TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
     for (int t = blockIdx.x; t < n_tiles; t += step) {
       const TileInfo nxt = load_tile(p, t + step, n_tiles);
@@ -335,116 +361,111 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       const int row0 = cur.row0, nrows = cur.nrows, mt = cur.mt;
       cur = nxt;
-      float w[HALF];
-      if constexpr (EPI != EPI_STORE_BF16) {
-        // route weights of this warp's 32 rows (row0 is a multiple of 64)
-        const float4* wp = reinterpret_cast<const float4*>(p.sorted_w + row0 + c0);
-#pragma unroll
-        for (int j = 0; j < HALF / 4; ++j) {
-          const float4 v = wp[j];
-          w[4 * j] = v.x;
-          w[4 * j + 1] = v.y;
-          w[4 * j + 2] = v.z;
-          w[4 * j + 3] = v.w;
-        }
-      }
+      load_w(row0, c0);
       // all epilogue warps take the same decision: a failed wait in any of
       // them ends the loop for all (the named barriers below need all 8)
       if (!mbar_wait(&accfull[abuf], aphase, p.status) && lane == 0) atomicOr(epi_fail, 1);
       named_bar_sync(1, 32 * G_EPI_WARPS);
       if (*reinterpret_cast<volatile int*>(epi_fail) != 0) break;
       tc_fence_after();
-      float acc0[HALF];
-      float acc1[NUM_A == 2 ? HALF : 1];
-      (void)acc1;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)abuf * (NUM_A * G_BN) + c0;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)abuf * (NUM_A * BN) + c0;
+#pragma unroll 1
+      for (int sub = 0; sub < HALF / SUB; ++sub) {
+        const int cs = c0 + sub * SUB;   // first column of this pass
+        if (sub > 0) load_w(row0, cs);
+        float acc0[SUB];
+        float acc1[NUM_A == 2 ? SUB : 1];
+        (void)acc1;
 #pragma unroll
-      for (int j = 0; j < HALF / 16; ++j) tmem_ld16(tbase + j * 16, acc0 + j * 16);
-      if constexpr (NUM_A == 2) {
+        for (int j = 0; j < SUB / 16; ++j) tmem_ld16(tbase + sub * SUB + j * 16, acc0 + j * 16);
+        if constexpr (NUM_A == 2) {
 #pragma unroll
-        for (int j = 0; j < HALF / 16; ++j) tmem_ld16(tbase + G_BN + j * 16, acc1 + j * 16);
+          for (int j = 0; j < SUB / 16; ++j) tmem_ld16(tbase + BN + sub * SUB + j * 16, acc1 + j * 16);
+        }
+        tc_wait_ld();
+        if (sub == HALF / SUB - 1) {   // this tile's accumulators are read out
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[abuf]);
+        }
+
+        if constexpr (EPI == EPI_STORE_BF16) {
+          // rows 0..127 of the pair -> acc0, rows 128..255 -> acc1
+          uint16_t* dst = p.out_bf16 + (int64_t)(row0 + cs) * p.out_ld + mt * p.out_tile_cols + i;
+#pragma unroll
+          for (int n = 0; n < SUB; ++n)
+            if (cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+          if constexpr (NUM_A == 2) {
+            uint16_t* dst1 = dst + G_BM;
+#pragma unroll
+            for (int n = 0; n < SUB; ++n)
+              if (cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+          }
+        } else {
+          // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
+          // bf16(h) is the input of the activation re-quantisation.
+          const float lim = p.swiglu_limit;
+#pragma unroll
+          for (int n = 0; n < SUB; ++n) {
+            float g = bf16r(acc0[n]);
+            float u = bf16r(acc1[n]);
+            if (lim > 0.f) {
+              u = fminf(fmaxf(u, -lim), lim);
+              g = fminf(g, lim);
+            }
+            acc0[n] = bf16r(silu_f(g) * u * w[n]);
+          }
+          if constexpr (EPI == EPI_SWIGLU_FP8) {
+            // per-token amax over the 128 rows of this tile = one 128-block of I:
+            // redux over the warp's 32 rows, then across the 4 lane quarters
+            float mine = 0.f;
+#pragma unroll
+            for (int n = 0; n < SUB; ++n) {
+              const float m = warp_max_nonneg(fabsf(acc0[n]));
+              if (lane == n) mine = m;
+            }
+            red[q * BN + cs + lane] = mine;
+            named_bar_sync(1, 32 * G_EPI_WARPS);
+            const float amax_l = fmaxf(fmaxf(red[cs + lane], red[BN + cs + lane]),
+                                       fmaxf(red[2 * BN + cs + lane], red[3 * BN + cs + lane]));
+            const int e_l = fp8_scale_exp(amax_l);
+            uint8_t* dst = p.out_q + (int64_t)(row0 + cs) * p.out_ld + mt * G_BM + i;
+#pragma unroll
+            for (int n = 0; n < SUB; ++n) {
+              const int e = __shfl_sync(0xffffffffu, e_l, n);
+              if (cs + n < nrows) {
+                const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
+                dst[(int64_t)n * p.out_ld] = (uint8_t)e4m3_byte(v);
+              }
+            }
+            if (q == 0 && cs + lane < nrows) {
+              const int n = cs + lane;
+              *reinterpret_cast<uint32_t*>(p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + (n & 31) * 16 +
+                                           (n >> 5) * 4) = (uint32_t)(e_l + 127) * 0x01010101u;
+            }
+            named_bar_sync(1, 32 * G_EPI_WARPS);
+          } else {
+            // per-token amax over the 32 rows of this warp = one 32-block of I
+            uint8_t* dst = p.out_q + (int64_t)(row0 + cs) * (p.out_ld / 2) + (mt * G_BM + i) / 2;
+            uint8_t* sfd = p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + q;
+#pragma unroll
+            for (int n = 0; n < SUB; ++n) {
+              if (cs + n < nrows) {
+                const float amax = warp_max_nonneg(fabsf(acc0[n]));
+                const int e = mx_scale_exp(amax);
+                const uint32_t code = e2m1_code(acc0[n] * pow2_any(-e));
+                const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
+                if ((lane & 1) == 0) dst[(int64_t)n * (p.out_ld / 2)] = (uint8_t)(code | (hi << 4));
+                const int cn = cs + n;
+                if (lane == 0) sfd[(cn & 31) * 16 + (cn >> 5) * 4] = (uint8_t)(e + 127);
+              }
+            }
+          }
+        }
       }
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[abuf]);
-      if (++abuf == 2) {
+      if (++abuf == C::ACC_BUFS) {
         abuf = 0;
         aphase ^= 1u;
-      }
-
-      if constexpr (EPI == EPI_STORE_BF16) {
-        // rows 0..127 of the pair -> acc0, rows 128..255 -> acc1
-        uint16_t* dst = p.out_bf16 + (int64_t)(row0 + c0) * p.out_ld + mt * p.out_tile_cols + i;
-#pragma unroll
-        for (int n = 0; n < HALF; ++n)
-          if (c0 + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
-        if constexpr (NUM_A == 2) {
-          uint16_t* dst1 = dst + G_BM;
-#pragma unroll
-          for (int n = 0; n < HALF; ++n)
-            if (c0 + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
-        }
-      } else {
-        // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
-        // bf16(h) is the input of the activation re-quantisation.
-        const float lim = p.swiglu_limit;
-#pragma unroll
-        for (int n = 0; n < HALF; ++n) {
-          float g = bf16r(acc0[n]);
-          float u = bf16r(acc1[n]);
-          if (lim > 0.f) {
-            u = fminf(fmaxf(u, -lim), lim);
-            g = fminf(g, lim);
-          }
-          acc0[n] = bf16r(silu_f(g) * u * w[n]);
-        }
-        if constexpr (EPI == EPI_SWIGLU_FP8) {
-          // per-token amax over the 128 rows of this tile = one 128-block of I:
-          // redux over the warp's 32 rows, then across the 4 lane quarters
-          float mine = 0.f;
-#pragma unroll
-          for (int n = 0; n < HALF; ++n) {
-            const float m = warp_max_nonneg(fabsf(acc0[n]));
-            if (lane == n) mine = m;
-          }
-          red[q * G_BN + c0 + lane] = mine;
-          named_bar_sync(1, 32 * G_EPI_WARPS);
-          const float amax_l = fmaxf(fmaxf(red[c0 + lane], red[G_BN + c0 + lane]),
-                                     fmaxf(red[2 * G_BN + c0 + lane], red[3 * G_BN + c0 + lane]));
-          const int e_l = fp8_scale_exp(amax_l);
-          uint8_t* dst = p.out_q + (int64_t)(row0 + c0) * p.out_ld + mt * G_BM + i;
-#pragma unroll
-          for (int n = 0; n < HALF; ++n) {
-            const int e = __shfl_sync(0xffffffffu, e_l, n);
-            if (c0 + n < nrows) {
-              const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
-              dst[(int64_t)n * p.out_ld] = (uint8_t)e4m3_byte(v);
-            }
-          }
-          if (q == 0 && c0 + lane < nrows) {
-            const int n = c0 + lane;
-            *reinterpret_cast<uint32_t*>(p.out_sf + ((int64_t)mt * p.rb_cap + row0 / G_BN) * 512 + (n & 31) * 16 +
-                                         (n >> 5) * 4) = (uint32_t)(e_l + 127) * 0x01010101u;
-          }
-          named_bar_sync(1, 32 * G_EPI_WARPS);
-        } else {
-          // per-token amax over the 32 rows of this warp = one 32-block of I
-          uint8_t* dst = p.out_q + (int64_t)(row0 + c0) * (p.out_ld / 2) + (mt * G_BM + i) / 2;
-          uint8_t* sfd = p.out_sf + ((int64_t)mt * p.rb_cap + row0 / G_BN) * 512 + q;
-#pragma unroll
-          for (int n = 0; n < HALF; ++n) {
-            if (c0 + n < nrows) {
-              const float amax = warp_max_nonneg(fabsf(acc0[n]));
-              const int e = mx_scale_exp(amax);
-              const uint32_t code = e2m1_code(acc0[n] * pow2_any(-e));
-              const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
-              if ((lane & 1) == 0) dst[(int64_t)n * (p.out_ld / 2)] = (uint8_t)(code | (hi << 4));
-              const int cn = c0 + n;
-              if (lane == 0) sfd[(cn & 31) * 16 + (cn >> 5) * 4] = (uint8_t)(e + 127);
-            }
-          }
-        }
       }
     }
   }

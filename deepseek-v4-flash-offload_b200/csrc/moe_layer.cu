@@ -24,6 +24,7 @@ namespace dsv4 {
 // and each chunk is one pad-row block of one expert.
 // ---------------------------------------------------------------------------
 constexpr int AL_THREADS = 1024;
+constexpr int GEMM_BN_MAX = 128;   // largest GEMM tile (tokens per expert chunk)
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
   // scratch: 32 ints.  All 1024 threads participate.
@@ -274,12 +275,13 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 // writes token t's row to its sorted row inv[a] (padding rows are never
 // touched; invalid assignments, inv < 0, are skipped).  Scales
 // go to 512-byte atoms, one per (128-column k-tile kt, 64-row block rb) at
-// (kt * rb_cap + rb) * 512, row n of the block at (n%32)*16 + (n/32)*4, one
+// (kt * rb_cap + rb) * 512 for BN-row blocks (BN = 64 or 128, the GEMM
+// tile), row n of the block at (n%32)*16 + (n/32)*4, one
 // byte per 32-block (FP8: the per-128 exponent replicated four times): the
 // order the tensor cores read after a 32x128b.warpx4 copy.
 // ---------------------------------------------------------------------------
-__host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, int64_t rb_cap) {
-  return ((int64_t)kt * rb_cap + row / 64) * 512 + (row % 32) * 16 + ((row % 64) / 32) * 4;
+__host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, int64_t rb_cap, int bn) {
+  return ((int64_t)kt * rb_cap + row / bn) * 512 + (row % 32) * 16 + ((row % bn) / 32) * 4;
 }
 
 // One warp per (token, 128-column block): the token's row is read and
@@ -287,7 +289,7 @@ __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, i
 // (inv[t*topk + j]), 4 bytes per lane per row; lanes 0..topk-1 store the
 // rows' scale words.
 __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                        int64_t n_tokens, int topk, int K, int64_t rb_cap,
+                                        int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
                                         uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   griddep_wait();
   griddep_launch();
@@ -315,14 +317,14 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
       if (row >= 0) *reinterpret_cast<uint32_t*>(q + row * K + kb * 128 + lane * 4) = o;
     }
     if (my_row >= 0)
-      *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap)) = (uint32_t)(e + 127) * 0x01010101u;
+      *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = (uint32_t)(e + 127) * 0x01010101u;
   }
 }
 
 // MXFP4 (a4w4): per 32 columns an E8M0 scale floor(log2(amax/6)) + 127 and
 // E2M1 codes, round to nearest even, saturating; lanes 8g..8g+7 own block g.
 __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                          int64_t n_tokens, int topk, int K, int64_t rb_cap,
+                                          int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
                                           uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
   griddep_wait();
   griddep_launch();
@@ -354,7 +356,7 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
       const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
       if (row >= 0) *reinterpret_cast<uint16_t*>(q + row * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
     }
-    if (my_row >= 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap)) = sword;
+    if (my_row >= 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = sword;
   }
 }
 
@@ -476,8 +478,10 @@ static int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
 static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens) {
   WsLayout w;
   w.p_max = max_tokens * topk;
-  // every expert group is padded to a multiple of G_BN rows
-  w.p_cap = (w.p_max + (G_BN - 1) * std::min<int64_t>(E, w.p_max) + G_BN - 1) / G_BN * G_BN + G_BN;
+  // every expert group is padded to a multiple of the GEMM tile (64 or 128
+  // rows): room for the larger padding
+  w.p_cap = (w.p_max + (GEMM_BN_MAX - 1) * std::min<int64_t>(E, w.p_max) + GEMM_BN_MAX - 1) / GEMM_BN_MAX *
+                GEMM_BN_MAX + GEMM_BN_MAX;
   w.max_chunks = w.p_cap / G_BN + 1;
   int64_t o = 0;
   auto take = [&](int64_t bytes) {
@@ -518,8 +522,9 @@ struct dsv4_moe_plan {
   uint8_t* ws = nullptr;
   dsv4::WsLayout wl;
   CUtensorMap tmA13, tmA2;
-  CUtensorMap tmB1_fp8[3], tmB1_fp4[3], tmB2_fp8[3], tmB2_fp4[3];  // 16, 32, 64 activation rows per box
+  CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 128 activation rows per box
   bool timing = false;
+  int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -544,9 +549,37 @@ extern "C" int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32
 // the current device every time a plan is created.
 template <int NUM_A, bool B_FP4, int EPI>
 static int prepare_gemm() {
-  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A>::SMEM_BYTES));
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 64>::SMEM_BYTES));
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 128>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 128>::SMEM_BYTES));
   return DSV4_OK;
+}
+
+// The GEMM tile: the plan's setting, else the environment's
+// (DSV4_GEMM_BN=64|128), else 64 tokens.  A 128-token tile halves the MMA
+// instructions per token but single-buffers the accumulators, so the
+// SwiGLU epilogue no longer overlaps the next tile; on config 2 (2048
+// tokens, a4w4) it measured slower than 64, hence the default.
+static int gemm_bn(int plan_bn) {
+  static const int env_bn = [] {
+    const char* e = getenv("DSV4_GEMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (plan_bn == 64 || plan_bn == 128) return plan_bn;
+  if (env_bn == 64 || env_bn == 128) return env_bn;
+  return 64;
+}
+
+template <bool B_FP4, int EPI>
+static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, const CUtensorMap& tmA,
+                               const CUtensorMap* tmB, const GemmParams& g) {
+  const dim3 grid(num_sms), block(G_THREADS);
+  if (bn == 128)
+    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 128>, grid, block, GemmCfg<2, 128>::SMEM_BYTES, st, pdl, tmA,
+                    tmB[0], tmB[1], tmB[2], tmB[3], g);
+  return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64>::SMEM_BYTES, st, pdl, tmA,
+                  tmB[0], tmB[1], tmB[2], tmB[2], g);
 }
 
 extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts,
@@ -596,8 +629,8 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
     const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA2, U4, 5, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
   }
-  const uint32_t brows[3] = {16, 32, 64};
-  for (int j = 0; j < 3; ++j) {
+  const uint32_t brows[4] = {16, 32, 64, 128};
+  for (int j = 0; j < 4; ++j) {
     const uint32_t bbox[2] = {G_BK, brows[j]};
     {
       const uint64_t dims[2] = {H, PC}, s8[1] = {H}, s4[1] = {H / 2};
@@ -639,6 +672,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   cudaStream_t st = (cudaStream_t)stream;
   const WsLayout& w = p->wl;
   const int P = (int)(n_tokens * p->topk);
+  const int bn = gemm_bn(p->gemm_tile);   // GEMM tile = expert-group padding
   int* status = wsp<int>(p, w.status);
   int32_t* sorted_flat = wsp<int32_t>(p, w.sorted_flat);
   int32_t* inv = wsp<int32_t>(p, w.inv);
@@ -654,17 +688,17 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, p->topk,
                            p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets), sorted_flat,
                            inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                           wsp<int4>(p, w.chunks), n_chunks, (int)G_BN, status));
+                           wsp<int4>(p, w.chunks), n_chunks, bn, status));
   mark(1);
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
-  const int64_t rb_cap = w.p_cap / G_BN;
+  const int64_t rb_cap = w.p_cap / bn;   // BN-row scale blocks per k-tile
   {
     const int64_t warps = n_tokens * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
     DSV4_CUDA_CHECK(launch_k(fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
                              dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, n_tokens,
-                             p->topk, p->H, rb_cap, p->ws + w.xq, p->ws + w.xsf));
+                             p->topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf));
   }
   mark(2);
   GemmParams g1{};
@@ -696,20 +730,15 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g2.out_sf = nullptr;
   g2.out_bf16 = wsp<uint16_t>(p, w.out);
   g2.out_ld = p->H;
-  const dim3 grid(p->num_sms), block(G_THREADS);
   if (fp4)
-    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, true, EPI_SWIGLU_MXFP4>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
-                             p->tmA13, p->tmB1_fp4[0], p->tmB1_fp4[1], p->tmB1_fp4[2], g1));
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp4, g1)));
   else
-    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, false, EPI_SWIGLU_FP8>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
-                             p->tmA13, p->tmB1_fp8[0], p->tmB1_fp8[1], p->tmB1_fp8[2], g1));
+    DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp8, g1)));
   mark(3);
   if (fp4)
-    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, true, EPI_STORE_BF16>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
-                             p->tmA2, p->tmB2_fp4[0], p->tmB2_fp4[1], p->tmB2_fp4[2], g2));
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp4, g2)));
   else
-    DSV4_CUDA_CHECK(launch_k(moe_gemm_kernel<2, false, EPI_STORE_BF16>, grid, block, GemmCfg<2>::SMEM_BYTES, st, pdl,
-                             p->tmA2, p->tmB2_fp8[0], p->tmB2_fp8[1], p->tmB2_fp8[2], g2));
+    DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, g2)));
   mark(4);
   {
     const int threads = std::min(128, p->H / 8);
@@ -731,6 +760,15 @@ extern "C" int dsv4_moe_enable_timing(dsv4_moe_plan* p, int32_t enable) {
     for (auto& e : p->ev)
       if (!e) DSV4_CUDA_CHECK(cudaEventCreate(&e));
   p->timing = enable != 0;
+  DSV4_API_END
+}
+
+extern "C" int dsv4_moe_set_gemm_tile(dsv4_moe_plan* p, int32_t tokens_per_tile) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p, "null plan");
+  DSV4_CHECK_ARG(tokens_per_tile == 0 || tokens_per_tile == 64 || tokens_per_tile == 128,
+                 "tokens per GEMM tile must be 0 (default), 64 or 128");
+  p->gemm_tile = tokens_per_tile;
   DSV4_API_END
 }
 

@@ -165,6 +165,11 @@ int dsv4_moe_combine_ordered(const void* rows_bf16, const int32_t* order, int64_
  * [4] combine. */
 int dsv4_moe_enable_timing(dsv4_moe_plan* plan, int32_t enable);
 int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
+/* Tokens per GEMM tile (no counterpart in the reference): 64 or 128, or 0
+ * for the library's choice (64; the environment variable DSV4_GEMM_BN
+ * overrides it).  The tile is also the padding of each expert's row group.
+ * Takes effect from the next dsv4_moe_forward on the plan. */
+int dsv4_moe_set_gemm_tile(dsv4_moe_plan* plan, int32_t tokens_per_tile);
 /* Device pointers of the plan's align outputs (valid after a forward):
  * counts[E], offsets[E+1], sorted_flat[P], inv[P], active[E], n_active[1]. */
 int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,

@@ -135,3 +135,24 @@ def test_cfg1_decode_matches_oracle(ops, layer1, T):
     plan.status()
     ref = L.oracle(x, w.cpu().numpy(), idx.cpu().numpy().astype(np.int64), "bf16")
     assert rel_err(bf16_to_np(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("T", [40, 256, 700])
+def test_cfg0_gemm_tile_of_128_tokens(ops, layer0, T):
+    """With a 128-token GEMM tile expert groups are padded to 128 rows and
+    chunks of up to 128 rows run as one MMA N."""
+    L = layer0
+    x = S.make_tokens(L.cfg, 300 + T, T)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
+    plan = _plan(ops, L, T)
+    plan.set_gemm_tile(128)
+    for profile in ("bf16", "a4w4"):
+        y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
+                         L.slot_of, profile)
+        plan.status()
+        assert rel_err(bf16_to_np(y), L.oracle(x, w, idx, profile)) <= TOL, profile
+    d = plan.debug_align(T)
+    starts = d["offsets"].numpy()[:-1]
+    assert np.all(starts % 128 == 0)
+    ref = O.moe_align(idx, L.n)
+    assert np.array_equal(np.argsort(d["inv"].numpy(), kind="stable"), ref["order"])
