@@ -50,10 +50,11 @@ int dsv4_abi_version(void);
  * One expert = w1/w3 [I, H/2] + w2 [H, I/2] packed E2M1 (low nibble = even k)
  * and E8M0 per-32 scales, stored as ONE contiguous slot:
  *   [w13 packed (w1 rows then w3 rows) | w2 packed | w13 scales | w2 scales]
- * The packed weights are tiled into contiguous 8 KiB blocks of 128 rows x
- * 128 elements (one TMA box each); the scales are re-tiled into 512-byte
- * atoms (128 rows x 4 scale bytes, row r at (r%32)*16 + (r/32)*4) that the
- * tensor cores read directly.
+ * The packed weights are tiled into contiguous 16 KiB blocks of 256 rows x
+ * 128 elements (one TMA box each): for w13 a block holds 128 rows of w1 and
+ * the same 128 rows of w3, for w2 two consecutive 128-row tiles.  The scales
+ * are re-tiled into 512-byte atoms (128 rows x 4 scale bytes, row r at
+ * (r%32)*16 + (r/32)*4), two per block, that the tensor cores read directly.
  * Replaces the six per-expert host tensors of ExpertBank.register
  * (offload.py:59-68) and their per-call stacking (deepseek_v4.py:218-223).
  * ------------------------------------------------------------------------ */
