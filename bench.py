@@ -758,7 +758,7 @@ def run_reference(a):
 def run_ep(a, rank, world, device):
     from dsv4_plugin.parallel_ep import run_ep_bench
     line = run_ep_bench(a, rank, world, device, METRIC, UNIT, build_layer, _token_batches, Clocks,
-                        L2_FLUSH_BYTES)
+                        L2_FLUSH_BYTES, gemm_bytes=_gemm_bytes, peaks=_peaks())
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
 

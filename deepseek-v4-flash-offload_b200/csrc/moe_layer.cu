@@ -120,7 +120,9 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     float wv = 0.f;
     if (tid < P) {
       e = idx[tid];
-      if (e < 0 || e >= E) {
+      if (e == -1) {   // an empty assignment (padding of the expert-parallel exchange)
+        inv[tid] = -1;
+      } else if (e < 0 || e >= E) {
         set_status(status, DSV4_EINVAL);
         inv[tid] = -1;
         e = -1;
@@ -185,7 +187,9 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   __syncthreads();
   for (int p = tid; p < P; p += AL_THREADS) {
     int e = idx[p];
-    if (e < 0 || e >= E) {
+    if (e == -1) {   // an empty assignment
+      inv[p] = -1;
+    } else if (e < 0 || e >= E) {
       set_status(status, DSV4_EINVAL);
       inv[p] = -1;
       e = -1;
@@ -301,6 +305,8 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
   for (int64_t b = warp0; b < ntask; b += nwarps) {
     const int64_t tok = b / kblk;
     const int kb = (int)(b - tok * kblk);
+    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
+    if (__ballot_sync(0xffffffffu, my_row >= 0) == 0u) continue;   // no assignment to write
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -311,7 +317,6 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
     uint32_t o = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv_s, -448.f), 448.f)) << (8 * i);
-    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
     for (int j = 0; j < topk; ++j) {
       const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
       if (row >= 0) *reinterpret_cast<uint32_t*>(q + row * K + kb * 128 + lane * 4) = o;
@@ -336,6 +341,8 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
   for (int64_t b = warp0; b < ntask; b += nwarps) {
     const int64_t tok = b / kblk;
     const int kb = (int)(b - tok * kblk);
+    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
+    if (__ballot_sync(0xffffffffu, my_row >= 0) == 0u) continue;   // no assignment to write
     const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
     const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
                         bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
@@ -351,7 +358,6 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
                            ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
                            ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
                            ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
-    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
     for (int j = 0; j < topk; ++j) {
       const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
       if (row >= 0) *reinterpret_cast<uint16_t*>(q + row * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;

@@ -70,6 +70,87 @@ class ExpertParallel:
         return back, ordered
 
 
+class StaticExchange:
+    """Dispatch / return with a fixed capacity of C = T*k rows per peer.
+
+    The exact exchange above needs the per-peer row counts on the host (one
+    synchronisation per step).  Here every rank sends C rows to every peer
+    (the worst case: all of its assignments on one peer), padding rows carry
+    expert id -1, which the routed-expert kernels skip.  Every step is a
+    device operation with a shape known in advance, so the whole layer
+    (router, exchange, experts, return, combine) can be captured in one CUDA
+    graph, NCCL collectives included.  Bookkeeping uses only ops without
+    host synchronisation (stable sort, scatter_add, cumsum, gathers)."""
+
+    def __init__(self, n_experts: int, rank: int, world: int, tokens: int, topk: int, hidden: int, device,
+                 group=None, dtype=torch.bfloat16):
+        if n_experts % world:
+            raise ValueError("n_experts must divide evenly over the ranks")
+        self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
+        self.e_loc = n_experts // world
+        self.t, self.k, self.h = tokens, topk, hidden
+        self.cap = tokens * topk
+        n = world * self.cap
+        self.send_x = torch.empty((n, hidden), dtype=dtype, device=device)
+        self.recv_x = torch.empty_like(self.send_x)
+        self.send_meta = torch.empty((n, 2), dtype=torch.int32, device=device)
+        self.recv_meta = torch.empty_like(self.send_meta)
+        self.back = torch.empty_like(self.send_x)
+        self._p = torch.arange(tokens * topk, device=device)
+        self._dev = None
+
+    def pack(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
+        """Fill the send buffers; -> pos [P] (slot of each assignment).  On
+        CUDA one library call (``dsv4_ep_dispatch_pack``), which also fills
+        the combine order; elsewhere the same bookkeeping in torch ops."""
+        if x.is_cuda:
+            from dsv4_plugin._lib import check, lib
+            if self._dev is None:
+                p = self.t * self.k
+                self._dev = {"pos": torch.empty(p, dtype=torch.int32, device=x.device),
+                             "ordered": torch.empty((self.t, self.k), dtype=torch.int32, device=x.device),
+                             "status": torch.zeros(1, dtype=torch.int32, device=x.device)}
+            d = self._dev
+            x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
+            check(lib().dsv4_ep_dispatch_pack(x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.k, self.h,
+                                              self.n_experts, self.world, self.send_x.data_ptr(),
+                                              self.send_meta.data_ptr(), d["pos"].data_ptr(),
+                                              d["ordered"].data_ptr(), d["status"].data_ptr(),
+                                              torch.cuda.current_stream(x.device).cuda_stream))
+            return d["pos"]
+        flat_e = indices.reshape(-1).to(torch.int64)
+        dest = torch.div(flat_e, self.e_loc, rounding_mode="floor")
+        order = torch.sort(dest, stable=True).indices
+        counts = torch.zeros(self.world, dtype=torch.int64, device=dest.device)
+        counts.scatter_add_(0, dest, torch.ones_like(dest))
+        start = torch.cumsum(counts, 0) - counts
+        rank_sorted = self._p - start.index_select(0, dest.index_select(0, order))
+        rank = torch.empty_like(rank_sorted)
+        rank[order] = rank_sorted
+        pos = dest * self.cap + rank
+        self.send_meta.fill_(-1)
+        self.send_meta[pos, 0] = flat_e.to(torch.int32)
+        self.send_meta[pos, 1] = weights.reshape(-1).float().view(torch.int32)
+        self.send_x[pos] = x.index_select(0, torch.div(self._p, self.k, rounding_mode="floor"))
+        return pos
+
+    def exchange(self):
+        dist.all_to_all_single(self.recv_x, self.send_x, group=self.group)
+        dist.all_to_all_single(self.recv_meta, self.send_meta, group=self.group)
+        return self.recv_x, self.recv_meta[:, 0], self.recv_meta[:, 1].view(torch.float32)
+
+    def give_back(self, y_recv: torch.Tensor):
+        dist.all_to_all_single(self.back, y_recv, group=self.group)
+        return self.back
+
+    def order(self, pos: torch.Tensor, indices: torch.Tensor):
+        """Per token, its k slots in ascending expert id order [T, k]."""
+        if self._dev is not None and pos.is_cuda:
+            return self._dev["ordered"]
+        srt = torch.argsort(indices.to(torch.int64), dim=1, stable=True)
+        return pos.view(self.t, self.k).gather(1, srt)
+
+
 class ExpertParallelMoE:
     """Expert-parallel forward of an ``OffloadDeepseekV4MoE`` whose bank
     holds this rank's experts."""
@@ -84,6 +165,49 @@ class ExpertParallelMoE:
         table[lo:lo + n] = torch.tensor(slots, dtype=torch.int32)
         self.slot_of = table.to(bank.device)
         self.plan = None
+        self._static = {}
+        self.segment_times = None   # set to {} to time the segments of eager forward_static calls
+
+    def forward_static(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
+        """The same layer through ``StaticExchange``: no host synchronisation,
+        so the call can be captured in a CUDA graph.  Equals ``forward`` bit
+        for bit."""
+        from dsv4_plugin import ops
+        moe = self.moe
+        t = hs.shape[0]
+        ex = self._static.get(t)
+        if ex is None:
+            ex = StaticExchange(moe.n_routed_experts, self.ep.rank, self.ep.world, t, moe.topk, hs.shape[1],
+                                hs.device, self.ep.group)
+            self._static[t] = ex
+        marks = [] if self.segment_times is not None else None
+
+        def mark():
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        mark()
+        w, idx = moe._route(hs, None)
+        mark()
+        pos = ex.pack(hs, w, idx)
+        mark()
+        x_recv, e_recv, w_recv = ex.exchange()
+        mark()
+        plan = moe.engine.plan_for(moe.n_routed_experts, 1, x_recv.shape[0], moe.swiglu_limit or 0.0)
+        self.plan = plan
+        y_recv = plan.forward(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile)
+        mark()
+        back = ex.give_back(y_recv)
+        mark()
+        y = ops.combine_ordered(back, ex.order(pos, idx))
+        mark()
+        if marks is not None:
+            marks[-1].synchronize()
+            names = ("route", "pack", "dispatch_a2a", "experts", "return_a2a", "combine")
+            self.segment_times = {n: marks[i].elapsed_time(marks[i + 1]) for i, n in enumerate(names)}
+        return y
 
     def forward(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         from dsv4_plugin import ops
@@ -100,8 +224,11 @@ class ExpertParallelMoE:
         return ops.combine_ordered(rows, order)
 
 
-def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batches, Clocks, flush_bytes):
-    """Weak-scaling bench: T tokens per rank, E/R experts per rank."""
+def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batches, Clocks, flush_bytes,
+                 gemm_bytes=None, peaks=None):
+    """Weak-scaling bench: T tokens per rank, E/R experts per rank.  The layer
+    runs through the fixed-capacity exchange and is replayed as one CUDA
+    graph per step (router, NCCL dispatch, experts, NCCL return, combine)."""
     import os
 
     if not dist.is_initialized():
@@ -113,8 +240,18 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
     host, dev = token_batches(8, T, device, rank)
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    xs = torch.empty_like(dev[0])
+    xs.copy_(dev[0])
+    for _ in range(2):
+        epm.forward_static(xs)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ys = epm.forward_static(xs)
+    torch.cuda.synchronize(device)
 
-    def steps(n, record=True):
+    def steps(n, src, record=True, e2e=False):
         ms = []
         for s in range(n):
             flush.zero_()
@@ -122,19 +259,23 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
             torch.cuda.synchronize(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            epm.forward(dev[s % len(dev)])
+            xs.copy_(src[s % len(src)], non_blocking=True)
+            g.replay()
+            if e2e:
+                y_host.copy_(ys, non_blocking=True)
             e1.record(stream)
             e1.synchronize()
             if record:
                 ms.append(e0.elapsed_time(e1))
         return ms
 
-    steps(a.warmup, record=False)
+    y_host = torch.empty((T, moe.gate.weight.shape[1]), dtype=torch.bfloat16).pin_memory()
+    steps(a.warmup, dev, record=False)
     clk = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
     dist.barrier()
     torch.cuda.synchronize(device)
     clk.start()
-    ms = steps(a.steps)
+    ms = steps(a.steps, dev)
     dist.barrier()
     torch.cuda.synchronize(device)
     clocks = clk.stop()
@@ -143,33 +284,43 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     tot_ms = float(t.sum().item())
     value = world * T * a.steps / (tot_ms / 1e3)
-
-    # e2e: host tokens in, host output back, same exchange
-    y_host = torch.empty((T, moe.gate.weight.shape[1]), dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(dev[0])
-
-    def e2e_steps(n, record=True):
-        out = []
-        for s in range(n):
-            flush.zero_()
-            dist.barrier()
-            torch.cuda.synchronize(device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            xd.copy_(host[s % len(host)], non_blocking=True)
-            y = epm.forward(xd)
-            y_host.copy_(y, non_blocking=True)
-            e1.record(stream)
-            e1.synchronize()
-            if record:
-                out.append(e0.elapsed_time(e1))
-        return out
-
-    e2e_steps(2, record=False)
-    te = torch.tensor(e2e_steps(a.steps), dtype=torch.float64, device=device)
+    steps(2, host, record=False, e2e=True)
+    te = torch.tensor(steps(a.steps, host, e2e=True), dtype=torch.float64, device=device)
     dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.sum().item())
-    epm.plan.status()
+    # per-rank gate/up GEMM roofline from an eager pass with stage timing
+    plan = epm.plan
+    plan.enable_timing(True)
+    g1 = []
+    for s in range(3):
+        flush.zero_()
+        dist.barrier()
+        epm.forward_static(dev[s % len(dev)])
+        torch.cuda.synchronize(device)
+        st = plan.stage_times()
+        g1.append((st["gate_up_gemm"], plan.n_active(), st))
+    plan.enable_timing(False)
+    epm.segment_times = {}
+    for s in range(3):
+        flush.zero_()
+        dist.barrier()
+        epm.forward_static(dev[s % len(dev)])
+    seg = dict(epm.segment_times)
+    epm.segment_times = None
+    plan.status()
+    roof = None
+    if gemm_bytes is not None and peaks is not None:
+        hbm, kind = peaks
+        p_rows = int(epm._static[T].recv_meta.shape[0])
+        ach = [gemm_bytes(d, T * moe.topk, "gate_up") / (ms_ / 1e3) / 1e9 for ms_, d, _ in g1]
+        worst = torch.tensor([min(ach)], dtype=torch.float64, device=device)
+        dist.all_reduce(worst, op=dist.ReduceOp.MIN)
+        roof = {"bound": "hbm", "kernel": "moe_gemm_kernel (gate/up) of the slowest rank",
+                "achieved": round(float(worst.item()), 1), "peak": hbm, "peak_kind": f"{kind} HBM copy",
+                "unit": "GB/s", "frac": round(float(worst.item()) / hbm, 4), "traffic": None,
+                "exchange_rows_per_rank": p_rows}
+    del g
+    torch.cuda.synchronize(device)
     del epm
     dist.barrier()
     dist.destroy_process_group()
@@ -184,9 +335,13 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
             "config": {"workload": f"cfg1 decode bf16 profile, expert parallel: T={T} tokens per rank, "
                                    f"E={moe.n_routed_experts} experts, {moe.n_routed_experts // world} per rank",
                        "tokens_per_step": T * world, "global_batch": T * world,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)",
+                       "parallelism": f"ep{world} (NCCL all-to-all, fixed capacity {T * moe.topk} rows per peer, "
+                                      "one CUDA graph per step)",
                        "l2": "256 MiB flush before every timed step; 8 rotating token batches per rank"},
+            "roofline": roof,
             "e2e": {"value": round(world * T * a.steps / (e2e_ms / 1e3), 1), "unit": unit,
                     "h2d_bytes_per_step": T * h * 2, "d2h_bytes_per_step": T * h * 2},
             "clocks": clocks, "gpu_launches": 8 * a.steps,
-            "detail": {"step_ms_median": round(statistics.median(t.tolist()), 5)}}
+            "detail": {"step_ms_median": round(statistics.median(t.tolist()), 5),
+                       "rank0_eager_segments_ms": {k: round(v, 5) for k, v in seg.items()},
+                       "rank0_stage_ms": {k: round(v, 5) for k, v in g1[-1][2].items()}}}

@@ -121,7 +121,9 @@ int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float
  * (token, slot) assignments by expert id.  sorted_flat[pos] = t*k + j,
  * inv[t*k + j] = pos, offsets = exclusive prefix of counts (E+1 entries),
  * active = ascending ids with count > 0, *n_active their number.  An index
- * outside [0, n_experts) sets DSV4_EINVAL in *status (device word).
+ * of -1 is an empty assignment (inv = -1, no error: the padding rows of the
+ * expert-parallel exchange); any other index outside [0, n_experts) sets
+ * DSV4_EINVAL in *status (device word).
  * ------------------------------------------------------------------------ */
 int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t topk, int32_t n_experts, int32_t* counts,
                    int32_t* offsets, int32_t* sorted_flat, int32_t* inv, int32_t* active, int32_t* n_active,
@@ -175,6 +177,27 @@ int dsv4_moe_set_gemm_tile(dsv4_moe_plan* plan, int32_t tokens_per_tile);
  * counts[E], offsets[E+1], sorted_flat[P], inv[P], active[E], n_active[1]. */
 int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,
                          int32_t** inv, int32_t** active, int32_t** n_active);
+
+/* ------------------------------------------------------------------------ *
+ * Expert-parallel dispatch packing (no counterpart in the reference, whose
+ * expert-parallel size is 1, deepseek_v4.py:82).  Expert e lives on rank
+ * e / (n_experts / world).  Every rank sends cap = n_tokens * topk rows to
+ * every peer, so the all-to-all has a fixed shape (graph-capturable).  For
+ * assignment a = t*topk + j with destination d the slot is d*cap + its rank
+ * among the assignments to d (stable):
+ *   send_x[slot] = x[t], send_meta[slot] = (expert, bits of the weight),
+ *   slot_of_assignment[a] = slot;
+ * padding slots get send_meta = (-1, 0), an empty assignment.
+ * ordered_slots[t*topk + j] lists token t's slots in ascending expert order
+ * (-1 after the last), the order in which the returned rows are added.
+ * send_x: [world*cap, hidden] bf16; send_meta: [world*cap, 2] int32;
+ * slot_of_assignment, ordered_slots: [n_tokens*topk] int32.  An expert id
+ * outside [0, n_experts) sets DSV4_EINVAL in *status and is dropped.
+ * ------------------------------------------------------------------------ */
+int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weights, const int32_t* route_indices,
+                          int64_t n_tokens, int32_t topk, int32_t hidden, int32_t n_experts, int32_t world,
+                          void* send_x_bf16, int32_t* send_meta, int32_t* slot_of_assignment,
+                          int32_t* ordered_slots, int* status, void* stream);
 
 #ifdef __cplusplus
 }

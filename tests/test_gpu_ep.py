@@ -63,6 +63,23 @@ def _run(rank, world, port, tokens, out):
             torch.cuda.synchronize(dev)
             epm.plan.status()
             out[(rank, profile)] = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        # fixed-capacity exchange, eager and captured in a CUDA graph with its NCCL calls
+        ref = full.forward(xt).clone()
+        got = epm.forward_static(xt)
+        torch.cuda.synchronize(dev)
+        epm.plan.status()
+        out[(rank, "static")] = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        xs = xt.clone()
+        epm.forward_static(xs)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ys = epm.forward_static(xs)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        out[(rank, "graph")] = bool(torch.equal(ys.view(torch.int16), ref.view(torch.int16)))
+        del g
+        torch.cuda.synchronize(dev)
         del epm
     finally:
         dist.destroy_process_group()
@@ -75,7 +92,7 @@ def test_ep_world1_equals_single_gpu(tokens):
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_run, args=(1, _port(), tokens, out), nprocs=1, join=True)
-    assert dict(out) == {(0, "bf16"): True, (0, "a4w4"): True}
+    assert dict(out) == {(0, "bf16"): True, (0, "a4w4"): True, (0, "static"): True, (0, "graph"): True}
 
 
 def test_ep_world2_equals_single_gpu():
@@ -84,4 +101,30 @@ def test_ep_world2_equals_single_gpu():
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_run, args=(2, _port(), 33, out), nprocs=2, join=True)
-    assert all(out.values()) and len(out) == 4
+    assert all(out.values()) and len(out) == 8
+
+
+@pytest.mark.parametrize("world,tokens,topk", [(2, 33, 8), (8, 64, 8), (4, 300, 6)])
+def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk):
+    """dsv4_ep_dispatch_pack against the same bookkeeping in torch ops (the
+    CPU path of StaticExchange.pack): slots, metadata, rows, combine order."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from dsv4_plugin.parallel_ep import StaticExchange
+    n_experts, h = 64, 256
+    g = torch.Generator().manual_seed(tokens)
+    x = torch.randn(tokens, h, generator=g).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(n_experts, generator=g)[:topk] for _ in range(tokens)]).to(torch.int32)
+    w = torch.rand(tokens, topk, generator=g)
+    ref = StaticExchange(n_experts, 0, world, tokens, topk, h, "cpu")
+    pos_ref = ref.pack(x, w, idx)
+    ord_ref = ref.order(pos_ref, idx)
+    dev = StaticExchange(n_experts, 0, world, tokens, topk, h, "cuda")
+    pos = dev.pack(x.cuda(), w.cuda(), idx.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(pos.cpu().to(torch.int64), pos_ref)
+    assert torch.equal(dev.send_meta.cpu(), ref.send_meta)
+    valid = ref.send_meta[:, 0] >= 0
+    assert torch.equal(dev.send_x.cpu()[valid].view(torch.int16), ref.send_x[valid].view(torch.int16))
+    assert torch.equal(dev.order(pos, idx).cpu().to(torch.int64), ord_ref)
+    assert int(dev._dev["status"].item()) == 0
