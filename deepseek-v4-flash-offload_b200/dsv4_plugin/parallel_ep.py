@@ -128,7 +128,8 @@ class StaticExchange:
         rank = torch.empty_like(rank_sorted)
         rank[order] = rank_sorted
         pos = dest * self.cap + rank
-        self.send_meta.fill_(-1)
+        self.send_meta[:, 0].fill_(-1)   # padding: empty assignment, weight 0
+        self.send_meta[:, 1].fill_(0)
         self.send_meta[pos, 0] = flat_e.to(torch.int32)
         self.send_meta[pos, 1] = weights.reshape(-1).float().view(torch.int32)
         self.send_x[pos] = x.index_select(0, torch.div(self._p, self.k, rounding_mode="floor"))
