@@ -12,7 +12,10 @@
 // routed-expert kernels.  `ordered[t][0..k)` lists the slots of token t in
 // ascending expert id order: the order in which the returned rows are added
 // (deepseek_v4.py:195-197).
+#include <cstring>
+#include <memory>
 #include <string>
+#include <vector>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -156,4 +159,349 @@ extern "C" int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weig
                            (uint16_t*)send_x_bf16));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
+}
+
+namespace dsv4 {
+
+// ---------------------------------------------------------------------------
+// Exchange over NVLink peer memory (CUDA IPC).  Each rank owns one device
+// block: recv_x [world*cap, H] bf16 and recv_meta [world*cap] (expert,
+// weight) that the peers write their dispatched rows into (source s fills
+// rows s*cap..), back [world*cap, H] bf16 that the peers write the expert
+// outputs of this rank's assignments into (owner d fills rows d*cap..),
+// and flags.  Only real rows cross NVLink; padding is marked in the
+// metadata.  Every step increments a device epoch; a rank publishes
+// "dispatch done" / "return done" by storing the epoch into its slot of each
+// peer's flags (release, system scope) after its rows are fenced, and a
+// receiver waits (acquire, bounded) until every source's flag has reached
+// the epoch.  A peer writes into this rank's receive buffers for step e+1
+// only after it received this rank's step-e return, which this rank sends
+// after consuming step e, so one buffer set suffices.
+// ---------------------------------------------------------------------------
+struct EpBlock {
+  int64_t off_back, off_meta, off_flags, off_ctrl, bytes;
+};
+static EpBlock ep_block(int world, int64_t cap, int hidden) {
+  auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
+  EpBlock b;
+  const int64_t rows = (int64_t)world * cap;
+  b.off_back = al(rows * hidden * 2);
+  b.off_meta = b.off_back + al(rows * hidden * 2);
+  b.off_flags = b.off_meta + al(rows * 8);
+  b.off_ctrl = b.off_flags + al(2 * (int64_t)world * 4);
+  b.bytes = b.off_ctrl + 256;
+  return b;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One CTA: epoch += 1, slots of the assignments (as ep_pack_index_kernel),
+// metadata straight into the owners' recv_meta (padding included), the
+// combine order, and a system fence.
+__global__ void __launch_bounds__(EP_THREADS, 1)
+    ep_p2p_index_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int64_t P, int topk,
+                        int e_loc, int world, int my_rank, int64_t cap, uint8_t* const* __restrict__ peers,
+                        int64_t off_meta, uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos,
+                        int32_t* __restrict__ ordered, int* __restrict__ status) {
+  __shared__ int wc[32][EP_MAX_WORLD];
+  __shared__ int base[EP_MAX_WORLD];
+  __shared__ int round_tot[EP_MAX_WORLD];
+  griddep_wait();
+  griddep_launch();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) ctrl[0] = ctrl[0] + 1u;   // this step's epoch
+  if (tid < world) base[tid] = 0;
+  for (int64_t r0 = 0; r0 < P; r0 += EP_THREADS) {
+    for (int i = tid; i < 32 * EP_MAX_WORLD; i += EP_THREADS) (&wc[0][0])[i] = 0;
+    __syncthreads();
+    const int64_t a = r0 + tid;
+    int e = -1, d = -1;
+    if (a < P) {
+      e = idx[a];
+      if (e < 0 || e >= e_loc * world) {
+        set_status(status, DSV4_EINVAL);
+        e = -1;
+      } else {
+        d = e / e_loc;
+      }
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, d);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    if (d >= 0 && rank == 0) wc[warp][d] = __popc(same);
+    __syncthreads();
+    if (tid < world) {
+      int s = 0;
+      for (int v = 0; v < 32; ++v) {
+        const int c = wc[v][tid];
+        wc[v][tid] = s;
+        s += c;
+      }
+      round_tot[tid] = s;
+    }
+    __syncthreads();
+    if (d >= 0) {
+      const int64_t r = base[d] + wc[warp][d] + rank;
+      pos[a] = (int32_t)((int64_t)d * cap + r);
+      int2* m = reinterpret_cast<int2*>(peers[d] + off_meta) + (int64_t)my_rank * cap + r;
+      *m = make_int2(e, __float_as_int(w[a]));
+    } else if (a < P) {
+      pos[a] = -1;
+    }
+    __syncthreads();
+    if (tid < world) base[tid] += round_tot[tid];
+    __syncthreads();
+  }
+  for (int64_t s = tid; s < (int64_t)world * cap; s += EP_THREADS) {
+    const int d = (int)(s / cap);
+    const int64_t r = s - (int64_t)d * cap;
+    if (r >= base[d]) *(reinterpret_cast<int2*>(peers[d] + off_meta) + (int64_t)my_rank * cap + r) = make_int2(-1, 0);
+  }
+  for (int64_t t = tid; t < P / topk; t += EP_THREADS) {
+    int ke[16], kp[16];
+    int n = 0;
+    for (int j = 0; j < topk; ++j) {
+      const int e = idx[t * topk + j];
+      const int p = pos[t * topk + j];
+      if (p < 0) continue;
+      int i = n++;
+      while (i > 0 && ke[i - 1] > e) {
+        ke[i] = ke[i - 1];
+        kp[i] = kp[i - 1];
+        --i;
+      }
+      ke[i] = e;
+      kp[i] = p;
+    }
+    for (int j = 0; j < topk; ++j) ordered[t * topk + j] = j < n ? kp[j] : -1;
+  }
+  __threadfence_system();
+}
+
+// After every CTA fenced its peer writes, the last CTA to finish publishes
+// the epoch into slot `flag_slot` of every peer's flags.
+__device__ __forceinline__ void ep_publish(uint32_t* __restrict__ ctrl, int counter, uint8_t* const* __restrict__ peers,
+                                           int world, int64_t off_flags, int flag_slot) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&ctrl[counter], 1u);
+    if (prev == gridDim.x - 1) {
+      ctrl[counter] = 0u;
+      __threadfence_system();
+      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctrl[0]);
+      for (int d = 0; d < world; ++d)
+        st_release_sys(reinterpret_cast<uint32_t*>(peers[d] + off_flags) + flag_slot, epoch);
+    }
+  }
+}
+
+// One warp per assignment: the token's row straight into the owner's recv_x.
+__global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ pos, int64_t P,
+                                   int topk, int H, int world, int my_rank, int64_t cap,
+                                   uint8_t* const* __restrict__ peers, int64_t off_flags,
+                                   uint32_t* __restrict__ ctrl) {
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t a = warp0; a < P; a += nwarps) {
+    const int p = pos[a];
+    if (p < 0) continue;
+    const int d = (int)(p / cap);
+    const int64_t r = p - (int64_t)d * cap;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (a / topk) * H);
+    uint4* dst = reinterpret_cast<uint4*>(peers[d]) + ((int64_t)my_rank * cap + r) * (H / 8);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  }
+  ep_publish(ctrl, 1, peers, world, off_flags, my_rank);
+}
+
+// One warp per received slot: the expert output row back into the source's
+// `back` (rows my_rank*cap.. of the source).
+__global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y_recv, const int2* __restrict__ meta, int world,
+                                     int my_rank, int64_t cap, int H, uint8_t* const* __restrict__ peers,
+                                     int64_t off_back, int64_t off_flags, uint32_t* __restrict__ ctrl) {
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t s = warp0; s < (int64_t)world * cap; s += nwarps) {
+    if (meta[s].x < 0) continue;
+    const int src = (int)(s / cap);
+    const int64_t j = s - (int64_t)src * cap;
+    const uint4* from = reinterpret_cast<const uint4*>(y_recv + s * H);
+    uint4* dst = reinterpret_cast<uint4*>(peers[src] + off_back) + ((int64_t)my_rank * cap + j) * (H / 8);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = from[c];
+  }
+  ep_publish(ctrl, 2, peers, world, off_flags, world + my_rank);
+}
+
+// One thread: wait (bounded) until every source has published this step's
+// epoch in flags[first .. first+world).
+__global__ void ep_p2p_wait_kernel(const uint32_t* __restrict__ flags, const uint32_t* __restrict__ ctrl, int world,
+                                   int* __restrict__ status) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x != 0) return;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(&ctrl[0]);
+  const uint64_t t0 = globaltimer_ns();
+  for (int s = 0; s < world; ++s) {
+    while ((int32_t)(ld_acquire_sys(flags + s) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > DSV4_WAIT_NS) {
+        set_status(status, DSV4_ETIMEOUT);
+        return;
+      }
+    }
+  }
+}
+
+}  // namespace dsv4
+
+struct dsv4_ep {
+  int rank = 0, world = 1, device = 0, hidden = 0;
+  int64_t cap = 0;
+  dsv4::EpBlock blk{};
+  uint8_t* base = nullptr;
+  uint8_t** peers_dev = nullptr;
+  std::vector<uint8_t*> opened;   // peer blocks opened through IPC
+  ~dsv4_ep() {
+    cudaSetDevice(device);
+    for (uint8_t* p : opened)
+      if (p) cudaIpcCloseMemHandle(p);
+    if (peers_dev) cudaFree(peers_dev);
+    if (base) cudaFree(base);
+  }
+};
+
+namespace dsv4 {
+namespace {
+int ep_check(dsv4_ep* ep) {
+  if (!ep) return fail(DSV4_EINVAL, "null expert-parallel handle");
+  if (!ep->peers_dev) return fail(DSV4_EINVAL, "dsv4_ep_connect has not been called");
+  return DSV4_OK;
+}
+}  // namespace
+}  // namespace dsv4
+
+extern "C" int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t cap_rows,
+                              int32_t hidden, void* ipc_handle_out) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(out && ipc_handle_out, "null pointer");
+  DSV4_CHECK_ARG(world > 0 && world <= EP_MAX_WORLD && rank >= 0 && rank < world, "rank/world out of range");
+  DSV4_CHECK_ARG(cap_rows > 0 && hidden > 0 && hidden % 8 == 0, "bad capacity / hidden");
+  std::unique_ptr<dsv4_ep> ep(new dsv4_ep);
+  ep->device = device;
+  DSV4_CUDA_CHECK(cudaSetDevice(device));
+  ep->rank = rank;
+  ep->world = world;
+  ep->cap = cap_rows;
+  ep->hidden = hidden;
+  ep->blk = ep_block(world, cap_rows, hidden);
+  DSV4_CUDA_CHECK(cudaMalloc(&ep->base, (size_t)ep->blk.bytes));
+  DSV4_CUDA_CHECK(cudaMemset(ep->base + ep->blk.off_flags, 0, (size_t)(ep->blk.bytes - ep->blk.off_flags)));
+  cudaIpcMemHandle_t h;
+  DSV4_CUDA_CHECK(cudaIpcGetMemHandle(&h, ep->base));
+  memcpy(ipc_handle_out, &h, sizeof(h));
+  *out = ep.release();
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_ipc_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int dsv4_ep_connect(dsv4_ep* ep, const void* handles) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(ep && handles, "null pointer");
+  DSV4_CHECK_ARG(!ep->peers_dev, "already connected");
+  DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
+  std::vector<uint8_t*> peers(ep->world, nullptr);
+  for (int r = 0; r < ep->world; ++r) {
+    if (r == ep->rank) {
+      peers[r] = ep->base;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    DSV4_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    peers[r] = static_cast<uint8_t*>(p);
+    ep->opened.push_back(peers[r]);
+  }
+  DSV4_CUDA_CHECK(cudaMalloc(&ep->peers_dev, sizeof(uint8_t*) * ep->world));
+  DSV4_CUDA_CHECK(cudaMemcpy(ep->peers_dev, peers.data(), sizeof(uint8_t*) * ep->world, cudaMemcpyHostToDevice));
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_meta, void** back) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(ep && recv_x && recv_meta && back, "null pointer");
+  *recv_x = ep->base;
+  *back = ep->base + ep->blk.off_back;
+  *recv_meta = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_meta);
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights,
+                                const int32_t* route_indices, int64_t n_tokens, int32_t topk, int32_t n_experts,
+                                int32_t* slot_of_assignment, int32_t* ordered_slots, int* status, void* stream) {
+  DSV4_API_BEGIN
+  if (int rc = ep_check(ep)) return rc;
+  DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && slot_of_assignment && ordered_slots && status,
+                 "null pointer");
+  DSV4_CHECK_ARG(topk > 0 && topk <= 16 && n_tokens >= 0 && n_tokens * topk <= ep->cap,
+                 "n_tokens * topk must be in [0, capacity] and topk in [1, 16]");
+  DSV4_CHECK_ARG(n_experts > 0 && n_experts % ep->world == 0, "n_experts must divide over the ranks");
+  DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0, "rows must be 16-byte aligned");
+  DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool pdl = pdl_enabled();
+  const int64_t P = n_tokens * topk;
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, route_weights, P,
+                           (int)topk, (int)(n_experts / ep->world), ep->world, ep->rank, ep->cap,
+                           (uint8_t* const*)ep->peers_dev, ep->blk.off_meta, ctrl, slot_of_assignment, ordered_slots,
+                           status));
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((P * 32 + 255) / 256, 148 * 8));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
+                           (const uint16_t*)x_bf16, (const int32_t*)slot_of_assignment, P, (int)topk, ep->hidden,
+                           ep->world, ep->rank, ep->cap, (uint8_t* const*)ep->peers_dev, ep->blk.off_flags, ctrl));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
+                           (const uint32_t*)(ep->base + ep->blk.off_flags), (const uint32_t*)ctrl, ep->world, status));
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* y_recv_bf16, int* status, void* stream) {
+  DSV4_API_BEGIN
+  if (int rc = ep_check(ep)) return rc;
+  DSV4_CHECK_ARG(y_recv_bf16 && status, "null pointer");
+  DSV4_CHECK_ARG(((uintptr_t)y_recv_bf16 % 16) == 0, "rows must be 16-byte aligned");
+  DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool pdl = pdl_enabled();
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
+  const int64_t rows = (int64_t)ep->world * ep->cap;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows * 32 + 255) / 256, 148 * 8));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_return_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
+                           (const uint16_t*)y_recv_bf16, (const int2*)(ep->base + ep->blk.off_meta), ep->world,
+                           ep->rank, ep->cap, ep->hidden, (uint8_t* const*)ep->peers_dev, ep->blk.off_back,
+                           ep->blk.off_flags, ctrl));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
+                           (const uint32_t*)(ep->base + ep->blk.off_flags) + ep->world, (const uint32_t*)ctrl,
+                           ep->world, status));
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_destroy(dsv4_ep* ep) {
+  delete ep;
+  return DSV4_OK;
 }

@@ -152,6 +152,85 @@ class StaticExchange:
         return pos.view(self.t, self.k).gather(1, srt)
 
 
+class _DevPtr:
+    """A device buffer owned by the library, seen as a torch tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3}
+
+
+class P2PExchange:
+    """Exchange over NVLink peer memory (``dsv4_ep_*``): the same slots as
+    ``StaticExchange``, but each rank writes only its real rows straight
+    into the owners' receive blocks (mapped through CUDA IPC) and the owners
+    write the expert outputs straight back; device flags with a per-step
+    epoch replace the collectives.  No host synchronisation; capturable in a
+    CUDA graph.  Creating it is collective (the IPC handles are gathered)."""
+
+    def __init__(self, n_experts: int, rank: int, world: int, tokens: int, topk: int, hidden: int, device,
+                 group=None):
+        import ctypes as C
+
+        from dsv4_plugin._lib import check, lib
+        if n_experts % world:
+            raise ValueError("n_experts must divide evenly over the ranks")
+        self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
+        self.t, self.k, self.h = tokens, topk, hidden
+        self.cap = tokens * topk
+        self.device = torch.device(device)
+        nb = lib().dsv4_ep_ipc_handle_bytes()
+        handle = C.create_string_buffer(nb)
+        self._h = C.c_void_p()
+        check(lib().dsv4_ep_create(C.byref(self._h), self.device.index, rank, world, self.cap, hidden, handle))
+        mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(self.device)
+        every = torch.empty(world * nb, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        check(lib().dsv4_ep_connect(self._h, every.cpu().numpy().tobytes()))
+        rx, rm, bk = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(rm), C.byref(bk)))
+        rows = world * self.cap
+        self.recv_x = torch.as_tensor(_DevPtr(rx.value, (rows, hidden), "<i2"), device=self.device).view(torch.bfloat16)
+        self.recv_meta = torch.as_tensor(_DevPtr(rm.value, (rows, 2), "<i4"), device=self.device)
+        self.back = torch.as_tensor(_DevPtr(bk.value, (rows, hidden), "<i2"), device=self.device).view(torch.bfloat16)
+        self.pos = torch.empty(self.cap, dtype=torch.int32, device=self.device)
+        self.ordered = torch.empty((tokens, topk), dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
+        from dsv4_plugin._lib import check, lib
+        x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
+        check(lib().dsv4_ep_dispatch(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.k,
+                                     self.n_experts, self.pos.data_ptr(), self.ordered.data_ptr(),
+                                     self.status.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+        return self.recv_x, self.recv_meta[:, 0], self.recv_meta[:, 1].view(torch.float32)
+
+    def give_back(self, y_recv: torch.Tensor):
+        from dsv4_plugin._lib import check, lib
+        y = y_recv.contiguous()
+        check(lib().dsv4_ep_return(self._h, y.data_ptr(), self.status.data_ptr(),
+                                   torch.cuda.current_stream(self.device).cuda_stream))
+        return self.back
+
+    def check_status(self):
+        """Raise when a device-side step failed (e.g. a wait ran out)."""
+        torch.cuda.current_stream(self.device).synchronize()
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            from dsv4_plugin._lib import Dsv4Error
+            raise Dsv4Error(code, "expert-parallel exchange reported this status")
+
+    def close(self):
+        """Collective: unmap the peers' blocks and free this rank's."""
+        from dsv4_plugin._lib import lib
+        if self._h:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            lib().dsv4_ep_destroy(self._h)
+            self._h = None
+
+
 class ExpertParallelMoE:
     """Expert-parallel forward of an ``OffloadDeepseekV4MoE`` whose bank
     holds this rank's experts."""
@@ -167,6 +246,7 @@ class ExpertParallelMoE:
         self.slot_of = table.to(bank.device)
         self.plan = None
         self._static = {}
+        self._p2p = {}
         self.segment_times = None   # set to {} to time the segments of eager forward_static calls
 
     def forward_static(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
@@ -210,6 +290,33 @@ class ExpertParallelMoE:
             self.segment_times = {n: marks[i].elapsed_time(marks[i + 1]) for i, n in enumerate(names)}
         return y
 
+    def forward_p2p(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
+        """The same layer through ``P2PExchange`` (NVLink peer memory): no
+        collectives, no host synchronisation; capturable in a CUDA graph.
+        Equals ``forward`` bit for bit.  The first call with a new token
+        count is collective (it maps the peers' buffers)."""
+        from dsv4_plugin import ops
+        moe = self.moe
+        t = hs.shape[0]
+        ex = self._p2p.get(t)
+        if ex is None:
+            ex = P2PExchange(moe.n_routed_experts, self.ep.rank, self.ep.world, t, moe.topk, hs.shape[1],
+                             hs.device, self.ep.group)
+            self._p2p[t] = ex
+        w, idx = moe._route(hs, None)
+        x_recv, e_recv, w_recv = ex.dispatch(hs, w, idx)
+        plan = moe.engine.plan_for(moe.n_routed_experts, 1, x_recv.shape[0], moe.swiglu_limit or 0.0)
+        self.plan = plan
+        y_recv = plan.forward(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile)
+        back = ex.give_back(y_recv)
+        return ops.combine_ordered(back, ex.ordered)
+
+    def close(self):
+        """Collective: release the peer-memory exchanges."""
+        for ex in self._p2p.values():
+            ex.close()
+        self._p2p.clear()
+
     def forward(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         from dsv4_plugin import ops
         moe = self.moe
@@ -241,15 +348,17 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
     host, dev = token_batches(8, T, device, rank)
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    exchange = os.environ.get("DSV4_EP_EXCHANGE", "p2p")
+    fwd = epm.forward_p2p if exchange == "p2p" else epm.forward_static
     xs = torch.empty_like(dev[0])
     xs.copy_(dev[0])
     for _ in range(2):
-        epm.forward_static(xs)
+        fwd(xs)
     torch.cuda.synchronize(device)
     dist.barrier()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        ys = epm.forward_static(xs)
+        ys = fwd(xs)
     torch.cuda.synchronize(device)
 
     def steps(n, src, record=True, e2e=False):
@@ -296,7 +405,7 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
     for s in range(3):
         flush.zero_()
         dist.barrier()
-        epm.forward_static(dev[s % len(dev)])
+        fwd(dev[s % len(dev)])
         torch.cuda.synchronize(device)
         st = plan.stage_times()
         g1.append((st["gate_up_gemm"], plan.n_active(), st))
@@ -308,6 +417,8 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
         epm.forward_static(dev[s % len(dev)])
     seg = dict(epm.segment_times)
     epm.segment_times = None
+    for ex in epm._p2p.values():
+        ex.check_status()
     plan.status()
     roof = None
     if gemm_bytes is not None and peaks is not None:
@@ -322,6 +433,7 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
                 "exchange_rows_per_rank": p_rows}
     del g
     torch.cuda.synchronize(device)
+    epm.close()
     del epm
     dist.barrier()
     dist.destroy_process_group()
@@ -336,8 +448,9 @@ def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batche
             "config": {"workload": f"cfg1 decode bf16 profile, expert parallel: T={T} tokens per rank, "
                                    f"E={moe.n_routed_experts} experts, {moe.n_routed_experts // world} per rank",
                        "tokens_per_step": T * world, "global_batch": T * world,
-                       "parallelism": f"ep{world} (NCCL all-to-all, fixed capacity {T * moe.topk} rows per peer, "
-                                      "one CUDA graph per step)",
+                       "parallelism": (f"ep{world} (" + ("NVLink peer-memory exchange" if exchange == "p2p" else
+                                                         "NCCL all-to-all") +
+                                       f", fixed capacity {T * moe.topk} rows per peer, one CUDA graph per step)"),
                        "l2": "256 MiB flush before every timed step; 8 rotating token batches per rank"},
             "roofline": roof,
             "e2e": {"value": round(world * T * a.steps / (e2e_ms / 1e3), 1), "unit": unit,

@@ -199,6 +199,37 @@ int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weights, const 
                           void* send_x_bf16, int32_t* send_meta, int32_t* slot_of_assignment,
                           int32_t* ordered_slots, int* status, void* stream);
 
+/* ------------------------------------------------------------------------ *
+ * Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference).  Each rank owns one device block (recv rows, their metadata,
+ * returned rows, flags); peers map it through CUDA IPC and write into it
+ * directly, only real rows crossing NVLink.  Per step:
+ *   dsv4_ep_dispatch: slots as dsv4_ep_dispatch_pack; metadata and rows
+ *     written into the owners' blocks (source s fills rows s*cap.. of the
+ *     owner); then waits (bounded, DSV4_ETIMEOUT in *status) until every
+ *     source published this step;
+ *   (the routed-expert layer runs on recv_x / recv_meta, world*cap rows)
+ *   dsv4_ep_return: each received real row back into its source's `back`
+ *     (owner d fills rows d*cap..), then waits for every owner;
+ *   dsv4_moe_combine_ordered(back, ordered_slots, ...) gives the output.
+ * Every call is an asynchronous device operation with a fixed shape, so a
+ * step can be captured in a CUDA graph.  All ranks must make the same calls
+ * in the same order.  cap = capacity rows per source (n_tokens * topk).
+ * The IPC handle is dsv4_ep_ipc_handle_bytes() bytes; dsv4_ep_connect takes
+ * all ranks' handles, rank-major.
+ * ------------------------------------------------------------------------ */
+typedef struct dsv4_ep dsv4_ep;
+int dsv4_ep_ipc_handle_bytes(void);
+int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t cap_rows, int32_t hidden,
+                   void* ipc_handle_out);
+int dsv4_ep_connect(dsv4_ep* ep, const void* all_handles);
+int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_meta, void** back_bf16);
+int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights, const int32_t* route_indices,
+                     int64_t n_tokens, int32_t topk, int32_t n_experts, int32_t* slot_of_assignment,
+                     int32_t* ordered_slots, int* status, void* stream);
+int dsv4_ep_return(dsv4_ep* ep, const void* y_recv_bf16, int* status, void* stream);
+int dsv4_ep_destroy(dsv4_ep* ep);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,21 @@ def _run(rank, world, port, tokens, out):
         out[(rank, "graph")] = bool(torch.equal(ys.view(torch.int16), ref.view(torch.int16)))
         del g
         torch.cuda.synchronize(dev)
+        # exchange over NVLink peer memory, eager and captured
+        got = epm.forward_p2p(xt)
+        epm._p2p[xt.shape[0]].check_status()
+        out[(rank, "p2p")] = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        epm.forward_p2p(xs)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ys = epm.forward_p2p(xs)
+        for _ in range(3):
+            g.replay()
+        epm._p2p[xs.shape[0]].check_status()
+        out[(rank, "p2p_graph")] = bool(torch.equal(ys.view(torch.int16), ref.view(torch.int16)))
+        del g
+        epm.close()
         del epm
     finally:
         dist.destroy_process_group()
@@ -92,7 +107,8 @@ def test_ep_world1_equals_single_gpu(tokens):
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_run, args=(1, _port(), tokens, out), nprocs=1, join=True)
-    assert dict(out) == {(0, "bf16"): True, (0, "a4w4"): True, (0, "static"): True, (0, "graph"): True}
+    assert dict(out) == {(0, "bf16"): True, (0, "a4w4"): True, (0, "static"): True, (0, "graph"): True,
+                         (0, "p2p"): True, (0, "p2p_graph"): True}
 
 
 def test_ep_world2_equals_single_gpu():
@@ -101,7 +117,7 @@ def test_ep_world2_equals_single_gpu():
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_run, args=(2, _port(), 33, out), nprocs=2, join=True)
-    assert all(out.values()) and len(out) == 8
+    assert all(out.values()) and len(out) == 12
 
 
 @pytest.mark.parametrize("world,tokens,topk", [(2, 33, 8), (8, 64, 8), (4, 300, 6)])
