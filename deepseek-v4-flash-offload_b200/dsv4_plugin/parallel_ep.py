@@ -186,7 +186,8 @@ class P2PExchange:
         mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(self.device)
         every = torch.empty(world * nb, dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(every, mine, group=group)
-        check(lib().dsv4_ep_connect(self._h, every.cpu().numpy().tobytes()))
+        allh = every.cpu().numpy().tobytes()
+        check(lib().dsv4_ep_connect(self._h, C.create_string_buffer(allh, len(allh))))
         rx, rm, bk = C.c_void_p(), C.c_void_p(), C.c_void_p()
         check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(rm), C.byref(bk)))
         rows = world * self.cap
