@@ -144,3 +144,12 @@ def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk):
     assert torch.equal(dev.send_x.cpu()[valid].view(torch.int16), ref.send_x[valid].view(torch.int16))
     assert torch.equal(dev.order(pos, idx).cpu().to(torch.int64), ord_ref)
     assert int(dev._dev["status"].item()) == 0
+
+
+def test_ep_world4_equals_single_gpu():
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs four GPUs")
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_run, args=(4, _port(), 40, out), nprocs=4, join=True)
+    assert all(out.values()) and len(out) == 24
