@@ -193,6 +193,27 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   const int n_tiles = (*p.n_chunks) * p.a_row_tiles;
   const int k_tiles = p.k_tiles;
   const int step = gridDim.x;
+  constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;  // packed bytes of the 256-row A box
+  // The weights do not depend on the predecessor kernel: the producer puts
+  // the first tile's first ring stages of weights and weight scales in
+  // flight before it waits; that tile's activations follow after the wait.
+  int pre = 0;
+  if (warp == 0 && lane == 0) {
+    const TileInfo first = load_tile(p, blockIdx.x, n_tiles);
+    if (first.slot >= 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint8_t* sf_base = p.arena + (int64_t)first.slot * p.slot_bytes + p.sfa_off;
+      const uint32_t b_tx = (uint32_t)b_rows_for(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
+      pre = k_tiles < C::STAGES ? k_tiles : C::STAGES;
+      for (int kt = 0; kt < pre; ++kt) {   // stage kt, first phase: the ring is empty
+        uint8_t* st = smem + kt * C::STAGE_BYTES;
+        mbar_expect_tx(&full[kt], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+        tma_load_5d(st, &tmA, &full[kt], 0, 0, kt, first.mt, first.slot, pol_w);
+        bulk_load(st + NUM_A * C::A_BYTES + C::B_BYTES,
+                  sf_base + ((int64_t)first.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES, &full[kt], pol_w);
+      }
+    }
+  }
   griddep_wait();
   griddep_launch();
 
@@ -217,22 +238,24 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
         const int nb = b_rows_for(cur.nrows);
         const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmB128));
+        const int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
-            ok = false;
-            break;
-          }
           uint8_t* st = smem + stage * C::STAGE_BYTES;
           uint8_t* sA = st;                        // 256 rows: A0 then A1
           uint8_t* sB = st + NUM_A * C::A_BYTES;
           uint8_t* sSFA = sB + C::B_BYTES;         // 2 x 512 B
           uint8_t* sSFB = sSFA + NUM_A * C::SF_BYTES;
-          constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;  // packed bytes of the 256-row A box
-          const uint32_t b_tx = (uint32_t)nb * (B_FP4 ? G_BK / 2 : G_BK);
-          mbar_expect_tx(&full[stage], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
-          tma_load_5d(sA, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
-          bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES, &full[stage],
-                    pol_w);
+          if (kt >= early) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+              ok = false;
+              break;
+            }
+            const uint32_t b_tx = (uint32_t)nb * (B_FP4 ? G_BK / 2 : G_BK);
+            mbar_expect_tx(&full[stage], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+            tma_load_5d(sA, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
+            bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES,
+                      &full[stage], pol_w);
+          }
           tma_load_2d(sB, mB, &full[stage], kt * G_BK, cur.row0, pol_x);
           // B scales: the atom of (k-tile kt, this 64-row chunk), already in tensor-core order
           bulk_load(sSFB, sfb_base + (int64_t)kt * p.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
