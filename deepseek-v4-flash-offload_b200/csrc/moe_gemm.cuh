@@ -48,28 +48,29 @@ constexpr int G_EPI_WARPS = 8;
 constexpr int G_MMA2_WARP = 2 + G_EPI_WARPS;   // MMA issuer of weight rows 128-255
 constexpr int G_THREADS = 32 * (G_MMA2_WARP + 1);
 constexpr uint32_t G_TMEM_COLS = 512;
-constexpr uint32_t G_SF_COL = 256;   // TMEM columns 256..271: A and B scales of each issuer
 
 enum : int { EPI_SWIGLU_FP8 = 0, EPI_SWIGLU_MXFP4 = 1, EPI_STORE_BF16 = 2 };
 
-// BN = tokens per tile: 64 (decode) or 128 (prefill: twice the work per
-// MMA instruction, whose issue cost does not grow with N up to 128).  With
-// BN = 128 the accumulators (2 halves x 128 columns) fill half of TMEM, so
-// they are single-buffered and the ring has 4 stages.
+// BN = tokens per tile: 64 (decode) or 112 (prefill: 1.75x the work per MMA
+// instruction, whose issue cost does not grow with N).  112 is the widest
+// tile whose two double-buffered accumulators (2 x 2 x 112 = 448 columns)
+// leave room in TMEM for the 16 scale-factor columns, so the epilogue of one
+// tile still overlaps the main loop of the next.
 template <int NUM_A, int BN = G_BN>
 struct GemmCfg {
-  static_assert(BN == 64 || BN == 128, "tile of 64 or 128 tokens");
+  static_assert(BN == 64 || BN == 112, "tile of 64 or 112 tokens");
   static constexpr int A_BYTES = G_BM * G_BK;  // 16 KB (E2M1 expanded to 1 B / element)
-  static constexpr int B_BYTES = BN * G_BK;    // 8 or 16 KB
+  static constexpr int B_BYTES = BN * G_BK;    // 8 or 14 KB
   static constexpr int SF_BYTES = 512;
   static constexpr int STAGE_RAW = NUM_A * A_BYTES + B_BYTES + (NUM_A + 1) * SF_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int STAGES = BN == 64 ? 5 : 4;
-  static constexpr int ACC_BUFS = BN == 64 ? 2 : 1;
+  static constexpr int ACC_BUFS = 2;
+  static constexpr uint32_t SF_COL = ACC_BUFS * NUM_A * BN;   // A and B scales of each issuer: 16 columns
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * BN * 4 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert(ACC_BUFS * NUM_A * BN <= (int)G_SF_COL, "accumulators below the scale columns");
+  static_assert(SF_COL + 16 <= G_TMEM_COLS, "scale columns above the accumulators");
 };
 
 struct GemmParams {
@@ -132,16 +133,17 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
 }
 
 // Activation rows loaded per tile: the chunk's valid rows rounded up to 16,
-// 32, 64 or 128 (decode chunks are mostly short); also the MMA N.
+// 32, 64 or the tile width (decode chunks are mostly short); also the MMA N.
+template <int BN>
 __device__ __forceinline__ int b_rows_for(int nrows) {
-  return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : (nrows <= 64 ? 64 : 128));
+  return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : (nrows <= 64 ? 64 : BN));
 }
 
 template <int NUM_A, bool B_FP4, int EPI, int BN>
 __global__ void __launch_bounds__(G_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB16,
                     const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
-                    const __grid_constant__ CUtensorMap tmB128, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmBwide, const GemmParams p) {
   static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
   using C = GemmCfg<NUM_A, BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     prefetch_tensormap(&tmB16);
     prefetch_tensormap(&tmB32);
     prefetch_tensormap(&tmB64);
-    if (BN == 128) prefetch_tensormap(&tmB128);
+    if (BN > 64) prefetch_tensormap(&tmBwide);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, G_TMEM_COLS);
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (first.slot >= 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint8_t* sf_base = p.arena + (int64_t)first.slot * p.slot_bytes + p.sfa_off;
-      const uint32_t b_tx = (uint32_t)b_rows_for(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
+      const uint32_t b_tx = (uint32_t)b_rows_for<BN>(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
       pre = k_tiles < C::STAGES ? k_tiles : C::STAGES;
       for (int kt = 0; kt < pre; ++kt) {   // stage kt, first phase: the ring is empty
         uint8_t* st = smem + kt * C::STAGE_BYTES;
@@ -236,8 +238,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         const uint8_t* sf_base = p.arena + (int64_t)cur.slot * p.slot_bytes + p.sfa_off;
         const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
-        const int nb = b_rows_for(cur.nrows);
-        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmB128));
+        const int nb = b_rows_for<BN>(cur.nrows);
+        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmBwide));
         const int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
         for (int kt = 0; kt < k_tiles; ++kt) {
           uint8_t* st = smem + stage * C::STAGE_BYTES;
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       bool ok = true;
       // each issuer copies the scales it reads into its own TMEM columns:
       // tcgen05 operations of different threads are not ordered
-      const uint32_t sfa = tmem + G_SF_COL + 8 * half, sfb = tmem + G_SF_COL + 8 * half + 4;
+      const uint32_t sfa = tmem + C::SF_COL + 8 * half, sfb = tmem + C::SF_COL + 8 * half + 4;
       TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
       for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
         const TileInfo nxt = load_tile(p, t + step, n_tiles);
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           cur = nxt;
           continue;
         }
-        const int nb = b_rows_for(cur.nrows);
+        const int nb = b_rows_for<BN>(cur.nrows);
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
@@ -361,7 +363,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     int abuf = 0;
     uint32_t aphase = 0;
     float w[SUB];
-    // route weights of 32 rows starting at cs (row0 + cs is a multiple of 32)
+    // route weights of 32 rows starting at cs (row0 + cs is a multiple of 8;
+    // the sorted-weight buffer has a tile of slack after its last group)
     auto load_w = [&](int row0, int cs) {
       if constexpr (EPI != EPI_STORE_BF16) {
         const float4* wp = reinterpret_cast<const float4*>(p.sorted_w + row0 + cs);
@@ -392,21 +395,29 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       if (*reinterpret_cast<volatile int*>(epi_fail) != 0) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)abuf * (NUM_A * BN) + c0;
-#pragma unroll 1
-      for (int sub = 0; sub < HALF / SUB; ++sub) {
+      constexpr int NPASS = (HALF + SUB - 1) / SUB;
+#pragma unroll
+      for (int sub = 0; sub < NPASS; ++sub) {
         const int cs = c0 + sub * SUB;   // first column of this pass
+        const int width = HALF - sub * SUB < SUB ? HALF - sub * SUB : SUB;   // 32, or 24 (BN = 112)
         if (sub > 0) load_w(row0, cs);
         float acc0[SUB];
         float acc1[NUM_A == 2 ? SUB : 1];
         (void)acc1;
-#pragma unroll
-        for (int j = 0; j < SUB / 16; ++j) tmem_ld16(tbase + sub * SUB + j * 16, acc0 + j * 16);
+        tmem_ld16(tbase + sub * SUB, acc0);
+        if (width == 32)
+          tmem_ld16(tbase + sub * SUB + 16, acc0 + 16);
+        else
+          tmem_ld8(tbase + sub * SUB + 16, acc0 + 16);
         if constexpr (NUM_A == 2) {
-#pragma unroll
-          for (int j = 0; j < SUB / 16; ++j) tmem_ld16(tbase + BN + sub * SUB + j * 16, acc1 + j * 16);
+          tmem_ld16(tbase + BN + sub * SUB, acc1);
+          if (width == 32)
+            tmem_ld16(tbase + BN + sub * SUB + 16, acc1 + 16);
+          else
+            tmem_ld8(tbase + BN + sub * SUB + 16, acc1 + 16);
         }
         tc_wait_ld();
-        if (sub == HALF / SUB - 1) {   // this tile's accumulators are read out
+        if (sub == NPASS - 1) {   // this tile's accumulators are read out
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&accempty[abuf]);
@@ -417,12 +428,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           uint16_t* dst = p.out_bf16 + (int64_t)(row0 + cs) * p.out_ld + mt * p.out_tile_cols + i;
 #pragma unroll
           for (int n = 0; n < SUB; ++n)
-            if (cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+            if (n < width && cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
           if constexpr (NUM_A == 2) {
             uint16_t* dst1 = dst + G_BM;
 #pragma unroll
             for (int n = 0; n < SUB; ++n)
-              if (cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+              if (n < width && cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
           }
         } else {
           // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
@@ -444,24 +455,27 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             float mine = 0.f;
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
-              const float m = warp_max_nonneg(fabsf(acc0[n]));
-              if (lane == n) mine = m;
+              if (n < width) {
+                const float m = warp_max_nonneg(fabsf(acc0[n]));
+                if (lane == n) mine = m;
+              }
             }
-            red[q * BN + cs + lane] = mine;
+            if (lane < width) red[q * BN + cs + lane] = mine;
             named_bar_sync(1, 32 * G_EPI_WARPS);
-            const float amax_l = fmaxf(fmaxf(red[cs + lane], red[BN + cs + lane]),
-                                       fmaxf(red[2 * BN + cs + lane], red[3 * BN + cs + lane]));
+            const float amax_l = lane < width ? fmaxf(fmaxf(red[cs + lane], red[BN + cs + lane]),
+                                                      fmaxf(red[2 * BN + cs + lane], red[3 * BN + cs + lane]))
+                                              : 0.f;
             const int e_l = fp8_scale_exp(amax_l);
             uint8_t* dst = p.out_q + (int64_t)(row0 + cs) * p.out_ld + mt * G_BM + i;
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
               const int e = __shfl_sync(0xffffffffu, e_l, n);
-              if (cs + n < nrows) {
+              if (n < width && cs + n < nrows) {
                 const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
                 dst[(int64_t)n * p.out_ld] = (uint8_t)e4m3_byte(v);
               }
             }
-            if (q == 0 && cs + lane < nrows) {
+            if (q == 0 && lane < width && cs + lane < nrows) {
               const int n = cs + lane;
               *reinterpret_cast<uint32_t*>(p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + (n & 31) * 16 +
                                            (n >> 5) * 4) = (uint32_t)(e_l + 127) * 0x01010101u;
@@ -473,7 +487,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             uint8_t* sfd = p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + q;
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
-              if (cs + n < nrows) {
+              if (n < width && cs + n < nrows) {
                 const float amax = warp_max_nonneg(fabsf(acc0[n]));
                 const int e = mx_scale_exp(amax);
                 const uint32_t code = e2m1_code(acc0[n] * pow2_any(-e));

@@ -24,7 +24,7 @@ namespace dsv4 {
 // and each chunk is one pad-row block of one expert.
 // ---------------------------------------------------------------------------
 constexpr int AL_THREADS = 1024;
-constexpr int GEMM_BN_MAX = 128;   // largest GEMM tile (tokens per expert chunk)
+constexpr int GEMM_BN_MAX = 128;   // bound on the GEMM tile (64 or 112 tokens per expert chunk)
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
   // scratch: 32 ints.  All 1024 threads participate.
@@ -279,13 +279,14 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 // writes token t's row to its sorted row inv[a] (padding rows are never
 // touched; invalid assignments, inv < 0, are skipped).  Scales
 // go to 512-byte atoms, one per (128-column k-tile kt, 64-row block rb) at
-// (kt * rb_cap + rb) * 512 for BN-row blocks (BN = 64 or 128, the GEMM
-// tile), row n of the block at (n%32)*16 + (n/32)*4, one
+// (kt * rb_cap + rb) * 512 for BN-row blocks (BN = 64 or 112, the GEMM
+// tile), row n of the block (n = row % BN) at (n%32)*16 + (n/32)*4, one
 // byte per 32-block (FP8: the per-128 exponent replicated four times): the
 // order the tensor cores read after a 32x128b.warpx4 copy.
 // ---------------------------------------------------------------------------
 __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, int64_t rb_cap, int bn) {
-  return ((int64_t)kt * rb_cap + row / bn) * 512 + (row % 32) * 16 + ((row % bn) / 32) * 4;
+  const int n = (int)(row % bn);   // row inside its tile (tiles of 112 rows do not start on a 32-row boundary)
+  return ((int64_t)kt * rb_cap + row / bn) * 512 + (n % 32) * 16 + (n / 32) * 4;
 }
 
 // One warp per (token, 128-column block): the token's row is read and
@@ -390,6 +391,9 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
     }
     pos[i] = v;
   }
+  // a token without any assignment (every id -1: padding of the expert-
+  // parallel exchange) has no output row to write
+  if (k == 0) return;
   for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < H; c += gridDim.y * blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
@@ -484,8 +488,8 @@ static int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
 static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens) {
   WsLayout w;
   w.p_max = max_tokens * topk;
-  // every expert group is padded to a multiple of the GEMM tile (64 or 128
-  // rows): room for the larger padding
+  // every expert group is padded to a multiple of the GEMM tile (64 or 112
+  // rows): room for padding up to 128 rows, and a tile of slack at the end
   w.p_cap = (w.p_max + (GEMM_BN_MAX - 1) * std::min<int64_t>(E, w.p_max) + GEMM_BN_MAX - 1) / GEMM_BN_MAX *
                 GEMM_BN_MAX + GEMM_BN_MAX;
   w.max_chunks = w.p_cap / G_BN + 1;
@@ -528,7 +532,7 @@ struct dsv4_moe_plan {
   uint8_t* ws = nullptr;
   dsv4::WsLayout wl;
   CUtensorMap tmA13, tmA2;
-  CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 128 activation rows per box
+  CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 112 activation rows per box
   bool timing = false;
   int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -557,23 +561,22 @@ template <int NUM_A, bool B_FP4, int EPI>
 static int prepare_gemm() {
   DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 64>::SMEM_BYTES));
-  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 128>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 128>::SMEM_BYTES));
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 112>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 112>::SMEM_BYTES));
   return DSV4_OK;
 }
 
 // The GEMM tile: the plan's setting, else the environment's
-// (DSV4_GEMM_BN=64|128), else 64 tokens.  A 128-token tile halves the MMA
-// instructions per token but single-buffers the accumulators, so the
-// SwiGLU epilogue no longer overlaps the next tile; on config 2 (2048
-// tokens, a4w4) it measured slower than 64, hence the default.
+// (DSV4_GEMM_BN=64|112), else 64 tokens.  A 112-token tile issues 1.75x
+// fewer MMA instructions per token than a 64-token one, at the cost of more
+// padding rows per expert group.
 static int gemm_bn(int plan_bn) {
   static const int env_bn = [] {
     const char* e = getenv("DSV4_GEMM_BN");
     return e ? atoi(e) : 0;
   }();
-  if (plan_bn == 64 || plan_bn == 128) return plan_bn;
-  if (env_bn == 64 || env_bn == 128) return env_bn;
+  if (plan_bn == 64 || plan_bn == 112) return plan_bn;
+  if (env_bn == 64 || env_bn == 112) return env_bn;
   return 64;
 }
 
@@ -581,8 +584,8 @@ template <bool B_FP4, int EPI>
 static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, const CUtensorMap& tmA,
                                const CUtensorMap* tmB, const GemmParams& g) {
   const dim3 grid(num_sms), block(G_THREADS);
-  if (bn == 128)
-    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 128>, grid, block, GemmCfg<2, 128>::SMEM_BYTES, st, pdl, tmA,
+  if (bn == 112)
+    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112>, grid, block, GemmCfg<2, 112>::SMEM_BYTES, st, pdl, tmA,
                     tmB[0], tmB[1], tmB[2], tmB[3], g);
   return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64>::SMEM_BYTES, st, pdl, tmA,
                   tmB[0], tmB[1], tmB[2], tmB[2], g);
@@ -635,7 +638,7 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
     const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA2, U4, 5, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
   }
-  const uint32_t brows[4] = {16, 32, 64, 128};
+  const uint32_t brows[4] = {16, 32, 64, 112};
   for (int j = 0; j < 4; ++j) {
     const uint32_t bbox[2] = {G_BK, brows[j]};
     {
@@ -697,7 +700,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
                            wsp<int4>(p, w.chunks), n_chunks, bn, status));
   mark(1);
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
-  const int64_t rb_cap = w.p_cap / bn;   // BN-row scale blocks per k-tile
+  const int64_t rb_cap = (w.p_cap + bn - 1) / bn;   // BN-row scale blocks per k-tile
   {
     const int64_t warps = n_tokens * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
@@ -772,8 +775,8 @@ extern "C" int dsv4_moe_enable_timing(dsv4_moe_plan* p, int32_t enable) {
 extern "C" int dsv4_moe_set_gemm_tile(dsv4_moe_plan* p, int32_t tokens_per_tile) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(p, "null plan");
-  DSV4_CHECK_ARG(tokens_per_tile == 0 || tokens_per_tile == 64 || tokens_per_tile == 128,
-                 "tokens per GEMM tile must be 0 (default), 64 or 128");
+  DSV4_CHECK_ARG(tokens_per_tile == 0 || tokens_per_tile == 64 || tokens_per_tile == 112,
+                 "tokens per GEMM tile must be 0 (default), 64 or 112");
   p->gemm_tile = tokens_per_tile;
   DSV4_API_END
 }

@@ -248,7 +248,7 @@ class MoEPlan:
     STAGES = ("align", "quant_gather", "gate_up_gemm", "down_gemm", "combine")
 
     def set_gemm_tile(self, tokens_per_tile: int = 0) -> None:
-        """Tokens per GEMM tile: 64, 128, or 0 for the library default."""
+        """Tokens per GEMM tile: 64, 112, or 0 for the library default."""
         check(lib().dsv4_moe_set_gemm_tile(self._h, int(tokens_per_tile)))
 
     def enable_timing(self, enable: bool = True) -> None:

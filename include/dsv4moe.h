@@ -138,7 +138,9 @@ int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t topk, int32
  * route weight and activation re-quant -> down GEMM -> deterministic
  * combine (ascending expert order per token, fp32) -> y bf16 [T, H].
  * route_weights/route_indices are the router outputs [T, k];
- * slot_of_expert[e] is the arena slot holding expert e (or -1).
+ * slot_of_expert[e] is the arena slot holding expert e (or -1).  A token
+ * whose k indices are all -1 (empty assignments) gets no output row: its
+ * row of y is left as it was.
  * ------------------------------------------------------------------------ */
 typedef struct dsv4_moe_plan dsv4_moe_plan;
 int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
@@ -168,7 +170,7 @@ int dsv4_moe_combine_ordered(const void* rows_bf16, const int32_t* order, int64_
  * [4] combine. */
 int dsv4_moe_enable_timing(dsv4_moe_plan* plan, int32_t enable);
 int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
-/* Tokens per GEMM tile (no counterpart in the reference): 64 or 128, or 0
+/* Tokens per GEMM tile (no counterpart in the reference): 64 or 112, or 0
  * for the library's choice (64; the environment variable DSV4_GEMM_BN
  * overrides it).  The tile is also the padding of each expert's row group.
  * Takes effect from the next dsv4_moe_forward on the plan. */

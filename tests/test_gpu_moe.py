@@ -138,14 +138,15 @@ def test_cfg1_decode_matches_oracle(ops, layer1, T):
 
 
 @pytest.mark.parametrize("T", [40, 256, 700])
-def test_cfg0_gemm_tile_of_128_tokens(ops, layer0, T):
-    """With a 128-token GEMM tile expert groups are padded to 128 rows and
-    chunks of up to 128 rows run as one MMA N."""
+def test_cfg0_gemm_tile_of_112_tokens(ops, layer0, T):
+    """With a 112-token GEMM tile expert groups are padded to 112 rows and
+    chunks of up to 112 rows run as one MMA N (the epilogue's second pass of
+    each warp is 24 columns wide)."""
     L = layer0
     x = S.make_tokens(L.cfg, 300 + T, T)
     w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
     plan = _plan(ops, L, T)
-    plan.set_gemm_tile(128)
+    plan.set_gemm_tile(112)
     for profile in ("bf16", "a4w4"):
         y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
                          L.slot_of, profile)
@@ -153,6 +154,6 @@ def test_cfg0_gemm_tile_of_128_tokens(ops, layer0, T):
         assert rel_err(bf16_to_np(y), L.oracle(x, w, idx, profile)) <= TOL, profile
     d = plan.debug_align(T)
     starts = d["offsets"].numpy()[:-1]
-    assert np.all(starts % 128 == 0)
+    assert np.all(starts % 112 == 0)
     ref = O.moe_align(idx, L.n)
     assert np.array_equal(np.argsort(d["inv"].numpy(), kind="stable"), ref["order"])
