@@ -117,8 +117,10 @@ __device__ __forceinline__ float pow2_any(int k) {
 // zero results carry no sign bit.
 __device__ __forceinline__ uint32_t e2m1_code(float x) {
   float a = fminf(fabsf(x), 6.0f);
-  float q = a < 2.0f ? 0.5f : (a < 4.0f ? 1.0f : 2.0f);
-  float r = fminf(rintf(a / q) * q, 6.0f);
+  // grid step q = 0.5, 1 or 2: a / q is a * (1 / q), exact for powers of two
+  const float q = a < 2.0f ? 0.5f : (a < 4.0f ? 1.0f : 2.0f);
+  const float inv_q = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
+  float r = fminf(rintf(a * inv_q) * q, 6.0f);
   int t = (int)(r * 2.0f);  // 0,1,2,3,4,6,8,12
   uint32_t mag = t <= 4 ? (uint32_t)t : (t == 6 ? 5u : (t == 8 ? 6u : 7u));
   return (x < 0.0f && mag != 0u) ? (mag | 8u) : mag;
@@ -290,6 +292,18 @@ __device__ __forceinline__ void tc_mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// Packed E2M1 x E2M1 (two elements per byte in shared memory), 64 of K per
+// instruction, one E8M0 scale per 32 elements (two per row per instruction).
+__device__ __forceinline__ void tc_mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate, uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 8 consecutive 32-bit columns -> 8 registers per thread.
@@ -324,6 +338,17 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   d |= (uint64_t)2u << 61;
   return d;
 }
+// K-major, 64-byte swizzle: 8-row atoms of 64 B, atoms 512 B apart (packed
+// E2M1: 128 elements per row).
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)4u << 61;
+  return d;
+}
 // Descriptor of a 32-row x 16-byte scale-factor block (no swizzle, 8-row
 // core matrices 128 B apart), the source of tc_cp_sf.
 __device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
@@ -340,6 +365,20 @@ __host__ __device__ __forceinline__ uint32_t idesc_mxf8f6f4(int n, bool b_fp4, u
   d |= (sf_id & 3u) << 4;              // B scale-factor id
   d |= 5u << 7;                        // A format E2M1
   d |= (b_fp4 ? 5u : 0u) << 10;        // B format E2M1 / E4M3
+  d |= ((uint32_t)(n >> 3) & 63u) << 17;
+  d |= 1u << 23;                       // scale format UE8M0
+  d |= (128u >> 4) << 24;              // M = 128
+  d |= (sf_id & 3u) << 29;             // A scale-factor id
+  return d;
+}
+// Instruction descriptor of kind::mxf4.block_scale.scale_vec::2X: A = B =
+// E2M1 (format code 1 of this kind), M = 128, E8M0 scales, both K-major;
+// sf_id 0 or 2 picks the scale byte pair of the 64-element K step.
+__host__ __device__ __forceinline__ uint32_t idesc_mxf4(int n, uint32_t sf_id) {
+  uint32_t d = 0;
+  d |= (sf_id & 3u) << 4;              // B scale-factor id
+  d |= 1u << 7;                        // A format E2M1
+  d |= 1u << 10;                       // B format E2M1
   d |= ((uint32_t)(n >> 3) & 63u) << 17;
   d |= 1u << 23;                       // scale format UE8M0
   d |= (128u >> 4) << 24;              // M = 128

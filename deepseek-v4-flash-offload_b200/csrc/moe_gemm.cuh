@@ -10,9 +10,12 @@
 // them to the one-byte-per-element shared-memory form the f8f6f4 tensor-core
 // path reads), with their E8M0 per-32 scales;
 // B = E4M3 activations (bf16 profile) or E2M1 activations (a4w4), with E8M0
-// per-32 scales.  One tcgen05.mma.kind::mxf8f6f4.block_scale per 32 of K.
-// The products equal those of bf16(dequant(W)) x bf16(fp8_roundtrip(X)) of
-// the reference exactly, so only accumulation order differs.
+// per-32 scales.  bf16 profile: one tcgen05.mma.kind::mxf8f6f4.block_scale
+// per 32 of K.  a4w4: both operands stay packed (two E2M1 per byte, TMA
+// type UINT8 with a 64-byte swizzle) and one kind::mxf4.block_scale per 64
+// of K, half the instructions and half the shared-memory bytes per product.
+// The products equal those of the reference's dequantised operands exactly,
+// so only accumulation order differs.
 //
 // Decode MMAs are tiny (N = 16 tokens).  A tcgen05 instruction costs the
 // thread that issues it about 60-70 cycles whatever N is (up to 128), while
@@ -56,19 +59,25 @@ enum : int { EPI_SWIGLU_FP8 = 0, EPI_SWIGLU_MXFP4 = 1, EPI_STORE_BF16 = 2 };
 // tile whose two double-buffered accumulators (2 x 2 x 112 = 448 columns)
 // leave room in TMEM for the 16 scale-factor columns, so the epilogue of one
 // tile still overlaps the main loop of the next.
-template <int NUM_A, int BN = G_BN>
+// With packed operands (PACKED: the a4w4 profile) a stage is 22-25 KB
+// instead of 42-48 KB, so the ring is 8 stages deep.
+template <int NUM_A, int BN = G_BN, bool PACKED = false>
 struct GemmCfg {
   static_assert(BN == 64 || BN == 112, "tile of 64 or 112 tokens");
-  static constexpr int A_BYTES = G_BM * G_BK;  // 16 KB (E2M1 expanded to 1 B / element)
-  static constexpr int B_BYTES = BN * G_BK;    // 8 or 14 KB
+  static constexpr int ROW_BYTES = PACKED ? G_BK / 2 : G_BK;   // shared-memory bytes per row of a k-tile
+  static constexpr int A_BYTES = G_BM * ROW_BYTES;  // 8 KB packed, 16 KB with E2M1 expanded to 1 B / element
+  static constexpr int B_BYTES = BN * ROW_BYTES;
   static constexpr int SF_BYTES = 512;
   static constexpr int STAGE_RAW = NUM_A * A_BYTES + B_BYTES + (NUM_A + 1) * SF_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int STAGES = BN == 64 ? 5 : 4;
+  static constexpr int STAGES = PACKED ? 8 : (BN == 64 ? 5 : 4);
   static constexpr int ACC_BUFS = 2;
   static constexpr uint32_t SF_COL = ACC_BUFS * NUM_A * BN;   // A and B scales of each issuer: 16 columns
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 4 * BN * 4 + 1024;
+  static constexpr int RED_BYTES = 4 * BN * 4;                   // per-column amax of each lane quarter
+  static constexpr int XPOSE_STRIDE = 36;                         // bytes per column row (32 + 4: no bank conflicts)
+  static constexpr int XPOSE_BYTES = G_EPI_WARPS * 32 * XPOSE_STRIDE;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + RED_BYTES + XPOSE_BYTES + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(SF_COL + 16 <= G_TMEM_COLS, "scale columns above the accumulators");
 };
@@ -134,6 +143,29 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
 
 // Activation rows loaded per tile: the chunk's valid rows rounded up to 16,
 // 32, 64 or the tile width (decode chunks are mostly short); also the MMA N.
+// Column maxima of |h[n]| over a warp's 32 lanes, all 32 columns at once:
+// five butterfly rounds each halve the columns a lane keeps (16, 8, 4, 2,
+// 1) while exchanging the other half with its partner, so 31 shuffles
+// leave lane L with column L's maximum.  The maximum is taken on the bit
+// patterns (non-negative floats order like unsigned integers), as
+// warp_max_nonneg does.  v is scratch (overwritten).
+__device__ __forceinline__ float column_amax_transposed(const float* h, float* v, int lane) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) u[n] = __float_as_uint(fabsf(h[n]));
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < s; ++j) {
+      const uint32_t send = upper ? u[j] : u[j + s];
+      const uint32_t keep = upper ? u[j + s] : u[j];
+      u[j] = max(keep, __shfl_xor_sync(0xffffffffu, send, s));
+    }
+  }
+  return __uint_as_float(u[0]);
+}
+
 template <int BN>
 __device__ __forceinline__ int b_rows_for(int nrows) {
   return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : (nrows <= 64 ? 64 : BN));
@@ -145,7 +177,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
                     const __grid_constant__ CUtensorMap tmBwide, const GemmParams p) {
   static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
-  using C = GemmCfg<NUM_A, BN>;
+  using C = GemmCfg<NUM_A, BN, B_FP4>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -157,6 +189,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   int* epi_fail = reinterpret_cast<int*>(tmem_holder + 1);
   float* red = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);  // [4][BN]
+  uint8_t* xpose_all = smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES + C::RED_BYTES;  // [8 warps][32][36]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -258,7 +291,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES,
                       &full[stage], pol_w);
           }
-          tma_load_2d(sB, mB, &full[stage], kt * G_BK, cur.row0, pol_x);
+          tma_load_2d(sB, mB, &full[stage], kt * C::ROW_BYTES, cur.row0, pol_x);
           // B scales: the atom of (k-tile kt, this 64-row chunk), already in tensor-core order
           bulk_load(sSFB, sfb_base + (int64_t)kt * p.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
           mbar_arrive(&full[stage]);
@@ -323,14 +356,27 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const uint32_t aSFB = aB + C::B_BYTES + NUM_A * C::SF_BYTES;
           tc_cp_sf(sfa, desc_sf(aSFA));
           tc_cp_sf(sfb, desc_sf(aSFB));
-          const uint64_t dA = desc_sw128(aA), dB = desc_sw128(aB);
+          if constexpr (B_FP4) {
+            const uint64_t dA = desc_sw64(aA), dB = desc_sw64(aB);
 #pragma unroll
-          for (int kb = 0; kb < G_BK / 32; ++kb) {
-            const uint32_t idesc = idesc_mxf8f6f4(nb, B_FP4, (uint32_t)kb);
-            const uint32_t sel = (uint32_t)kb << 30;
-            const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
-            // +32 bytes of K per step inside the 128-byte swizzle row
-            tc_mma_mxf8f6f4(d, dA + 2u * kb, dB + 2u * kb, idesc, acc, sfa | sel, sfb | sel);
+            for (int kb = 0; kb < G_BK / 64; ++kb) {
+              // scale bytes 2kb, 2kb+1 of each row's 32-bit column: sf_id 0 or 2
+              const uint32_t idesc = idesc_mxf4(nb, 2u * kb);
+              const uint32_t sel = (2u * kb) << 30;
+              const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
+              // +32 bytes (64 packed elements) of K per step inside the 64-byte swizzle row
+              tc_mma_mxf4(d, dA + 2u * kb, dB + 2u * kb, idesc, acc, sfa | sel, sfb | sel);
+            }
+          } else {
+            const uint64_t dA = desc_sw128(aA), dB = desc_sw128(aB);
+#pragma unroll
+            for (int kb = 0; kb < G_BK / 32; ++kb) {
+              const uint32_t idesc = idesc_mxf8f6f4(nb, false, (uint32_t)kb);
+              const uint32_t sel = (uint32_t)kb << 30;
+              const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
+              // +32 bytes of K per step inside the 128-byte swizzle row
+              tc_mma_mxf8f6f4(d, dA + 2u * kb, dB + 2u * kb, idesc, acc, sfa | sel, sfb | sel);
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -360,6 +406,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int half = (warp - 2) >> 2;  // which half of the BN columns
     const int i = q * 32 + lane;       // row inside the 128-row tile
     const int c0 = half * HALF;        // first column of this warp
+    uint8_t* xpose = xpose_all + (warp - 2) * 32 * C::XPOSE_STRIDE;   // [column][row] bytes of this warp
     int abuf = 0;
     uint32_t aphase = 0;
     float w[SUB];
@@ -417,6 +464,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             tmem_ld8(tbase + BN + sub * SUB + 16, acc1 + 16);
         }
         tc_wait_ld();
+        if (width < SUB) {   // columns past the pass width were not loaded
+#pragma unroll
+          for (int n = 0; n < SUB; ++n)
+            if (n >= width) acc0[n] = acc1[n] = 0.f;
+        }
         if (sub == NPASS - 1) {   // this tile's accumulators are read out
           tc_fence_before();
           __syncwarp();
@@ -452,29 +504,29 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if constexpr (EPI == EPI_SWIGLU_FP8) {
             // per-token amax over the 128 rows of this tile = one 128-block of I:
             // redux over the warp's 32 rows, then across the 4 lane quarters
-            float mine = 0.f;
-#pragma unroll
-            for (int n = 0; n < SUB; ++n) {
-              if (n < width) {
-                const float m = warp_max_nonneg(fabsf(acc0[n]));
-                if (lane == n) mine = m;
-              }
-            }
+            // lane L: max |h| of column cs+L over the warp's 32 rows
+            const float mine = column_amax_transposed(acc0, acc1, lane);
             if (lane < width) red[q * BN + cs + lane] = mine;
             named_bar_sync(1, 32 * G_EPI_WARPS);
             const float amax_l = lane < width ? fmaxf(fmaxf(red[cs + lane], red[BN + cs + lane]),
                                                       fmaxf(red[2 * BN + cs + lane], red[3 * BN + cs + lane]))
                                               : 0.f;
             const int e_l = fp8_scale_exp(amax_l);
-            uint8_t* dst = p.out_q + (int64_t)(row0 + cs) * p.out_ld + mt * G_BM + i;
+            // E4M3 bytes into [column][row], then lane L stores column L's 32 bytes
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
               const int e = __shfl_sync(0xffffffffu, e_l, n);
-              if (n < width && cs + n < nrows) {
-                const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
-                dst[(int64_t)n * p.out_ld] = (uint8_t)e4m3_byte(v);
-              }
+              const float v = fminf(fmaxf(acc0[n] * pow2i(-e), -448.f), 448.f);
+              xpose[n * C::XPOSE_STRIDE + lane] = (uint8_t)e4m3_byte(v);
             }
+            __syncwarp();
+            if (lane < width && cs + lane < nrows) {
+              const uint32_t* src = reinterpret_cast<const uint32_t*>(xpose + lane * C::XPOSE_STRIDE);
+              uint4* dst = reinterpret_cast<uint4*>(p.out_q + (int64_t)(row0 + cs + lane) * p.out_ld + mt * G_BM + q * 32);
+              dst[0] = make_uint4(src[0], src[1], src[2], src[3]);
+              dst[1] = make_uint4(src[4], src[5], src[6], src[7]);
+            }
+            __syncwarp();
             if (q == 0 && lane < width && cs + lane < nrows) {
               const int n = cs + lane;
               *reinterpret_cast<uint32_t*>(p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + (n & 31) * 16 +
@@ -482,21 +534,35 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
             named_bar_sync(1, 32 * G_EPI_WARPS);
           } else {
-            // per-token amax over the 32 rows of this warp = one 32-block of I
-            uint8_t* dst = p.out_q + (int64_t)(row0 + cs) * (p.out_ld / 2) + (mt * G_BM + i) / 2;
-            uint8_t* sfd = p.out_sf + ((int64_t)mt * p.rb_cap + row0 / BN) * 512 + q;
+            // per-token amax over the 32 rows of this warp = one 32-block of I;
+            // lane L holds column cs+L's
+            const int e_l = mx_scale_exp(column_amax_transposed(acc0, acc1, lane));
+            const bool col_ok = lane < width && cs + lane < nrows;
+            if (col_ok) {
+              const int cn = cs + lane;
+              p.out_sf[((int64_t)mt * p.rb_cap + row0 / BN) * 512 + q + (cn & 31) * 16 + (cn >> 5) * 4] =
+                  (uint8_t)(e_l + 127);
+            }
+            // E2M1 codes into [column][row], then lane L packs column L's 32
+            // rows two per byte (even row in the low nibble) and stores 16 B
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
-              if (n < width && cs + n < nrows) {
-                const float amax = warp_max_nonneg(fabsf(acc0[n]));
-                const int e = mx_scale_exp(amax);
-                const uint32_t code = e2m1_code(acc0[n] * pow2_any(-e));
-                const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
-                if ((lane & 1) == 0) dst[(int64_t)n * (p.out_ld / 2)] = (uint8_t)(code | (hi << 4));
-                const int cn = cs + n;
-                if (lane == 0) sfd[(cn & 31) * 16 + (cn >> 5) * 4] = (uint8_t)(e + 127);
-              }
+              const int e = __shfl_sync(0xffffffffu, e_l, n);
+              xpose[n * C::XPOSE_STRIDE + lane] = (uint8_t)e2m1_code(acc0[n] * pow2_any(-e));
             }
+            __syncwarp();
+            if (col_ok) {
+              const uint32_t* src = reinterpret_cast<const uint32_t*>(xpose + lane * C::XPOSE_STRIDE);
+              uint32_t o[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t t0 = src[2 * k] | (src[2 * k] >> 4), t1 = src[2 * k + 1] | (src[2 * k + 1] >> 4);
+                o[k] = __byte_perm(t0, t1, 0x6420);
+              }
+              *reinterpret_cast<uint4*>(p.out_q + (int64_t)(row0 + cs + lane) * (p.out_ld / 2) + (mt * G_BM + q * 32) / 2) =
+                  make_uint4(o[0], o[1], o[2], o[3]);
+            }
+            __syncwarp();
           }
         }
       }

@@ -459,7 +459,8 @@ static EncodeTiledFn get_encoder() {
 }
 
 static int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
+                    const uint64_t* strides_bytes, const uint32_t* box, const char* what,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = get_encoder();
   if (!enc) return fail(DSV4_ECUDA, "cuTensorMapEncodeTiled is not available");
   cuuint64_t d[5], s[4];
@@ -470,8 +471,8 @@ static int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base
     es[i] = 1;
     if (i < rank - 1) s[i] = strides_bytes[i];
   }
-  CUresult r = enc(m, dt, (cuuint32_t)rank, base, d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(m, dt, (cuuint32_t)rank, base, d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DSV4_ECUDA, std::string("tensor map encode failed for ") + what +
                                                      " (CUresult " + std::to_string((int)r) + ")");
   return DSV4_OK;
@@ -531,7 +532,8 @@ struct dsv4_moe_plan {
   dsv4::SlotLayout slot;
   uint8_t* ws = nullptr;
   dsv4::WsLayout wl;
-  CUtensorMap tmA13, tmA2;
+  CUtensorMap tmA13, tmA2;      // weights expanded to one byte per element (bf16 profile)
+  CUtensorMap tmA13p, tmA2p;    // weights packed, two per byte (a4w4)
   CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 112 activation rows per box
   bool timing = false;
   int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
@@ -560,24 +562,29 @@ extern "C" int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32
 template <int NUM_A, bool B_FP4, int EPI>
 static int prepare_gemm() {
   DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 64>::SMEM_BYTES));
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GemmCfg<NUM_A, 64, B_FP4>::SMEM_BYTES));
   DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 112>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<NUM_A, 112>::SMEM_BYTES));
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GemmCfg<NUM_A, 112, B_FP4>::SMEM_BYTES));
   return DSV4_OK;
 }
 
 // The GEMM tile: the plan's setting, else the environment's
-// (DSV4_GEMM_BN=64|112), else 64 tokens.  A 112-token tile issues 1.75x
+// (DSV4_GEMM_BN=64|112), else by batch size.  A 112-token tile issues 1.75x
 // fewer MMA instructions per token than a 64-token one, at the cost of more
-// padding rows per expert group.
-static int gemm_bn(int plan_bn) {
+// padding rows per expert group (and, with FP8 activations, a 4-stage ring
+// instead of 5).  Decode batches (a few rows per expert) take 64; from 16
+// assignments per expert on average (T = 512 at top-8 of 256) the wide
+// tile, measured 1.08x faster on the a4w4 layer at T = 512, 1.17x at 2048.
+static int gemm_bn(int plan_bn, int64_t assignments, int n_experts) {
   static const int env_bn = [] {
     const char* e = getenv("DSV4_GEMM_BN");
     return e ? atoi(e) : 0;
   }();
   if (plan_bn == 64 || plan_bn == 112) return plan_bn;
   if (env_bn == 64 || env_bn == 112) return env_bn;
-  return 64;
+  return assignments >= 16 * (int64_t)n_experts ? 112 : 64;
 }
 
 template <bool B_FP4, int EPI>
@@ -585,9 +592,9 @@ static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, c
                                const CUtensorMap* tmB, const GemmParams& g) {
   const dim3 grid(num_sms), block(G_THREADS);
   if (bn == 112)
-    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112>, grid, block, GemmCfg<2, 112>::SMEM_BYTES, st, pdl, tmA,
+    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112>, grid, block, GemmCfg<2, 112, B_FP4>::SMEM_BYTES, st, pdl, tmA,
                     tmB[0], tmB[1], tmB[2], tmB[3], g);
-  return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64>::SMEM_BYTES, st, pdl, tmA,
+  return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64, B_FP4>::SMEM_BYTES, st, pdl, tmA,
                   tmB[0], tmB[1], tmB[2], tmB[2], g);
 }
 
@@ -631,25 +638,38 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
     const uint64_t dims[5] = {128, 256, kt, np, (uint64_t)n_slots}, str[4] = {64, 16384, kt * 16384, SB};
     const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA13, U4, 5, slot_arena + p->slot.w13p, dims, str, box, "w13")) != 0) return rc;
+    const uint64_t dimsp[5] = {64, 256, kt, np, (uint64_t)n_slots};   // packed: 64 bytes per row
+    const uint32_t boxp[5] = {64, 2 * G_BM, 1, 1, 1};
+    if ((rc = make_map(&p->tmA13p, U8, 5, slot_arena + p->slot.w13p, dimsp, str, boxp, "w13 packed",
+                       CU_TENSOR_MAP_SWIZZLE_64B)) != 0)
+      return rc;
   }
   {  // w2: H/256 pairs of 128-row tiles, K = I
     const uint64_t kt = I / 128, np = H / 256;
     const uint64_t dims[5] = {128, 256, kt, np, (uint64_t)n_slots}, str[4] = {64, 16384, kt * 16384, SB};
     const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
     if ((rc = make_map(&p->tmA2, U4, 5, slot_arena + p->slot.w2p, dims, str, box, "w2")) != 0) return rc;
+    const uint64_t dimsp[5] = {64, 256, kt, np, (uint64_t)n_slots};
+    const uint32_t boxp[5] = {64, 2 * G_BM, 1, 1, 1};
+    if ((rc = make_map(&p->tmA2p, U8, 5, slot_arena + p->slot.w2p, dimsp, str, boxp, "w2 packed",
+                       CU_TENSOR_MAP_SWIZZLE_64B)) != 0)
+      return rc;
   }
   const uint32_t brows[4] = {16, 32, 64, 112};
+  // activations: FP8 one byte per element (128-byte swizzle), E2M1 packed
+  // two per byte (64-byte swizzle, 64 bytes per row of a k-tile)
   for (int j = 0; j < 4; ++j) {
-    const uint32_t bbox[2] = {G_BK, brows[j]};
+    const uint32_t bbox[2] = {G_BK, brows[j]}, bboxp[2] = {G_BK / 2, brows[j]};
+    const CUtensorMapSwizzle SW64 = CU_TENSOR_MAP_SWIZZLE_64B;
     {
-      const uint64_t dims[2] = {H, PC}, s8[1] = {H}, s4[1] = {H / 2};
+      const uint64_t dims[2] = {H, PC}, dimsp[2] = {H / 2, PC}, s8[1] = {H}, s4[1] = {H / 2};
       if ((rc = make_map(&p->tmB1_fp8[j], U8, 2, p->ws + wl.xq, dims, s8, bbox, "x fp8")) != 0) return rc;
-      if ((rc = make_map(&p->tmB1_fp4[j], U4, 2, p->ws + wl.xq, dims, s4, bbox, "x fp4")) != 0) return rc;
+      if ((rc = make_map(&p->tmB1_fp4[j], U8, 2, p->ws + wl.xq, dimsp, s4, bboxp, "x fp4", SW64)) != 0) return rc;
     }
     {
-      const uint64_t dims[2] = {I, PC}, s8[1] = {I}, s4[1] = {I / 2};
+      const uint64_t dims[2] = {I, PC}, dimsp[2] = {I / 2, PC}, s8[1] = {I}, s4[1] = {I / 2};
       if ((rc = make_map(&p->tmB2_fp8[j], U8, 2, p->ws + wl.hq, dims, s8, bbox, "h fp8")) != 0) return rc;
-      if ((rc = make_map(&p->tmB2_fp4[j], U4, 2, p->ws + wl.hq, dims, s4, bbox, "h fp4")) != 0) return rc;
+      if ((rc = make_map(&p->tmB2_fp4[j], U8, 2, p->ws + wl.hq, dimsp, s4, bboxp, "h fp4", SW64)) != 0) return rc;
     }
   }
   if ((rc = prepare_gemm<2, false, EPI_SWIGLU_FP8>()) != 0) return rc;
@@ -681,7 +701,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   cudaStream_t st = (cudaStream_t)stream;
   const WsLayout& w = p->wl;
   const int P = (int)(n_tokens * p->topk);
-  const int bn = gemm_bn(p->gemm_tile);   // GEMM tile = expert-group padding
+  const int bn = gemm_bn(p->gemm_tile, P, p->E);   // GEMM tile = expert-group padding
   int* status = wsp<int>(p, w.status);
   int32_t* sorted_flat = wsp<int32_t>(p, w.sorted_flat);
   int32_t* inv = wsp<int32_t>(p, w.inv);
@@ -740,12 +760,12 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   g2.out_bf16 = wsp<uint16_t>(p, w.out);
   g2.out_ld = p->H;
   if (fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp4, g1)));
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13p, p->tmB1_fp4, g1)));
   else
     DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp8, g1)));
   mark(3);
   if (fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp4, g2)));
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2p, p->tmB2_fp4, g2)));
   else
     DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, g2)));
   mark(4);

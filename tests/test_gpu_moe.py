@@ -137,16 +137,18 @@ def test_cfg1_decode_matches_oracle(ops, layer1, T):
     assert rel_err(bf16_to_np(y), ref) <= TOL
 
 
+@pytest.mark.parametrize("tile", [64, 112])
 @pytest.mark.parametrize("T", [40, 256, 700])
-def test_cfg0_gemm_tile_of_112_tokens(ops, layer0, T):
-    """With a 112-token GEMM tile expert groups are padded to 112 rows and
+def test_cfg0_gemm_tile(ops, layer0, T, tile):
+    """Both GEMM tiles at every batch size (the default picks by batch
+    size).  With a 112-token tile expert groups are padded to 112 rows and
     chunks of up to 112 rows run as one MMA N (the epilogue's second pass of
     each warp is 24 columns wide)."""
     L = layer0
     x = S.make_tokens(L.cfg, 300 + T, T)
     w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), L.cfg.topk, "softmax", False)
     plan = _plan(ops, L, T)
-    plan.set_gemm_tile(112)
+    plan.set_gemm_tile(tile)
     for profile in ("bf16", "a4w4"):
         y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
                          L.slot_of, profile)
@@ -154,6 +156,6 @@ def test_cfg0_gemm_tile_of_112_tokens(ops, layer0, T):
         assert rel_err(bf16_to_np(y), L.oracle(x, w, idx, profile)) <= TOL, profile
     d = plan.debug_align(T)
     starts = d["offsets"].numpy()[:-1]
-    assert np.all(starts % 112 == 0)
+    assert np.all(starts % tile == 0)
     ref = O.moe_align(idx, L.n)
     assert np.array_equal(np.argsort(d["inv"].numpy(), kind="stable"), ref["order"])
