@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   int* tot = run + E;            // E
   int* scratch = tot + E;        // 32
   int* sidx = scratch + 32;      // AL_THREADS ints: scan scratch of the one-pass path
-  uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E]
+  uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E] u16 (one pass) or u32 (two passes)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool small = P <= AL_THREADS;
   griddep_wait();
@@ -183,19 +183,49 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     return;
   }
 
-  for (int e = tid; e < E; e += AL_THREADS) cnt[e] = 0;
+  // Larger batches: warp w owns the contiguous segment [w*seg, (w+1)*seg)
+  // of assignments and walks it 32 at a time, in order, twice.  Pass 1
+  // counts each expert per warp ([32][E] table); a column prefix over the
+  // warps then gives every warp the start of its rows inside each group,
+  // and pass 2 hands out the positions.  The order is the stable counting
+  // sort's; there is no block barrier inside the passes.
+  uint32_t* wcn = reinterpret_cast<uint32_t*>(wc);   // [32][E]
+  for (int j = tid; j < 32 * E; j += AL_THREADS) wcn[j] = 0u;
   __syncthreads();
-  for (int p = tid; p < P; p += AL_THREADS) {
-    int e = idx[p];
-    if (e == -1) {   // an empty assignment
-      inv[p] = -1;
-    } else if (e < 0 || e >= E) {
-      set_status(status, DSV4_EINVAL);
-      inv[p] = -1;
-      e = -1;
-    } else {
-      atomicAdd(&cnt[e], 1);
+  const int seg = (P + 31) / 32;
+  const int s0 = min(P, warp * seg), s1 = min(P, s0 + seg);
+  constexpr int R = 8;   // rounds whose indices are loaded together
+  for (int b0 = s0; b0 < s1; b0 += 32 * R) {
+    int ev[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int p = b0 + r * 32 + lane;
+      ev[r] = p < s1 ? idx[p] : -1;
     }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int p = b0 + r * 32 + lane;
+      int e = ev[r];
+      if (p < s1 && e != -1 && (e < 0 || e >= E)) {
+        set_status(status, DSV4_EINVAL);
+        e = -1;
+      }
+      if (p < s1 && e < 0) inv[p] = -1;   // empty (-1) or rejected assignment
+      const unsigned same = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (same & ((1u << lane) - 1u)) == 0u) wcn[warp * E + e] += (uint32_t)__popc(same);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // per expert: exclusive prefix over the warps, in place, and the total
+  for (int x = tid; x < E; x += AL_THREADS) {
+    uint32_t sum = 0;
+    for (int w = 0; w < 32; ++w) {
+      const uint32_t v = wcn[w * E + x];
+      wcn[w * E + x] = sum;
+      sum += v;
+    }
+    cnt[x] = (int)sum;
   }
   __syncthreads();
   // exclusive scan of the (padded) group sizes (E <= 1024: one expert per thread)
@@ -205,7 +235,6 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   const int off = block_exclusive_scan(cpad, scratch, &total);
   if (tid < E) {
     run[tid] = off;
-    tot[tid] = off + c;   // first padding row of the group
     counts[tid] = c;
     offsets[tid] = off;
   }
@@ -214,45 +243,39 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   // padding rows of each group (fewer than `pad`), one warp per group so the
   // stores of a warp are contiguous
   for (int e = warp; e < E; e += AL_THREADS / 32) {
-    const int r0 = tot[e], r1 = run[e] + (cnt[e] + pad - 1) / pad * pad;
+    const int r0 = run[e] + cnt[e], r1 = run[e] + (cnt[e] + pad - 1) / pad * pad;
     for (int r = r0 + lane; r < r1; r += 32) {
       sorted_flat[r] = -1;
       if (sorted_w) sorted_w[r] = 0.f;
     }
   }
-
-  for (int base = 0; base < P; base += AL_THREADS) {
-    for (int j = tid; j < 32 * E; j += AL_THREADS) wc[j] = 0;
-    __syncthreads();
-    const int p = base + tid;
-    int e = -1;
-    if (p < P) {
-      e = idx[p];
+  // pass 2: positions, in assignment order
+  for (int b0 = s0; b0 < s1; b0 += 32 * R) {
+    int ev[R];
+    float wv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int p = b0 + r * 32 + lane;
+      ev[r] = p < s1 ? idx[p] : -1;
+      wv[r] = (p < s1 && sorted_w) ? w_flat[p] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int p = b0 + r * 32 + lane;
+      int e = ev[r];
       if (e < 0 || e >= E) e = -1;
-    }
-    const unsigned mask = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(mask & ((1u << lane) - 1u));
-    if (e >= 0 && rank == 0) wc[warp * E + e] = (uint16_t)__popc(mask);
-    __syncthreads();
-    for (int x = tid; x < E; x += AL_THREADS) {
-      int s = 0;
-      for (int w = 0; w < 32; ++w) {
-        const int v = wc[w * E + x];
-        wc[w * E + x] = (uint16_t)s;
-        s += v;
+      const unsigned same = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(same & ((1u << lane) - 1u));
+      if (e >= 0) {
+        const int pos = run[e] + (int)wcn[warp * E + e] + rank;
+        sorted_flat[pos] = p;
+        inv[p] = pos;
+        if (sorted_w) sorted_w[pos] = wv[r];
       }
-      tot[x] = s;
+      __syncwarp();
+      if (e >= 0 && rank == 0) wcn[warp * E + e] += (uint32_t)__popc(same);
+      __syncwarp();
     }
-    __syncthreads();
-    if (e >= 0) {
-      const int pos = run[e] + wc[warp * E + e] + rank;
-      sorted_flat[pos] = p;
-      inv[p] = pos;
-      if (sorted_w) sorted_w[pos] = w_flat[p];
-    }
-    __syncthreads();
-    for (int x = tid; x < E; x += AL_THREADS) run[x] += tot[x];
-    __syncthreads();
   }
 
   // active experts, ascending
@@ -396,13 +419,23 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
   if (k == 0) return;
   for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < H; c += gridDim.y * blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < k; ++j) {
-      const uint4 r = *reinterpret_cast<const uint4*>(out + (int64_t)pos[j] * H + c);
-      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    // the rows' loads are issued together (up to 8 in flight), then added
+    // in ascending position
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      uint4 r[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc[2 * q] += bf16_from_bits(w[q] & 0xffffu);
-        acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
+      for (int u = 0; u < 8; ++u)
+        if (j0 + u < k) r[u] = *reinterpret_cast<const uint4*>(out + (int64_t)pos[j0 + u] * H + c);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < k) {
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[2 * q] += bf16_from_bits(w[q] & 0xffffu);
+            acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
+          }
+        }
       }
     }
     uint32_t o[4];
@@ -676,7 +709,7 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   if ((rc = prepare_gemm<2, true, EPI_SWIGLU_MXFP4>()) != 0) return rc;
   if ((rc = prepare_gemm<2, false, EPI_STORE_BF16>()) != 0) return rc;
   if ((rc = prepare_gemm<2, true, EPI_STORE_BF16>()) != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 2;
+  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   *out = p.release();
@@ -707,7 +740,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   int32_t* inv = wsp<int32_t>(p, w.inv);
   int32_t* n_active = wsp<int32_t>(p, w.n_active);
   int* n_chunks = wsp<int>(p, w.n_chunks);
-  const size_t al_smem = (size_t)(3 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 2;
+  const size_t al_smem = (size_t)(3 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 4;
   auto mark = [&](int i) {
     if (p->timing) cudaEventRecord(p->ev[i], st);
   };
@@ -849,7 +882,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * topk < (1LL << 31), "too many assignments");
   int rc = bind_device_of(counts, nullptr);
   if (rc != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 2;
+  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(

@@ -1,5 +1,6 @@
 // Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
-//   phase 1: fp32 partial logits, split over 128-wide slices of H:
+//   phase 1: fp32 partial logits, split over slices of H (128 wide for
+//            decode batches, H/8 wide from 256 tokens on):
 //            part[s, t, e] = sum over slice s of float(x[t, k]) * w[e, k];
 //   phase 2: one CTA per token: add the slices in order (deterministic),
 //            then one warp applies the score function, the biased top-k (or
@@ -101,6 +102,96 @@ __global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __res
     } else {
 #pragma unroll
       for (int b = 0; b < 4; ++b)
+        if (e + b < E) dst[t * E + e + b] = acc[a][b];
+    }
+  }
+}
+
+// Prefill-sized batches: one CTA computes 128 tokens x 128 experts over
+// kslice elements of H (a multiple of 32), thread (ty, tx) accumulating
+// tokens 8ty..8ty+7 against experts 8tx..8tx+7: four 16-byte shared loads
+// per 64 FMAs, so the FMA pipe rather than shared memory sets the pace.
+// Chunks of 32 of K are staged transposed as in route_logits_kernel.
+constexpr int RW_TOK = 128, RW_EXP = 128, RW_KC = 32;
+__global__ __launch_bounds__(256, 1) void route_logits_wide_kernel(const uint16_t* __restrict__ x,
+                                                                   const float* __restrict__ w,
+                                                                   float* __restrict__ part, int64_t T, int H,
+                                                                   int E, int kslice) {
+  __shared__ __align__(16) float xs[RW_KC][RW_TOK];
+  __shared__ __align__(16) float ws[RW_KC][RW_EXP];
+  griddep_wait();
+  griddep_launch();
+  const int tid = threadIdx.x;
+  const int e0 = blockIdx.x * RW_EXP;
+  const int slice = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.z * RW_TOK;
+  const int kbeg = slice * kslice;
+  uint4 xr[2];
+  float4 wr[4];
+  auto load = [&](int kc) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = tid + 256 * j, t = i & (RW_TOK - 1), c = (i >> 7) * 8;
+      xr[j] = t0 + t < T ? *reinterpret_cast<const uint4*>(x + (t0 + t) * H + kc + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j, e = i & (RW_EXP - 1), c = (i >> 7) * 4;
+      wr[j] = e0 + e < E ? *reinterpret_cast<const float4*>(w + (int64_t)(e0 + e) * H + kc + c)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  load(kbeg);
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[8][8] = {};
+  for (int kc = kbeg; kc < kbeg + kslice; kc += RW_KC) {
+    __syncthreads();   // the previous chunk has been consumed
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = tid + 256 * j, t = i & (RW_TOK - 1), c = (i >> 7) * 8;
+      const uint32_t v[4] = {xr[j].x, xr[j].y, xr[j].z, xr[j].w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        xs[c + 2 * m][t] = bf16_from_bits(v[m] & 0xffffu);
+        xs[c + 2 * m + 1][t] = bf16_from_bits(v[m] >> 16);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j, e = i & (RW_EXP - 1), c = (i >> 7) * 4;
+      ws[c][e] = wr[j].x;
+      ws[c + 1][e] = wr[j].y;
+      ws[c + 2][e] = wr[j].z;
+      ws[c + 3][e] = wr[j].w;
+    }
+    __syncthreads();
+    if (kc + RW_KC < kbeg + kslice) load(kc + RW_KC);
+#pragma unroll 4
+    for (int k = 0; k < RW_KC; ++k) {
+      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][8 * ty]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][8 * ty + 4]);
+      const float4 w0 = *reinterpret_cast<const float4*>(&ws[k][8 * tx]);
+      const float4 w1 = *reinterpret_cast<const float4*>(&ws[k][8 * tx + 4]);
+      const float xa[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(xa[a], wa[b], acc[a][b]);
+    }
+  }
+  float* dst = part + (int64_t)slice * T * E;
+  const int e = e0 + 8 * tx;
+#pragma unroll
+  for (int a = 0; a < 8; ++a) {
+    const int64_t t = t0 + 8 * ty + a;
+    if (t >= T) break;
+    if (e + 7 < E && (E & 3) == 0) {   // 16-byte aligned quads
+      *reinterpret_cast<float4*>(dst + t * E + e) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(dst + t * E + e + 4) = make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
+    } else {
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
         if (e + b < E) dst[t * E + e + b] = acc[a][b];
     }
   }
@@ -245,11 +336,23 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   if (n_tokens == 0) return DSV4_OK;
   if (int rc = bind_device_of(x_bf16, nullptr)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const int split = hidden / RL_SLICE;
-  const dim3 grid((n_experts + RL_EXP - 1) / RL_EXP, split, (unsigned)((n_tokens + RL_TOK - 1) / RL_TOK));
   const bool pdl = pdl_enabled();
-  DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
-                           (float*)workspace, n_tokens, hidden, n_experts, (int)RL_SLICE));
+  int split;
+  if (n_tokens >= 2 * RW_TOK) {
+    // prefill: 128 x 128 tiles, H split into 8 slices (512 of H each at
+    // H = 4096): 256 CTAs at T = 2048, E = 256, and 8 partials per logit
+    split = 8;
+    const dim3 grid((n_experts + RW_EXP - 1) / RW_EXP, split, (unsigned)((n_tokens + RW_TOK - 1) / RW_TOK));
+    DSV4_CUDA_CHECK(launch_k(route_logits_wide_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16,
+                             gate_w, (float*)workspace, n_tokens, hidden, n_experts, hidden / split));
+  } else {
+    // decode: 64 x 64 tiles, one slice per 128 of H, so that a handful of
+    // tokens still spreads over 128+ CTAs
+    split = hidden / RL_SLICE;
+    const dim3 grid((n_experts + RL_EXP - 1) / RL_EXP, split, (unsigned)((n_tokens + RL_TOK - 1) / RL_TOK));
+    DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
+                             (float*)workspace, n_tokens, hidden, n_experts, (int)RL_SLICE));
+  }
   DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl,
                            (const float*)workspace, split, n_tokens, n_experts, topk, score_func, renormalize,
                            route_scale, bias, tid2eid, input_ids, weights_out, indices_out));

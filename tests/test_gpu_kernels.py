@@ -108,8 +108,10 @@ def test_route_golden_cfg0(ops):
     np.testing.assert_allclose(w.cpu().numpy(), g["hash_w"], rtol=1e-5, atol=1e-7)
 
 
-@pytest.mark.parametrize("T", [1, 8, 64, 300])
+@pytest.mark.parametrize("T", [1, 8, 64, 255, 300, 2048])
 def test_route_cfg1_matches_oracle(ops, T):
+    """Decode sizes run the 64 x 64 split-K kernel, from 256 tokens the
+    128 x 128 one (300: a ragged last token tile)."""
     cfg = S.CFG1
     gw, bias = S.make_gate(cfg, 0)
     x = S.make_tokens(cfg, 0, T)
