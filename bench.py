@@ -428,8 +428,8 @@ def cpu_baseline(tokens: int, budget_s: float = 12.0):
 # ---------------------------------------------------------------------------
 # config 2: prefill, a4w4 profile
 # ---------------------------------------------------------------------------
-FP8_DENSE_TFLOPS = 4500.0   # nominal dense B200 rate of kind::mxf8f6f4 (E2M1 operands run at this rate)
-FP4_DENSE_TFLOPS = 9000.0   # nominal dense B200 rate of the packed-FP4 MMA kinds
+FP8_DENSE_TFLOPS = 4500.0   # nominal dense B200 rate of kind::mxf8f6f4 (the bf16 profile's MMA)
+FP4_DENSE_TFLOPS = 9000.0   # nominal dense B200 rate of kind::mxf4 (the a4w4 profile's MMA)
 
 
 def run_prefill(a):
@@ -519,7 +519,7 @@ def run_prefill(a):
     sm = {k: round(statistics.mean(x[k] for x in st_list), 5) for k in st_list[0]}
     g1_flops, g2_flops = 4.0 * c.hidden * c.inter * P, 2.0 * c.hidden * c.inter * P
     g1_bytes = _gemm_bytes(d, P, "gate_up") - P * (c.hidden + c.hidden // 32) + P * (c.hidden // 2 + c.hidden // 32)
-    g1_bound = max(g1_bytes / (hbm * 1e9), g1_flops / (FP8_DENSE_TFLOPS * 1e12)) * 1e3
+    g1_bound = max(g1_bytes / (hbm * 1e9), g1_flops / (FP4_DENSE_TFLOPS * 1e12)) * 1e3
     line = {"metric": METRIC, "value": round(T * a.steps / (tot_ms / 1e3), 1), "unit": UNIT, "n_gpus": 1,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
@@ -528,11 +528,11 @@ def run_prefill(a):
             "config": {"workload": f"cfg2 prefill a4w4 profile: T={T} tokens, H=4096, I=2048, E=256, top-8, "
                                    "all experts resident", "tokens_per_step": T, "global_batch": T,
                        "parallelism": "single GPU", "l2": "256 MiB flush before every timed step"},
-            "roofline": {"bound": "hbm" if t_hbm >= t_fp8 else "tensor",
-                         "layer_bound_ms": round(max(t_hbm, t_fp8), 5), "frac": round(max(t_hbm, t_fp8) / ms, 4),
+            "roofline": {"bound": "hbm" if t_hbm >= t_fp4 else "tensor",
+                         "layer_bound_ms": round(max(t_hbm, t_fp4), 5), "frac": round(max(t_hbm, t_fp4) / ms, 4),
                          "hbm_ms": round(t_hbm, 5), "fp8_rate_ms": round(t_fp8, 5), "fp4_rate_ms": round(t_fp4, 5),
                          "bytes": round(byts), "flops": flops, "peak_hbm_gbs": hbm, "peak_kind": peak_kind,
-                         "tensor_peak": f"{FP8_DENSE_TFLOPS:.0f} TFLOP/s nominal dense (the f8f6f4 kind)",
+                         "tensor_peak": f"{FP4_DENSE_TFLOPS:.0f} TFLOP/s nominal dense (kind::mxf4, the a4w4 MMA)",
                          "gate_up_frac": round(g1_bound / sm["gate_up_gemm"], 4)},
             "e2e": {"value": round(T * a.steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
