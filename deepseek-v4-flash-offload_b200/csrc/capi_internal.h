@@ -3,6 +3,7 @@
 // packed expert slot layout.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,6 +19,11 @@ int fail(int code, const std::string& msg);
 // (the library links its own runtime, so it does not see the caller's
 // cudaSetDevice).  Optionally returns the device ordinal.
 int bind_device_of(const void* ptr, int* device);
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link): rank-D map over `base` with element strides of 1.
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, const char* what,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Launch with programmatic stream serialization (PDL) when `pdl`: the kernel
 // may start while its stream predecessor finishes; it must call

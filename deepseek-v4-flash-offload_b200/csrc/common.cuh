@@ -304,6 +304,26 @@ __device__ __forceinline__ void tc_mma_mxf4(uint32_t d_tmem, uint64_t adesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// bf16 x bf16 -> fp32 in TMEM, both operands K-major in shared memory.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Instruction descriptor of kind::f16 with bf16 A and B, fp32 D, both K-major.
+__host__ __device__ __forceinline__ uint32_t idesc_bf16(int m, int n) {
+  uint32_t d = 0;
+  d |= 1u << 4;                        // D format F32
+  d |= 1u << 7;                        // A format BF16
+  d |= 1u << 10;                       // B format BF16
+  d |= ((uint32_t)(n >> 3) & 63u) << 17;
+  d |= ((uint32_t)(m >> 4) & 31u) << 24;
+  return d;
+}
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 8 consecutive 32-bit columns -> 8 registers per thread.

@@ -509,9 +509,8 @@ static EncodeTiledFn get_encoder() {
   return fn;
 }
 
-static int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box, const char* what,
-                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, const char* what, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = get_encoder();
   if (!enc) return fail(DSV4_ECUDA, "cuTensorMapEncodeTiled is not available");
   cuuint64_t d[5], s[4];

@@ -1,10 +1,15 @@
 // Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
-//   phase 1: fp32 partial logits, split over slices of H (128 wide for
-//            decode batches, H/8 wide from 256 tokens on):
+//   phase 1: fp32 partial logits, split over slices of H:
 //            part[s, t, e] = sum over slice s of float(x[t, k]) * w[e, k];
+//            decode batches (< 256 tokens) on the FP32 pipes, 128-wide
+//            slices; larger batches on the tensor cores (route_logits_tc_kernel),
+//            four slices;
 //   phase 2: one CTA per token: add the slices in order (deterministic),
 //            then one warp applies the score function, the biased top-k (or
 //            the hash table), the unbiased weights, renormalisation, scale.
+#include <stdlib.h>
+
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -197,6 +202,171 @@ __global__ __launch_bounds__(256, 1) void route_logits_wide_kernel(const uint16_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill router on the tensor cores.
+//
+// The fp32 gate w is split, per call, into three bf16 matrices whose sum is
+// w exactly: hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid).  Each
+// residual is exact in fp32 and the last one fits bf16's 8 significant bits.
+// x is bf16, so every product x*hi, x*mid, x*lo is exact in fp32, and the
+// tensor cores accumulate them in fp32: the logits keep fp32 accuracy, in a
+// different summation order than the FP32-pipe kernels (as any two fp32 GEMMs
+// differ).  One CTA computes 128 experts (MMA M) x 128 tokens (MMA N) over
+// H/RTC_SPLIT, one tcgen05.mma.kind::f16 per (16 of K, gate term), into 128
+// TMEM columns.  Warp 0: TMA producer; warp 1: TMEM owner and MMA issuer;
+// warps 2-5: epilogue (TMEM lane quarter warp % 4).
+// ---------------------------------------------------------------------------
+constexpr int RTC_M = 128, RTC_N = 128, RTC_KC = 64, RTC_STAGES = 3, RTC_TERMS = 3, RTC_SPLIT = 4;
+constexpr int RTC_TERM_BYTES = RTC_M * RTC_KC * 2;                 // 16 KB: 128 rows x 128 B
+constexpr int RTC_A_BYTES = RTC_TERMS * RTC_TERM_BYTES;            // 48 KB
+constexpr int RTC_B_BYTES = RTC_N * RTC_KC * 2;                    // 16 KB
+constexpr int RTC_STAGE_BYTES = RTC_A_BYTES + RTC_B_BYTES;         // 64 KB
+constexpr int RTC_SMEM = RTC_STAGES * RTC_STAGE_BYTES + 256 + 1024;
+constexpr int RTC_THREADS = 192;
+constexpr uint32_t RTC_TMEM_COLS = 128;
+
+// hi / mid / lo terms of the gate, [3][E*H] bf16; also clears the call's
+// error word (read by route_topk_kernel after the logits kernel).
+__global__ void gate_split_kernel(const float4* __restrict__ w, int64_t n4, uint2* __restrict__ out,
+                                  int* __restrict__ err) {
+  griddep_wait();
+  griddep_launch();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v4 = w[i];
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    uint32_t h[4], m[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = bf16_bits(v[j]);
+      const float r1 = v[j] - bf16_from_bits(h[j]);
+      m[j] = bf16_bits(r1);
+      const float r2 = r1 - bf16_from_bits(m[j]);
+      l[j] = bf16_bits(r2);
+    }
+    out[i] = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+    out[n4 + i] = make_uint2(m[0] | (m[1] << 16), m[2] | (m[3] << 16));
+    out[2 * n4 + i] = make_uint2(l[0] | (l[1] << 16), l[2] | (l[3] << 16));
+  }
+}
+
+__global__ void __launch_bounds__(RTC_THREADS, 1)
+    route_logits_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                           float* __restrict__ part, int64_t T, int E, int kslice, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + RTC_STAGES * RTC_STAGE_BYTES);
+  uint64_t* empty = full + RTC_STAGES;
+  uint64_t* accfull = empty + RTC_STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accfull + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RTC_M;
+  const int64_t t0 = (int64_t)blockIdx.y * RTC_N;
+  const int slice = blockIdx.z;
+  const int kbeg = slice * kslice;
+  const int nch = kslice / RTC_KC;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RTC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmW);
+    prefetch_tensormap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, RTC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  griddep_wait();   // the gate terms come from the split kernel just before
+  griddep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();   // x and the gate terms are read by several CTAs
+      int issued = 0;
+      for (int c = 0; c < nch; ++c) {
+        const int s = c % RTC_STAGES;
+        const uint32_t ph = (uint32_t)(c / RTC_STAGES) & 1u;
+        if (c >= RTC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, err)) break;
+        uint8_t* st = smem + s * RTC_STAGE_BYTES;
+        mbar_expect_tx(&full[s], RTC_STAGE_BYTES);
+        tma_load_3d(st, &tmW, &full[s], kbeg + c * RTC_KC, e0, 0, pol);
+        tma_load_2d(st + RTC_A_BYTES, &tmX, &full[s], kbeg + c * RTC_KC, (int)t0, pol);
+        mbar_arrive(&full[s]);   // the barrier's one arrival; the copies complete its transaction bytes
+        ++issued;
+      }
+      // the last stages' copies have landed before the CTA can exit
+      for (int c = issued - RTC_STAGES < 0 ? 0 : issued - RTC_STAGES; c < issued; ++c) {
+        const uint64_t tw = globaltimer_ns();
+        while (!mbar_try_wait(&full[c % RTC_STAGES], (uint32_t)(c / RTC_STAGES) & 1u) &&
+               globaltimer_ns() - tw < DSV4_WAIT_NS) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(RTC_M, RTC_N);
+      for (int c = 0; c < nch; ++c) {
+        const int s = c % RTC_STAGES;
+        const uint32_t ph = (uint32_t)(c / RTC_STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, err)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * RTC_STAGE_BYTES);
+        const uint64_t db = desc_sw128(a + RTC_A_BYTES);
+#pragma unroll
+        for (int term = 0; term < RTC_TERMS; ++term) {
+          const uint64_t da = desc_sw128(a + term * RTC_TERM_BYTES);
+#pragma unroll
+          for (int j = 0; j < RTC_KC / 16; ++j)   // +32 bytes (16 bf16) of K per step in the swizzle row
+            tc_mma_bf16(tmem, da + 2u * j, db + 2u * j, idesc, (c | term | j) != 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);
+      }
+      // every MMA issued above has completed once this arrives
+      tc_commit(accfull);
+      const uint64_t tw = globaltimer_ns();
+      while (!mbar_try_wait(accfull, 0) && globaltimer_ns() - tw < DSV4_WAIT_NS) {
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;   // TMEM lanes 32q..32q+31 = experts e0+32q..
+    // warp-uniform decision: tcgen05.ld below needs all 32 lanes
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(accfull, 0, err) && read_status(err) == 0);
+    tc_fence_after();
+    if (ok) {
+      const int e = e0 + q * 32 + lane;
+      float* dst = part + (int64_t)slice * T * E + e;
+#pragma unroll 1
+      for (int c0 = 0; c0 < RTC_N; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const int64_t t = t0 + c0 + n;
+          if (t < T && e < E) dst[t * E] = v[n];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, RTC_TMEM_COLS);
+  }
+}
+
 __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log1pf(expf(v)); }
 
 // One CTA (256 threads) per token.  Thread e adds the slices of logit
@@ -209,7 +379,7 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
                                                          const float* __restrict__ bias,
                                                          const int32_t* __restrict__ tid2eid,
                                                          const int64_t* __restrict__ ids, float* __restrict__ w_out,
-                                                         int32_t* __restrict__ i_out) {
+                                                         int32_t* __restrict__ i_out, const int* __restrict__ err) {
   constexpr int PER = RT_MAX_E / 32;
   __shared__ float sc_s[RT_MAX_E], ch_s[RT_MAX_E];
   __shared__ float red[2][8];
@@ -217,6 +387,15 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
   griddep_launch();
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (err && *reinterpret_cast<const volatile int*>(err) != 0) {
+    // the logits kernel gave up on a wait: expert id E is out of range, so
+    // the layer's align rejects these picks and its status reports it
+    if (tid < K) {
+      w_out[t * K + tid] = 0.f;
+      i_out[t * K + tid] = E;
+    }
+    return;
+  }
   const int e = tid;
   float l = -INFINITY;
   if (e < E) {
@@ -314,9 +493,41 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
 
 using namespace dsv4;
 
+namespace {
+// Batches from this many tokens take the tensor-core logits kernel.
+constexpr int64_t RTC_MIN_TOKENS = 256;
+int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
+// Tensor-core path workspace: [error word | gate terms bf16 [3][E][H] | partials [RTC_SPLIT][T][E] fp32]
+int64_t tc_terms_off() { return 256; }
+int64_t tc_part_off(int32_t hidden, int32_t n_experts) {
+  return 256 + al256((int64_t)RTC_TERMS * n_experts * hidden * 2);
+}
+// DSV4_ROUTE_TC=0 keeps prefill batches on the FP32-pipe kernel (the
+// tensor-core path is the default).
+const bool g_route_no_tc = [] {
+  const char* e = getenv("DSV4_ROUTE_TC");
+  return e && e[0] == '0';
+}();
+std::mutex g_tc_mu;
+bool g_tc_ready[64] = {};
+// The tensor-core kernel's shared-memory opt-in, once per device.
+int prepare_route_tc() {
+  int dev = 0;
+  DSV4_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_tc_mu);
+  if (dev >= 0 && dev < 64 && g_tc_ready[dev]) return DSV4_OK;
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(route_logits_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RTC_SMEM));
+  if (dev >= 0 && dev < 64) g_tc_ready[dev] = true;
+  return DSV4_OK;
+}
+}  // namespace
+
 extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts) {
   if (n_tokens < 0 || hidden <= 0 || n_experts <= 0) return DSV4_EINVAL;
-  return (int64_t)(hidden / RL_SLICE) * n_tokens * n_experts * (int64_t)sizeof(float);
+  const int64_t simt = (int64_t)(hidden / RL_SLICE) * n_tokens * n_experts * (int64_t)sizeof(float);
+  if (n_tokens < RTC_MIN_TOKENS || n_experts < RTC_M) return simt;
+  const int64_t tc = tc_part_off(hidden, n_experts) + (int64_t)RTC_SPLIT * n_tokens * n_experts * 4;
+  return std::max(simt, tc);
 }
 
 extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
@@ -338,7 +549,40 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
   int split;
-  if (n_tokens >= 2 * RW_TOK) {
+  const float* logits = (const float*)workspace;
+  const int* err = nullptr;
+  const bool tc = n_tokens >= RTC_MIN_TOKENS && n_experts >= RTC_M && ((uintptr_t)x_bf16 % 16) == 0 &&
+                  ((uintptr_t)workspace % 16) == 0 && ((uintptr_t)gate_w % 16) == 0 && !g_route_no_tc;
+  if (tc) {
+    // prefill: gate split into three bf16 terms, then the tensor-core logits
+    uint8_t* ws = (uint8_t*)workspace;
+    int* err_w = (int*)ws;
+    uint16_t* terms = (uint16_t*)(ws + tc_terms_off());
+    float* part = (float*)(ws + tc_part_off(hidden, n_experts));
+    const int64_t n4 = (int64_t)n_experts * hidden / 4;
+    DSV4_CUDA_CHECK(launch_k(gate_split_kernel, dim3(296), dim3(256), 0, st, pdl, (const float4*)gate_w, n4,
+                             (uint2*)terms, err_w));
+    CUtensorMap tmW, tmX;
+    {
+      const uint64_t dims[3] = {(uint64_t)hidden, (uint64_t)n_experts, (uint64_t)RTC_TERMS};
+      const uint64_t str[2] = {(uint64_t)hidden * 2, (uint64_t)hidden * n_experts * 2};
+      const uint32_t box[3] = {RTC_KC, RTC_M, RTC_TERMS};
+      if (int rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, terms, dims, str, box, "gate terms")) return rc;
+    }
+    {
+      const uint64_t dims[2] = {(uint64_t)hidden, (uint64_t)n_tokens};
+      const uint64_t str[1] = {(uint64_t)hidden * 2};
+      const uint32_t box[2] = {RTC_KC, RTC_N};
+      if (int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)x_bf16, dims, str, box, "x")) return rc;
+    }
+    if (int rc = prepare_route_tc()) return rc;
+    split = RTC_SPLIT;
+    const dim3 grid((n_experts + RTC_M - 1) / RTC_M, (unsigned)((n_tokens + RTC_N - 1) / RTC_N), RTC_SPLIT);
+    DSV4_CUDA_CHECK(launch_k(route_logits_tc_kernel, grid, dim3(RTC_THREADS), RTC_SMEM, st, pdl, tmW, tmX, part,
+                             n_tokens, n_experts, hidden / RTC_SPLIT, err_w));
+    logits = part;
+    err = err_w;
+  } else if (n_tokens >= 2 * RW_TOK) {
     // prefill: 128 x 128 tiles, H split into 8 slices (512 of H each at
     // H = 4096): 256 CTAs at T = 2048, E = 256, and 8 partials per logit
     split = 8;
@@ -353,9 +597,9 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
     DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
                              (float*)workspace, n_tokens, hidden, n_experts, (int)RL_SLICE));
   }
-  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl,
-                           (const float*)workspace, split, n_tokens, n_experts, topk, score_func, renormalize,
-                           route_scale, bias, tid2eid, input_ids, weights_out, indices_out));
+  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl, logits, split,
+                           n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
+                           weights_out, indices_out, err));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
@@ -426,7 +670,7 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
                                             hidden / RT_SPLIT_NOALLOC);
   route_topk_kernel<<<(unsigned)n_tokens, 256, 0, st>>>(
       scratch, RT_SPLIT_NOALLOC, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
-      weights_out, indices_out);
+      weights_out, indices_out, nullptr);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

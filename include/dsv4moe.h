@@ -93,6 +93,11 @@ int dsv4_act_quant_mxfp4(const void* x_bf16, int64_t rows, int64_t cols, uint8_t
  * scores + bias (or tid2eid[input_ids] when tid2eid != NULL); weights =
  * unbiased scores, renormalised when renormalize != 0, times route_scale.
  * Indices come out in descending biased-score order (ties: lower id first).
+ * The logits are fp32: decode batches on the FP32 pipes; from 256 tokens
+ * (with n_experts >= 128) on the tensor cores, the gate split into three
+ * bf16 terms that sum to it exactly (DSV4_ROUTE_TC=0 keeps the FP32 pipes).
+ * If a device-side wait of the tensor-core kernel runs out, every index is
+ * written as n_experts (out of range) so that the layer's align rejects it.
  * ------------------------------------------------------------------------ */
 int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts);
 int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
