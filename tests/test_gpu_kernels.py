@@ -143,6 +143,30 @@ def test_align_bit_exact(ops, T, k, E):
     assert np.array_equal(res["active"].cpu().numpy()[:na], ref["active"])
 
 
+@pytest.mark.parametrize("T", [64, 2048])
+def test_align_with_empty_assignments(ops, T):
+    """Expert id -1 marks an empty assignment (the padding rows of the
+    expert-parallel exchange): it gets inv = -1 and no sorted row, and the
+    other assignments sort exactly as without it.  T=64 (512 assignments)
+    takes the one-pass path, T=2048 (16384) the two-pass path."""
+    E, k = 256, 8
+    rng = np.random.default_rng(77 + T)
+    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)])
+    idx[rng.random(idx.shape) < 0.3] = -1
+    res = ops.moe_align(torch.from_numpy(idx.astype(np.int32)).cuda(), E)
+    flat = idx.reshape(-1)
+    valid = np.nonzero(flat >= 0)[0]
+    order = valid[np.argsort(flat[valid], kind="stable")]
+    counts = np.bincount(flat[valid], minlength=E)
+    inv = np.full(flat.size, -1, np.int64)
+    inv[order] = np.arange(order.size)
+    assert int(res["status"].item()) == 0
+    assert np.array_equal(res["counts"].cpu().numpy(), counts)
+    assert np.array_equal(res["offsets"].cpu().numpy(), np.concatenate([[0], np.cumsum(counts)]))
+    assert np.array_equal(res["sorted_flat"].cpu().numpy()[:order.size], order)
+    assert np.array_equal(res["inv"].cpu().numpy(), inv)
+
+
 def test_align_rejects_out_of_range_expert(ops):
     idx = torch.tensor([[0, 1], [2, 99]], dtype=torch.int32).cuda()
     res = ops.moe_align(idx, 16)
