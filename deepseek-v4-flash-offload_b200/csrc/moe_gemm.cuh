@@ -114,11 +114,6 @@ __device__ __forceinline__ float warp_max_f(float v) {
 // ~1e-6, far inside the layer's tolerance; v -> -inf gives -0.
 __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
-// max over the warp of non-negative floats (their bit patterns order like
-// unsigned integers): one redux instruction.
-__device__ __forceinline__ float warp_max_nonneg(float v) {
-  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
-}
 
 struct TileInfo {
   int slot;   // < 0: skip (expert not resident)
@@ -147,8 +142,8 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
 // five butterfly rounds each halve the columns a lane keeps (16, 8, 4, 2,
 // 1) while exchanging the other half with its partner, so 31 shuffles
 // leave lane L with column L's maximum.  The maximum is taken on the bit
-// patterns (non-negative floats order like unsigned integers), as
-// warp_max_nonneg does.  v is scratch (overwritten).
+// patterns (non-negative floats order like unsigned integers).  v is
+// scratch (overwritten).
 __device__ __forceinline__ float column_amax_transposed(const float* h, float* v, int lane) {
   uint32_t* u = reinterpret_cast<uint32_t*>(v);
 #pragma unroll

@@ -117,8 +117,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
-  int* tot = run + E;            // E
-  int* scratch = tot + E;        // 32
+  int* scratch = run + E;        // 32
   int* sidx = scratch + 32;      // AL_THREADS ints: scan scratch of the one-pass path
   uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E] u16 (one pass) or u32 (two passes)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -726,7 +725,7 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   if ((rc = prepare_gemm<2, true, EPI_SWIGLU_MXFP4>()) != 0) return rc;
   if ((rc = prepare_gemm<2, false, EPI_STORE_BF16>()) != 0) return rc;
   if ((rc = prepare_gemm<2, true, EPI_STORE_BF16>()) != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
+  const size_t al_smem = (size_t)(2 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   *out = p.release();
@@ -757,7 +756,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   int32_t* inv = wsp<int32_t>(p, w.inv);
   int32_t* n_active = wsp<int32_t>(p, w.n_active);
   int* n_chunks = wsp<int>(p, w.n_chunks);
-  const size_t al_smem = (size_t)(3 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 4;
+  const size_t al_smem = (size_t)(2 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 4;
   auto mark = [&](int i) {
     if (p->timing) cudaEventRecord(p->ev[i], st);
   };
@@ -899,7 +898,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * topk < (1LL << 31), "too many assignments");
   int rc = bind_device_of(counts, nullptr);
   if (rc != 0) return rc;
-  const size_t al_smem = (size_t)(3 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
+  const size_t al_smem = (size_t)(2 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
