@@ -207,7 +207,8 @@ __global__ __launch_bounds__(256, 1) void route_logits_wide_kernel(const uint16_
 //
 // The fp32 gate w is split, per call, into three bf16 matrices whose sum is
 // w exactly: hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid).  Each
-// residual is exact in fp32 and the last one fits bf16's 8 significant bits.
+// residual is exact in fp32 and the last one fits bf16's 8 significant bits
+// (for |w| below bf16's largest finite value, 3.39e38).
 // x is bf16, so every product x*hi, x*mid, x*lo is exact in fp32, and the
 // tensor cores accumulate them in fp32: the logits keep fp32 accuracy, in a
 // different summation order than the FP32-pipe kernels (as any two fp32 GEMMs

@@ -177,3 +177,31 @@ def test_layer_constructor_fields(monkeypatch):
     with pytest.raises(RuntimeError, match="input_ids"):
         m._route(torch.zeros(2, 256), None)
     ENG.reset_engine(None)
+
+
+def test_gate_split_terms_sum_to_the_gate_exactly():
+    """The tensor-core router splits the fp32 gate into hi = bf16(w),
+    mid = bf16(w - hi), lo = bf16(w - hi - mid) (gate_split_kernel in
+    csrc/route.cu, round to nearest even).  Every residual is exact in fp32,
+    the last one is already a bf16 value, and the three terms add up to w
+    exactly, so the bf16 products x * term lose nothing.  This holds for
+    |w| below bf16's largest finite value (3.39e38); larger fp32 values round
+    to infinity in the first term."""
+    rng = np.random.default_rng(5)
+    n = 200000
+    w = (rng.standard_normal(n) * 10.0 ** rng.integers(-30, 30, n)).astype(np.float32)
+    w = np.concatenate([w, np.float32([0.0, -0.0, 1.0, -1.0, 3.3e38, -3.3e38, 1.1754944e-38,
+                                       np.nextafter(np.float32(1), np.float32(2))])])
+
+    def bf16(v):
+        b = v.view(np.uint32).astype(np.uint64)
+        return ((b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+
+    hi = bf16(w)
+    r1 = (w - hi).astype(np.float32)
+    mid = bf16(r1)
+    r2 = (r1 - mid).astype(np.float32)
+    lo = bf16(r2)
+    assert np.array_equal(lo, r2)
+    assert np.array_equal(hi.astype(np.float64) + mid.astype(np.float64) + lo.astype(np.float64),
+                          w.astype(np.float64))
