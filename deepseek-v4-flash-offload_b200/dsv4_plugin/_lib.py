@@ -51,6 +51,13 @@ SIGNATURES = {
     "dsv4_moe_status": (C.c_int, [_p, _p]),
     "dsv4_moe_enable_timing": (C.c_int, [_p, _i32]),
     "dsv4_moe_set_gemm_tile": (C.c_int, [_p, _i32]),
+    "dsv4_slotcache_create": (C.c_int, [C.POINTER(_p), _i64]),
+    "dsv4_slotcache_destroy": (C.c_int, [_p]),
+    "dsv4_slotcache_lookup": (C.c_int, [_p, _p, _p, _i64, _p, _p]),
+    "dsv4_slotcache_slot_of": (_i32, [_p, _i64, _i64]),
+    "dsv4_slotcache_stats": (C.c_int, [_p, _p]),
+    "dsv4_slotcache_snapshot": (C.c_int, [_p, _p, _p, _p, _i64, _p]),
+    "dsv4_slotcache_clear": (C.c_int, [_p]),
     "dsv4_ep_dispatch_pack": (C.c_int, [_p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p]),
     "dsv4_ep_ipc_handle_bytes": (C.c_int, []),
     "dsv4_ep_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i64, _i32, _p]),

@@ -22,59 +22,100 @@ test parity; the routed-expert kernels never use it.
 from __future__ import annotations
 
 import collections
+import ctypes
 import os
 
+import numpy as np
 import torch
 
 KEYS6 = ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")
 
 
 class SlotLRU:
-    """LRU bookkeeping of (layer, eid) -> slot index, host only.
+    """LRU bookkeeping of (layer, eid) -> slot index, host only, in the
+    library (``dsv4_slotcache_*``, csrc/slotcache.cpp).
 
     ``lookup(keys)`` returns (slots, misses) for a batch of keys that must
     all be resident at the same time: keys of the batch are never evicted by
-    other keys of the same batch."""
+    other keys of the same batch.  ``od`` is a snapshot of the resident keys
+    in LRU order (least recently used first) with their slots."""
 
     def __init__(self, capacity: int):
+        from dsv4_plugin._lib import check, lib
         self.capacity = int(capacity)
-        self.od: collections.OrderedDict = collections.OrderedDict()
-        self.free = list(range(self.capacity - 1, -1, -1))
-        self.hits = self.misses = self.evictions = 0
+        h = ctypes.c_void_p()
+        check(lib().dsv4_slotcache_create(ctypes.byref(h), self.capacity))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                from dsv4_plugin._lib import lib
+                lib().dsv4_slotcache_destroy(h)
+            except Exception:   # interpreter shutdown: the process frees it
+                pass
+            self._h = None
 
     def lookup(self, keys):
-        if len(set(keys)) > self.capacity:
+        from dsv4_plugin._lib import DSV4_ENOMEM, check, lib
+        n = len(keys)
+        lay = np.fromiter((k[0] for k in keys), dtype=np.int64, count=n)
+        exp = np.fromiter((k[1] for k in keys), dtype=np.int64, count=n)
+        slots = np.empty(n, dtype=np.int32)
+        miss = np.empty(n, dtype=np.uint8)
+        rc = lib().dsv4_slotcache_lookup(self._h, lay.ctypes.data, exp.ctypes.data, n, slots.ctypes.data,
+                                         miss.ctypes.data)
+        if rc == DSV4_ENOMEM:
             raise MemoryError(f"{len(set(keys))} experts needed at once but only {self.capacity} slots")
-        batch = set(keys)
-        slots, misses = [], []
-        for k in keys:
-            s = self.od.get(k)
-            if s is not None:
-                self.hits += 1
-                self.od.move_to_end(k)
-                slots.append(s)
-                continue
-            self.misses += 1
-            if self.free:
-                s = self.free.pop()
-            else:
-                victim = next(v for v in self.od if v not in batch)
-                s = self.od.pop(victim)
-                self.evictions += 1
-            self.od[k] = s
-            slots.append(s)
-            misses.append((k, s))
-        return slots, misses
+        check(rc)
+        sl = slots.tolist()
+        return sl, [(keys[i], sl[i]) for i in np.flatnonzero(miss).tolist()]
+
+    def slot_of(self, k) -> int:
+        from dsv4_plugin._lib import lib
+        return int(lib().dsv4_slotcache_slot_of(self._h, int(k[0]), int(k[1])))
+
+    def _stats(self):
+        from dsv4_plugin._lib import check, lib
+        out = np.zeros(4, dtype=np.int64)
+        check(lib().dsv4_slotcache_stats(self._h, out.ctypes.data))
+        return out
+
+    @property
+    def hits(self) -> int:
+        return int(self._stats()[0])
+
+    @property
+    def misses(self) -> int:
+        return int(self._stats()[1])
+
+    @property
+    def evictions(self) -> int:
+        return int(self._stats()[2])
+
+    @property
+    def od(self) -> collections.OrderedDict:
+        from dsv4_plugin._lib import check, lib
+        n = max(len(self), 1)
+        lay = np.empty(n, dtype=np.int64)
+        exp = np.empty(n, dtype=np.int64)
+        slots = np.empty(n, dtype=np.int32)
+        got = np.zeros(1, dtype=np.int64)
+        check(lib().dsv4_slotcache_snapshot(self._h, lay.ctypes.data, exp.ctypes.data, slots.ctypes.data, n,
+                                            got.ctypes.data))
+        m = int(got[0])
+        return collections.OrderedDict(((int(lay[i]), int(exp[i])), int(slots[i])) for i in range(m))
 
     def clear(self):
-        self.od.clear()
-        self.free = list(range(self.capacity - 1, -1, -1))
+        from dsv4_plugin._lib import check, lib
+        check(lib().dsv4_slotcache_clear(self._h))
 
     def __contains__(self, k):
-        return k in self.od
+        return self.slot_of(k) >= 0
 
     def __len__(self):
-        return len(self.od)
+        return int(self._stats()[3])
 
 
 class ExpertBank:
@@ -242,7 +283,7 @@ class ExpertBank:
         keys = [(layer, e) for e in range(n_experts)]
         if not all(k in self._lru for k in keys):
             return None
-        t = torch.tensor([self._lru.od[k] for k in keys], dtype=torch.int32).to(self.device)
+        t = torch.tensor([self._lru.slot_of(k) for k in keys], dtype=torch.int32).to(self.device)
         self._tables[layer] = (epoch, t)
         return t
 

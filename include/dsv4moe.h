@@ -186,6 +186,32 @@ int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offset
                          int32_t** inv, int32_t** active, int32_t** n_active);
 
 /* ------------------------------------------------------------------------ *
+ * Expert slot cache: the LRU bookkeeping of ExpertBank.get_packed
+ * (offload.py:103-129; the engine's get_packed, engine.py:90-97), host only.
+ * Maps (layer, expert) to a slot of the device arena.  A lookup serves a
+ * whole batch of keys that must be resident together: a hit moves its key
+ * to the most-recently-used end; a miss takes a free slot (0, 1, ... first)
+ * or evicts the least recently used key that is not part of the batch, and
+ * reports miss_out[i] = 1 so that the caller copies the expert's packed slot
+ * into slot_out[i].  More distinct keys than slots: DSV4_ENOMEM and nothing
+ * changes.  Not thread-safe (one cache per bank, as the reference's dict).
+ * ------------------------------------------------------------------------ */
+typedef struct dsv4_slotcache dsv4_slotcache;
+int dsv4_slotcache_create(dsv4_slotcache** out, int64_t n_slots);
+int dsv4_slotcache_destroy(dsv4_slotcache* cache);
+int dsv4_slotcache_lookup(dsv4_slotcache* cache, const int64_t* layer, const int64_t* expert, int64_t n,
+                          int32_t* slot_out, uint8_t* miss_out);
+/* slot of a resident key, or -1; does not change the LRU order */
+int32_t dsv4_slotcache_slot_of(const dsv4_slotcache* cache, int64_t layer, int64_t expert);
+/* out4 = {hits, misses, evictions, resident keys} (offload.py:135-146 stats) */
+int dsv4_slotcache_stats(const dsv4_slotcache* cache, int64_t* out4);
+/* resident keys, least recently used first (up to cap of them); *n_out = resident count */
+int dsv4_slotcache_snapshot(const dsv4_slotcache* cache, int64_t* layer_out, int64_t* expert_out,
+                            int32_t* slot_out, int64_t cap, int64_t* n_out);
+/* forget every key (ExpertBank.invalidate); the statistics are kept */
+int dsv4_slotcache_clear(dsv4_slotcache* cache);
+
+/* ------------------------------------------------------------------------ *
  * Expert-parallel dispatch packing (no counterpart in the reference, whose
  * expert-parallel size is 1, deepseek_v4.py:82).  Expert e lives on rank
  * e / (n_experts / world).  Every rank sends cap = n_tokens * topk rows to
