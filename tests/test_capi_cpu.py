@@ -98,3 +98,52 @@ def test_ops_refuse_cpu_tensors(lib):
         ops.dequant_fp4_weight(torch.zeros(4, 16, dtype=torch.uint8), torch.zeros(4, 1, dtype=torch.uint8))
     with pytest.raises(ValueError, match="no CPU path"):
         ops.route_topk(torch.zeros(2, 256, dtype=torch.bfloat16), torch.zeros(16, 256), None, 4)
+
+
+def test_slotcache_c_abi_on_cpu():
+    """The LRU slot cache is host code: batch semantics, refusal of an
+    oversized batch, snapshot order and statistics through the C ABI."""
+    import ctypes
+
+    import numpy as np
+
+    from dsv4_plugin._lib import DSV4_ENOMEM, check, lib
+    L = lib()
+    h = ctypes.c_void_p()
+    check(L.dsv4_slotcache_create(ctypes.byref(h), 3))
+
+    def lookup(keys):
+        lay = np.array([k[0] for k in keys], np.int64)
+        exp = np.array([k[1] for k in keys], np.int64)
+        slots = np.empty(len(keys), np.int32)
+        miss = np.empty(len(keys), np.uint8)
+        rc = L.dsv4_slotcache_lookup(h, lay.ctypes.data, exp.ctypes.data, len(keys), slots.ctypes.data,
+                                     miss.ctypes.data)
+        return rc, slots.tolist(), miss.tolist()
+
+    def snapshot():
+        lay, exp, sl, n = np.empty(8, np.int64), np.empty(8, np.int64), np.empty(8, np.int32), np.zeros(1, np.int64)
+        check(L.dsv4_slotcache_snapshot(h, lay.ctypes.data, exp.ctypes.data, sl.ctypes.data, 8, n.ctypes.data))
+        return [((int(lay[i]), int(exp[i])), int(sl[i])) for i in range(int(n[0]))]
+
+    def stats():
+        out = np.zeros(4, np.int64)
+        check(L.dsv4_slotcache_stats(h, out.ctypes.data))
+        return out.tolist()
+
+    try:
+        assert lookup([(0, 1), (0, 2), (0, 1)]) == (0, [0, 1, 0], [1, 1, 0])   # free slots 0, 1, ... first
+        assert snapshot() == [((0, 2), 1), ((0, 1), 0)]                       # LRU first
+        assert lookup([(5, 7)]) == (0, [2], [1])
+        rc, slots, miss = lookup([(5, 7), (0, 9), (0, 2)])                    # (0, 9) evicts (0, 1), not (0, 2)
+        assert rc == 0 and miss == [0, 1, 0] and slots == [2, 0, 1]
+        assert L.dsv4_slotcache_slot_of(h, 0, 1) == -1 and L.dsv4_slotcache_slot_of(h, 0, 9) == 0
+        assert stats() == [3, 4, 1, 3]                                         # hits, misses, evictions, resident
+        before = snapshot()
+        assert lookup([(1, 1), (1, 2), (1, 3), (1, 4)])[0] == DSV4_ENOMEM      # 4 keys, 3 slots
+        assert snapshot() == before and stats() == [3, 4, 1, 3]                # nothing changed
+        check(L.dsv4_slotcache_clear(h))
+        assert snapshot() == [] and stats() == [3, 4, 1, 0]
+        assert lookup([(2, 2)]) == (0, [0], [1])
+    finally:
+        L.dsv4_slotcache_destroy(h)
