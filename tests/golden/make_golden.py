@@ -16,6 +16,9 @@ shims, and writes small ``.npz`` fixtures beside this script:
     quant stub is this build's MXFP4 rule (so the a4w4 fixture pins the
     plugin's data flow, not the closed NPU op's rounding).
 
+``--only route_cfg1`` writes just the config-1 routing fixture
+(``route_cfg1.npz``) and leaves the others as they are.
+
 Large inputs (expert weights) are not stored: they come from the seeded
 generator in ``dsv4_plugin/synthetic.py`` and the fixture stores their
 SHA-256 so a test can detect generator drift.  The fixtures are consumed by
@@ -145,9 +148,40 @@ def from_f32_bf16(a: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16)
 
 
+def make_route_cfg1(DV4, S):
+    """Config-1-sized routing through the reference plugin's own ``_route``
+    (deepseek_v4.py:118-148): sqrtsoftplus scores, the Zipf-shaped bias,
+    renormalisation and route_scale 1.5, at T = 64 and 512.  The inputs come
+    from the seeded generator; the fixture stores their SHA-256 and the
+    outputs only (``route_cfg1.npz``)."""
+    cfg = S.CFG1
+    gw, bias = S.make_gate(cfg, 0)
+    out = {}
+    for T in (64, 512):
+        x = S.make_tokens(cfg, 0, T)
+        m = DV4.OffloadDeepseekV4MoE.__new__(DV4.OffloadDeepseekV4MoE)
+        nn.Module.__init__(m)
+        m.hash = False
+        m.topk = cfg.topk
+        m.renormalize = cfg.renormalize
+        m.scoring_func = cfg.score_func
+        m.routed_scaling_factor = 1.5
+        m.n_routed_experts = cfg.n_experts
+        m.layer_idx = 0
+        m.gate = types.SimpleNamespace(weight=torch.from_numpy(gw), e_score_correction_bias=torch.from_numpy(bias),
+                                       tid2eid=None)
+        w, i = m._route(from_f32_bf16(x), None)
+        out[f"t{T}_sha"] = np.frombuffer(bytes.fromhex(_sha(gw, bias, x)), dtype=np.uint8)
+        out[f"t{T}_w"] = w.numpy().copy()
+        out[f"t{T}_idx"] = i.numpy().astype(np.int64)
+    np.savez_compressed(os.path.join(HERE, "route_cfg1.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", choices=["route_cfg1"], default=None,
+                    help="write only this fixture (the others stay as they are)")
     args = ap.parse_args()
     os.environ["DSV4_PIN_HOST"] = "0"
     sys.path.insert(0, args.ref)
@@ -161,6 +195,10 @@ def main():
     import dsv4_plugin.core.engine as ENG  # noqa: E402
     S = _load_synthetic()
     torch.set_num_threads(8)
+    if args.only == "route_cfg1":
+        make_route_cfg1(DV4, S)
+        print("wrote route_cfg1.npz to", HERE)
+        return
 
     # ---------------------------------------------------------------- ops
     rng = np.random.default_rng(20240601)

@@ -123,6 +123,24 @@ def test_router_hash_matches_reference(layer0):
         O.route(x, g["sq_gate_w"], None, cfg.topk, tid2eid=g["hash_tid2eid"], input_ids=None)
 
 
+@pytest.mark.parametrize("T", [64, 512])
+def test_router_cfg1_matches_reference_plugin(T):
+    """Config-1-sized routing (E=256, H=4096, sqrtsoftplus, Zipf bias,
+    renormalised, x1.5): the oracle against the reference plugin's own
+    ``_route`` run on the CPU (route_cfg1.npz)."""
+    g = _load("route_cfg1.npz")
+    cfg = S.CFG1
+    gw, bias = S.make_gate(cfg, 0)
+    x = S.make_tokens(cfg, 0, T)
+    h = hashlib.sha256()
+    for a in (gw, bias, x):
+        h.update(np.ascontiguousarray(a).tobytes())
+    assert h.digest() == g[f"t{T}_sha"].tobytes(), "synthetic generator drifted from the fixture"
+    w, idx = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+    assert np.array_equal(_sets(idx), _sets(g[f"t{T}_idx"]))
+    np.testing.assert_allclose(_aligned(w, idx), _aligned(g[f"t{T}_w"], g[f"t{T}_idx"]), rtol=1e-5, atol=1e-6)
+
+
 def _rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
