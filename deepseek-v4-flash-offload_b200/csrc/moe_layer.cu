@@ -623,17 +623,19 @@ static int prepare_gemm() {
 // (DSV4_GEMM_BN=64|112), else by batch size.  A 112-token tile issues 1.75x
 // fewer MMA instructions per token than a 64-token one, at the cost of more
 // padding rows per expert group (and, with FP8 activations, a 4-stage ring
-// instead of 5).  Decode batches (a few rows per expert) take 64; from 16
-// assignments per expert on average (T = 512 at top-8 of 256) the wide
-// tile, measured 1.08x faster on the a4w4 layer at T = 512, 1.17x at 2048.
-static int gemm_bn(int plan_bn, int64_t assignments, int n_experts) {
+// instead of 5).  Decode batches (a few rows per expert) take 64.  a4w4
+// (packed operands, an 8-stage ring at both widths) takes the wide tile from
+// 16 assignments per expert on average (T = 512 at top-8 of 256): measured
+// 1.08x faster on the layer at T = 512, 1.17x at 2048.  The bf16 profile,
+// which gives up a ring stage for it, from 32 per expert.
+static int gemm_bn(int plan_bn, int64_t assignments, int n_experts, bool packed) {
   static const int env_bn = [] {
     const char* e = getenv("DSV4_GEMM_BN");
     return e ? atoi(e) : 0;
   }();
   if (plan_bn == 64 || plan_bn == 112) return plan_bn;
   if (env_bn == 64 || env_bn == 112) return env_bn;
-  return assignments >= 16 * (int64_t)n_experts ? 112 : 64;
+  return assignments >= (packed ? 16 : 32) * (int64_t)n_experts ? 112 : 64;
 }
 
 template <bool B_FP4, int EPI>
@@ -750,7 +752,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   cudaStream_t st = (cudaStream_t)stream;
   const WsLayout& w = p->wl;
   const int P = (int)(n_tokens * p->topk);
-  const int bn = gemm_bn(p->gemm_tile, P, p->E);   // GEMM tile = expert-group padding
+  const int bn = gemm_bn(p->gemm_tile, P, p->E, profile == DSV4_PROFILE_A4W4);   // GEMM tile = group padding
   int* status = wsp<int>(p, w.status);
   int32_t* sorted_flat = wsp<int32_t>(p, w.sorted_flat);
   int32_t* inv = wsp<int32_t>(p, w.inv);

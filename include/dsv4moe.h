@@ -177,7 +177,8 @@ int dsv4_moe_enable_timing(dsv4_moe_plan* plan, int32_t enable);
 int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
 /* Tokens per GEMM tile (no counterpart in the reference): 64 or 112, or 0
  * for the library's choice (112 when the batch has at least 16 assignments
- * per expert, else 64; the environment variable DSV4_GEMM_BN overrides it).  The tile is also the padding of each expert's row group.
+ * per expert with a4w4, 32 with bf16, else 64; the environment variable
+ * DSV4_GEMM_BN overrides it).  The tile is also the padding of each expert's row group.
  * Takes effect from the next dsv4_moe_forward on the plan. */
 int dsv4_moe_set_gemm_tile(dsv4_moe_plan* plan, int32_t tokens_per_tile);
 /* Device pointers of the plan's align outputs (valid after a forward):
