@@ -98,6 +98,8 @@ int dsv4_act_quant_mxfp4(const void* x_bf16, int64_t rows, int64_t cols, uint8_t
  * bf16 terms that sum to it exactly (DSV4_ROUTE_TC=0 keeps the FP32 pipes).
  * If a device-side wait of the tensor-core kernel runs out, every index is
  * written as n_experts (out of range) so that the layer's align rejects it.
+ * dsv4_route_workspace_bytes covers both paths: the fp32 partial logits, and
+ * from 256 tokens also the three bf16 gate terms (6 * n_experts * hidden B).
  * ------------------------------------------------------------------------ */
 int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts);
 int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
