@@ -374,12 +374,15 @@ __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log
 // (t, e) in slice order and applies the score function; warp 0 then takes
 // the biased top-k (ties to the lower expert id, as torch.topk on the
 // reference's CPU path), or reads the hash table, and writes the unbiased
-// weights, renormalised and scaled.
+// weights, renormalised and scaled.  A hash-table token id outside
+// [0, vocab) reads nothing: its picks are written as expert id E (out of
+// range), which the layer's align rejects with DSV4_EINVAL.
 __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int split, int64_t T,
                                                          int E, int K, int score_func, int renorm, float scale,
                                                          const float* __restrict__ bias,
                                                          const int32_t* __restrict__ tid2eid,
-                                                         const int64_t* __restrict__ ids, float* __restrict__ w_out,
+                                                         const int64_t* __restrict__ ids, int64_t vocab,
+                                                         float* __restrict__ w_out,
                                                          int32_t* __restrict__ i_out, const int* __restrict__ err) {
   constexpr int PER = RT_MAX_E / 32;
   __shared__ float sc_s[RT_MAX_E], ch_s[RT_MAX_E];
@@ -447,7 +450,8 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
   for (int r = 0; r < K; ++r) {
     int pick;
     if (tid2eid) {
-      pick = tid2eid[ids[t] * K + r];
+      const int64_t id = ids[t];
+      pick = (id >= 0 && id < vocab) ? tid2eid[id * K + r] : E;
     } else {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
@@ -484,7 +488,8 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
   float ssum = 0.f;
   for (int r = 0; r < K; ++r) ssum += __shfl_sync(0xffffffffu, wsel, r);
   if (lane < K) {
-    const float v = renorm ? wsel / ssum : wsel;
+    // a rejected hash row (picks E) gets weight 0, not 0 / 0
+    const float v = (isel >= E) ? 0.f : (renorm ? wsel / ssum : wsel);
     w_out[t * K + lane] = v * scale;
     i_out[t * K + lane] = isel;
   }
@@ -532,17 +537,18 @@ extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, 
 }
 
 extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
-                               const int64_t* input_ids, int64_t n_tokens, int32_t hidden, int32_t n_experts,
-                               int32_t topk, int32_t score_func, int32_t renormalize, float route_scale,
-                               float* weights_out, int32_t* indices_out, void* workspace, int64_t workspace_bytes,
-                               void* stream) {
+                               const int64_t* input_ids, int64_t vocab_size, int64_t n_tokens, int32_t hidden,
+                               int32_t n_experts, int32_t topk, int32_t score_func, int32_t renormalize,
+                               float route_scale, float* weights_out, int32_t* indices_out, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out && workspace, "null pointer");
   DSV4_CHECK_ARG(hidden > 0 && hidden % 1024 == 0, "hidden must be a positive multiple of 1024");
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
-  DSV4_CHECK_ARG(!tid2eid || input_ids, "hash routing needs input_ids");
+  DSV4_CHECK_ARG(!tid2eid || (input_ids && vocab_size > 0), "hash routing needs input_ids and vocab_size");
+  DSV4_CHECK_ARG(n_tokens >= 0, "n_tokens must not be negative");
   DSV4_CHECK_ARG(workspace_bytes >= dsv4_route_workspace_bytes(n_tokens, hidden, n_experts),
                  "workspace too small");
   if (n_tokens == 0) return DSV4_OK;
@@ -600,7 +606,7 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
   }
   DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl, logits, split,
                            n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
-                           weights_out, indices_out, err));
+                           vocab_size, weights_out, indices_out, err));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
@@ -635,8 +641,9 @@ float* g_noalloc_ptr[kMaxDevices] = {};
 }  // namespace
 
 extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float* bias,
-                                       const int32_t* tid2eid, const int64_t* input_ids, int64_t n_tokens,
-                                       int32_t hidden, int32_t n_experts, int32_t topk, int32_t score_func,
+                                       const int32_t* tid2eid, const int64_t* input_ids, int64_t vocab_size,
+                                       int64_t n_tokens, int32_t hidden, int32_t n_experts, int32_t topk,
+                                       int32_t score_func,
                                        int32_t renormalize, float route_scale, float* weights_out,
                                        int32_t* indices_out, void* stream) {
   DSV4_API_BEGIN
@@ -645,7 +652,7 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
   DSV4_CHECK_ARG(n_experts > 0 && n_experts <= RT_MAX_E, "n_experts must be in [1, 256]");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= n_experts, "topk must be in [1, min(16, n_experts)]");
   DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
-  DSV4_CHECK_ARG(!tid2eid || input_ids, "hash routing needs input_ids");
+  DSV4_CHECK_ARG(!tid2eid || (input_ids && vocab_size > 0), "hash routing needs input_ids and vocab_size");
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens * (int64_t)n_experts <= DSV4_ROUTE_NOALLOC_MAX_LOGITS,
                  "n_tokens * n_experts exceeds the fixed scratch of " +
                      std::to_string(DSV4_ROUTE_NOALLOC_MAX_LOGITS) +
@@ -671,7 +678,7 @@ extern "C" int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, 
                                             hidden / RT_SPLIT_NOALLOC);
   route_topk_kernel<<<(unsigned)n_tokens, 256, 0, st>>>(
       scratch, RT_SPLIT_NOALLOC, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
-      weights_out, indices_out, nullptr);
+      vocab_size, weights_out, indices_out, nullptr);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

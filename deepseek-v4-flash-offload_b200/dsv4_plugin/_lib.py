@@ -39,10 +39,10 @@ SIGNATURES = {
     "dsv4_act_quant_fp8_rt": (C.c_int, [_p, _i64, _i64, _p]),
     "dsv4_act_quant_mxfp4": (C.c_int, [_p, _i64, _i64, _p, _p, _p]),
     "dsv4_route_workspace_bytes": (_i64, [_i64, _i32, _i32]),
-    "dsv4_route_topk": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _i64,
-                                  _p]),
-    "dsv4_route_topk_noalloc": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _p, _p,
-                                          _p]),
+    "dsv4_route_topk": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _p, _p, _p,
+                                  _i64, _p]),
+    "dsv4_route_topk_noalloc": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _p,
+                                          _p, _p]),
     "dsv4_moe_align": (C.c_int, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32, _i64]),
     "dsv4_moe_plan_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i32, _i64, _f32, _p, _i64, _p, _i64]),

@@ -108,7 +108,7 @@ def route_topk(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor | 
     check(lib().dsv4_route_topk(
         x.data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(),
         None if tid2eid is None else tid2eid.data_ptr(), None if input_ids is None else input_ids.data_ptr(),
-        t, h, e, topk, SCORE_FUNCS[score_func], int(bool(renormalize)), float(route_scale),
+        0 if tid2eid is None else tid2eid.shape[0], t, h, e, topk, SCORE_FUNCS[score_func], int(bool(renormalize)), float(route_scale),
         wo.data_ptr(), io.data_ptr(), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         _stream(x.device)))
     return wo, io

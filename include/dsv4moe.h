@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define DSV4_ABI_VERSION 1
+#define DSV4_ABI_VERSION 2
 
 #define DSV4_OK 0
 #define DSV4_EINVAL (-1)      /* bad shape, pointer or argument */
@@ -90,7 +90,9 @@ int dsv4_act_quant_mxfp4(const void* x_bf16, int64_t rows, int64_t cols, uint8_t
 /* ------------------------------------------------------------------------ *
  * Router: OffloadDeepseekV4MoE._route (deepseek_v4.py:118-148).
  * logits = float(x) @ gate_w^T; scores by score_func; experts = top-k of
- * scores + bias (or tid2eid[input_ids] when tid2eid != NULL); weights =
+ * scores + bias (or tid2eid[input_ids] when tid2eid != NULL, the table
+ * [vocab_size, topk]; a token id outside [0, vocab_size) gets expert id
+ * n_experts for every pick, which the layer's align rejects); weights =
  * unbiased scores, renormalised when renormalize != 0, times route_scale.
  * Indices come out in descending biased-score order (ties: lower id first).
  * The logits are fp32: decode batches on the FP32 pipes; from 256 tokens
@@ -103,25 +105,30 @@ int dsv4_act_quant_mxfp4(const void* x_bf16, int64_t rows, int64_t cols, uint8_t
  * ------------------------------------------------------------------------ */
 int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts);
 int dsv4_route_topk(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
-                    const int64_t* input_ids, int64_t n_tokens, int32_t hidden, int32_t n_experts, int32_t topk,
-                    int32_t score_func, int32_t renormalize, float route_scale, float* weights_out,
-                    int32_t* indices_out, void* workspace, int64_t workspace_bytes, void* stream);
+                    const int64_t* input_ids, int64_t vocab_size, int64_t n_tokens, int32_t hidden,
+                    int32_t n_experts, int32_t topk, int32_t score_func, int32_t renormalize, float route_scale,
+                    float* weights_out, int32_t* indices_out, void* workspace, int64_t workspace_bytes,
+                    void* stream);
 
 /* Router that allocates nothing; it has no counterpart in the reference.
  * For callers that cannot allocate device memory at routing time (a serving
  * engine whose cache pool already holds nearly all free HBM, or a C caller
- * without a device allocator).  Same arguments and results as
- * dsv4_route_topk minus the workspace: the logits scratch is a fixed
- * 1 MiB device array inside the library, so n_tokens * n_experts must not
- * exceed DSV4_ROUTE_NOALLOC_MAX_LOGITS (larger calls return DSV4_EINVAL).
+ * without a device allocator).  Same arguments as dsv4_route_topk minus
+ * the workspace.  Its results equal dsv4_route_topk's up to the fp32
+ * summation order of the logits (it adds 4 partial sums of H/4 each, the
+ * workspace router H/128 of them, or uses the tensor cores from 256
+ * tokens), so an expert pair whose biased scores tie to within rounding
+ * may be picked differently.  The logits scratch is a fixed 1 MiB device
+ * array inside the library, so n_tokens * n_experts must not exceed
+ * DSV4_ROUTE_NOALLOC_MAX_LOGITS (larger calls return DSV4_EINVAL).
  * The first call on a device resolves the array's address on that device;
  * make it before any stream capture.  All calls share the array: calls that
  * overlap on the GPU race on it. */
 #define DSV4_ROUTE_NOALLOC_MAX_LOGITS 65536
 int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
-                            const int64_t* input_ids, int64_t n_tokens, int32_t hidden, int32_t n_experts,
-                            int32_t topk, int32_t score_func, int32_t renormalize, float route_scale,
-                            float* weights_out, int32_t* indices_out, void* stream);
+                            const int64_t* input_ids, int64_t vocab_size, int64_t n_tokens, int32_t hidden,
+                            int32_t n_experts, int32_t topk, int32_t score_func, int32_t renormalize,
+                            float route_scale, float* weights_out, int32_t* indices_out, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * moe_align (deepseek_v4.py:154-164): stable counting sort of the T*k

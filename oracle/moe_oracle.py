@@ -115,6 +115,11 @@ def e2m1_code(v: np.ndarray) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # weight dequant (npu_ops.py:132-158)
 # ---------------------------------------------------------------------------
+# byte -> (value of the low nibble, value of the high nibble), as one 8-byte word
+_BYTE_PAIRS = np.ascontiguousarray(np.stack([FP4_TABLE[np.arange(256) & 0xF], FP4_TABLE[np.arange(256) >> 4]],
+                                            axis=-1)).view(np.uint64).reshape(256)
+
+
 def dequant_fp4_weight(w_packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
     """[N, K//2] packed E2M1 + [N, K//32] E8M0 -> float32 [N, K].
 
@@ -125,11 +130,11 @@ def dequant_fp4_weight(w_packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
     """
     u = w_packed.view(np.uint8)
     n, kh = u.shape
-    vals = np.empty((n, kh * 2), dtype=np.float32)
-    vals[:, 0::2] = FP4_TABLE[u & 0xF]
-    vals[:, 1::2] = FP4_TABLE[u >> 4]
+    # one gather per byte through a 256-entry table of value pairs (low nibble first)
+    vals = np.take(_BYTE_PAIRS, u).view(np.float32).reshape(n, kh * 2 // 32, 32)
     s = e8m0_to_f32(scale.view(np.uint8))
-    return (vals.reshape(n, -1, 32) * s[:, :, None]).reshape(n, kh * 2)
+    vals *= s[:, :, None]
+    return vals.reshape(n, kh * 2)
 
 
 # ---------------------------------------------------------------------------
@@ -373,3 +378,52 @@ class LruModel:
 
     def keys(self):
         return list(self.od.keys())
+
+
+class SlotLruModel:
+    """Packed-slot LRU of ``ExpertBank.get_packed`` (offload.py:103-129) as a
+    batch: the reference calls ``get_packed`` once per active expert of a
+    layer (deepseek_v4.py:216) and keeps the tensors of that layer alive in
+    Python, so its OrderedDict may evict a key of the same layer.  A slot
+    arena cannot: every expert of a layer must sit in its own slot while the
+    layer's kernels run.  So a lookup walks the layer's keys in the given
+    order, a hit moves its key to the most-recently-used end, and a miss
+    takes a free slot (lowest index first) or evicts the least recently used
+    key that is NOT part of the batch.  ``lookup`` returns (slots, missed
+    keys).  When no batch is at risk of evicting itself the hit / miss /
+    eviction counts equal ``LruModel``'s on the same key sequence
+    (``self_evictions_avoided`` counts the cases where they differ)."""
+
+    def __init__(self, capacity: int):
+        from collections import OrderedDict
+        self.capacity = int(capacity)
+        self.od = OrderedDict()          # key -> slot, least recently used first
+        self.free = list(range(self.capacity))
+        self.hits = self.misses = self.evictions = 0
+        self.self_evictions_avoided = 0
+
+    def lookup(self, keys):
+        batch = set(keys)
+        if len(batch) > self.capacity:
+            raise MemoryError(f"{len(batch)} experts needed at once but only {self.capacity} slots")
+        slots, missed = [], []
+        for k in keys:
+            if k in self.od:
+                self.hits += 1
+                self.od.move_to_end(k)
+                slots.append(self.od[k])
+                continue
+            self.misses += 1
+            if self.free:
+                s = self.free.pop(0)
+            else:
+                lru = next(iter(self.od))
+                if lru in batch:
+                    self.self_evictions_avoided += 1
+                victim = next(v for v in self.od if v not in batch)
+                s = self.od.pop(victim)
+                self.evictions += 1
+            self.od[k] = s
+            slots.append(s)
+            missed.append(k)
+        return slots, missed

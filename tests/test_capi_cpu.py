@@ -32,7 +32,7 @@ def test_exports_every_header_symbol(lib):
     assert not missing, missing
     # the ctypes table covers the header exactly
     assert sorted(lib.SIGNATURES) == names
-    assert lib.lib().dsv4_abi_version() == 1
+    assert lib.lib().dsv4_abi_version() == 2
 
 
 def test_slot_bytes(lib):

@@ -108,6 +108,47 @@ def test_route_golden_cfg0(ops):
     np.testing.assert_allclose(w.cpu().numpy(), g["hash_w"], rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("T", [64, 512])
+def test_route_cfg1_matches_reference_plugin(ops, T):
+    """Config 1 (E=256, H=4096, sqrtsoftplus, Zipf bias, renormalised):
+    the GPU router against the reference plugin's own ``_route`` run on the
+    CPU (route_cfg1.npz).  T=512 takes the tensor-core logits kernel."""
+    g = _gold("route_cfg1.npz")
+    cfg = S.CFG1
+    gw, bias = S.make_gate(cfg, 0)
+    x = S.make_tokens(cfg, 0, T)
+    w, i = ops.route_topk(bf16_tensor(x), torch.from_numpy(gw).cuda(), torch.from_numpy(bias).cuda(), cfg.topk,
+                          cfg.score_func, cfg.renormalize)
+    i, w = i.cpu().numpy(), w.cpu().numpy()
+    assert np.array_equal(_sets(i), _sets(g[f"t{T}_idx"]))
+    np.testing.assert_allclose(np.take_along_axis(w, np.argsort(i, -1), -1),
+                               np.take_along_axis(g[f"t{T}_w"], np.argsort(g[f"t{T}_idx"], -1), -1),
+                               rtol=1e-5, atol=1e-6)
+
+
+def test_route_hash_rejects_token_ids_outside_the_table(ops):
+    """A token id outside [0, vocab) reads no table row: its picks come out
+    as expert id E, which the layer's align rejects (the reference raises
+    an IndexError on the host for the same input)."""
+    cfg = S.CFG0
+    vocab = 50
+    rng = np.random.default_rng(3)
+    tid2eid = rng.integers(0, cfg.n_experts, size=(vocab, cfg.topk)).astype(np.int32)
+    ids = np.array([0, 49, 50, -1, 7, 1 << 40], dtype=np.int64)
+    x = bf16_tensor(S.make_tokens(cfg, 1, len(ids)))
+    gw = torch.from_numpy(S.make_gate(cfg, 0)[0]).cuda()
+    w, i = ops.route_topk(x, gw, None, cfg.topk, "sqrtsoftplus", True, tid2eid=torch.from_numpy(tid2eid).cuda(),
+                          input_ids=torch.from_numpy(ids).cuda())
+    i = i.cpu().numpy()
+    for t, tok in enumerate(ids.tolist()):
+        if 0 <= tok < vocab:
+            assert np.array_equal(i[t], tid2eid[tok])
+        else:
+            assert np.all(i[t] == cfg.n_experts)
+    al = ops.moe_align(torch.from_numpy(i).cuda(), cfg.n_experts)
+    assert int(al["status"].item()) == -1   # DSV4_EINVAL
+
+
 @pytest.mark.parametrize("T", [1, 8, 64, 255, 300, 2048])
 def test_route_cfg1_matches_oracle(ops, T):
     """Decode sizes run the 64 x 64 split-K kernel, from 256 tokens the

@@ -1,0 +1,152 @@
+"""GPU parity of the plugin's own layer, ``OffloadDeepseekV4MoE.forward``,
+against the CPU oracle of the reference's per-expert path.
+
+* config 1 (decode, H=4096, I=2048, E=256, top-8): the whole forward
+  (router + routed experts) in both profiles;
+* config 2 (prefill, T=2048, a4w4): the tensor-core router, the 112-token
+  GEMM tile and experts with many row chunks at full K.  Every token's
+  routing is checked; the outputs of a subset of tokens are checked against
+  the oracle (a token's output depends only on its own row and routing), and
+  the a4w4 output is compared with the bf16 profile's by the reference's own
+  acceptance statistic (test_moe_align.py:55-56, 180-191), scaled by the
+  bf16 output's largest magnitude because the synthetic weights are not the
+  checkpoint's;
+* the offload miss path: fewer HBM slots than experts, several steps issued
+  back to back with changing routing, so that slots are evicted and
+  refilled while earlier steps' kernels may still run; every step's output
+  against the oracle and the hit / miss / eviction counts against the batch
+  LRU model of offload.py:103-129.
+
+Tolerance: max |gpu - oracle| <= 1e-2 * max |oracle| (the oracle accumulates
+in fp32), for both profiles."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from dsv4_plugin import synthetic as S
+
+from helpers import bf16_tensor, bf16_to_np, make_plugin_layer, rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+LAYER = 3
+# an offload layer small enough for the oracle: config-0 dims, 64 experts, top-8
+CFG_MISS = S.MoEConfig("miss", 1024, 512, 64, 8, "sqrtsoftplus", True, zipf_s=1.1, zipf_bias_scale=0.3)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _profile(flag: bool):
+    from dsv4_plugin.models import deepseek_v4 as DV4
+    DV4._MXFP4_GMM = flag
+
+
+def _sets(a):
+    return np.sort(np.asarray(a), axis=-1)
+
+
+def _route_oracle(cfg, x, seed=0):
+    gw, bias = S.make_gate(cfg, seed, LAYER)
+    return O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize, cfg.route_scale)
+
+
+@pytest.mark.parametrize("T", [8, 64])
+def test_plugin_forward_cfg1_matches_oracle(dev, T):
+    cfg = S.CFG1
+    x = S.make_tokens(cfg, 21, T)
+    w, idx = _route_oracle(cfg, x)
+    need = sorted(set(idx.reshape(-1).tolist()))
+    experts = {e: S.make_expert(cfg, 0, e, LAYER) for e in need}
+    moe, eng = make_plugin_layer(cfg, experts, dev, layer_idx=LAYER)
+    xt = bf16_tensor(x)
+    try:
+        for flag, profile in ((False, "bf16"), (True, "a4w4")):
+            _profile(flag)
+            y = moe.forward(xt)
+            torch.cuda.synchronize()
+            ref = O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, profile)
+            assert rel_err(bf16_to_np(y), ref) <= TOL, profile
+    finally:
+        _profile(False)
+    gw_, gi_ = moe._route(xt, None)
+    assert np.array_equal(_sets(gi_.cpu().numpy()), _sets(idx))
+
+
+def test_plugin_forward_cfg2_a4w4_prefill(dev):
+    cfg = S.CFG1           # config 2 shares config 1's dims and router
+    T = 2048
+    x = S.make_tokens(cfg, 22, T)
+    w, idx = _route_oracle(cfg, x)
+    experts = {e: S.make_expert(cfg, 0, e, LAYER) for e in range(cfg.n_experts)}
+    moe, eng = make_plugin_layer(cfg, experts, dev, layer_idx=LAYER)
+    xt = bf16_tensor(x)
+    # the tensor-core router: every token's picks
+    gw_, gi_ = moe._route(xt, None)
+    gi_, gw_ = gi_.cpu().numpy(), gw_.cpu().numpy()
+    assert np.array_equal(_sets(gi_), _sets(idx))
+    np.testing.assert_allclose(np.take_along_axis(gw_, np.argsort(gi_, -1), -1),
+                               np.take_along_axis(w, np.argsort(idx, -1), -1), rtol=1e-5, atol=1e-6)
+    counts = np.bincount(idx.reshape(-1), minlength=cfg.n_experts)
+    assert counts.max() > 112, "the test needs experts with several 112-row chunks"
+    try:
+        _profile(True)
+        y4 = bf16_to_np(moe.forward(xt))
+        _profile(False)
+        y16 = bf16_to_np(moe.forward(xt))
+    finally:
+        _profile(False)
+    plan = eng.plan_for(cfg.n_experts, cfg.topk, T, cfg.swiglu_limit)
+    plan.status()
+    # tokens spread over the batch, plus the tokens of the most loaded expert's last chunk
+    heavy = int(np.argmax(counts))
+    rows_heavy = np.nonzero((idx == heavy).any(-1))[0]
+    sub = np.unique(np.concatenate([np.linspace(0, T - 1, 8).astype(int), rows_heavy[-4:]]))
+    deq = {}   # the subset's experts dequantised once for both profiles
+    ref4 = O.moe_routed(x[sub], w[sub], idx[sub], experts, cfg.n_experts, cfg.swiglu_limit, "a4w4", deq_cache=deq)
+    assert rel_err(y4[sub], ref4) <= TOL
+    ref16 = O.moe_routed(x[sub], w[sub], idx[sub], experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=deq)
+    assert rel_err(y16[sub], ref16) <= TOL
+    deq.clear()
+    # the reference's a4w4-vs-bf16 acceptance (max_abs < 0.35, mean < 0.08 on
+    # the checkpoint), relative to the bf16 output's largest magnitude
+    d = np.abs(y4.astype(np.float64) - y16)
+    scale = float(np.abs(y16).max())
+    print(f"a4w4 vs bf16 at T={T}: max_abs/ref_absmax={d.max() / scale:.4f} mean/ref_absmax={d.mean() / scale:.4f}")
+    assert d.max() / scale < 0.35 and d.mean() / scale < 0.08
+
+
+def test_offload_miss_path_matches_oracle_and_lru_model(dev):
+    """24 HBM slots for 64 experts; eight steps of 3 tokens (at most 24
+    distinct experts each) issued back to back, both profiles alternating."""
+    cfg = CFG_MISS
+    experts = {e: S.make_expert(cfg, 0, e, LAYER) for e in range(cfg.n_experts)}
+    moe, eng = make_plugin_layer(cfg, experts, dev, layer_idx=LAYER, slots=24)
+    steps = [S.make_tokens(cfg, 40 + s, 3) for s in range(8)]
+    xs = [bf16_tensor(x) for x in steps]
+    outs = []
+    try:
+        for s, xt in enumerate(xs):
+            _profile(s % 2 == 1)
+            outs.append(moe.forward(xt))
+    finally:
+        _profile(False)
+    torch.cuda.synchronize()
+    model = O.SlotLruModel(24)
+    deq = {}
+    for s, x in enumerate(steps):
+        w, idx = _route_oracle(cfg, x)
+        model.lookup([(LAYER, int(e)) for e in sorted(set(idx.reshape(-1).tolist()))])
+        ref = O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, "a4w4" if s % 2 else "bf16",
+                           deq_cache=deq)
+        assert rel_err(bf16_to_np(outs[s]), ref) <= TOL, f"step {s}"
+    st = eng.bank.stats()
+    assert model.evictions > 0, "the trace must evict"
+    assert (st["packed_hits"], st["packed_misses"], st["packed_evictions"]) == \
+        (model.hits, model.misses, model.evictions)

@@ -72,6 +72,24 @@ def test_slot_lru_random_against_oracle_model():
         assert (lru.hits, lru.misses, lru.evictions) == (ref.hits, ref.misses, ref.evictions)
 
 
+def test_slot_lru_batches_against_oracle_model():
+    """Whole-layer batches (sorted, distinct keys, as a layer's active
+    experts): slots, misses and counts equal the batch model's."""
+    from dsv4_plugin.core.bank import SlotLRU
+    rng = np.random.default_rng(11)
+    for cap in (8, 24, 40):
+        lru, ref = SlotLRU(cap), O.SlotLruModel(cap)
+        for _ in range(300):
+            layer = int(rng.integers(0, 3))
+            n = int(rng.integers(1, min(cap, 24) + 1))
+            keys = [(layer, int(e)) for e in sorted(rng.choice(64, n, replace=False).tolist())]
+            s1, m1 = lru.lookup(keys)
+            s2, m2 = ref.lookup(keys)
+            assert s1 == s2 and [k for k, _ in m1] == m2
+        assert (lru.hits, lru.misses, lru.evictions) == (ref.hits, ref.misses, ref.evictions)
+        assert list(lru.od.items()) == list(ref.od.items())
+
+
 def _six(seed, h=256, i=128):
     g = torch.Generator().manual_seed(seed)
     pk = lambda n, k: torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g)  # noqa: E731

@@ -42,7 +42,7 @@ def _route(L, noalloc, cfg, xt, gw, bias):
     w = torch.empty((T, cfg.topk), dtype=torch.float32, device="cuda")
     i = torch.empty((T, cfg.topk), dtype=torch.int32, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
-    args = (xt.data_ptr(), gw.data_ptr(), bias.data_ptr(), None, None, T, cfg.hidden, cfg.n_experts, cfg.topk,
+    args = (xt.data_ptr(), gw.data_ptr(), bias.data_ptr(), None, None, 0, T, cfg.hidden, cfg.n_experts, cfg.topk,
             2, 1, cfg.route_scale, w.data_ptr(), i.data_ptr())
     if noalloc:
         L.check(L.lib().dsv4_route_topk_noalloc(*args, s))
@@ -71,7 +71,7 @@ def test_noalloc_router_refuses_batches_beyond_its_scratch(L):
     gw = torch.zeros((cfg.n_experts, cfg.hidden), dtype=torch.float32, device="cuda")
     w = torch.empty((T, cfg.topk), dtype=torch.float32, device="cuda")
     i = torch.empty((T, cfg.topk), dtype=torch.int32, device="cuda")
-    rc = L.lib().dsv4_route_topk_noalloc(xt.data_ptr(), gw.data_ptr(), None, None, None, T, cfg.hidden,
+    rc = L.lib().dsv4_route_topk_noalloc(xt.data_ptr(), gw.data_ptr(), None, None, None, 0, T, cfg.hidden,
                                          cfg.n_experts, cfg.topk, 2, 1, 1.5, w.data_ptr(), i.data_ptr(),
                                          torch.cuda.current_stream().cuda_stream)
     assert rc == L.DSV4_EINVAL
