@@ -58,6 +58,16 @@ SIGNATURES = {
     "dsv4_slotcache_stats": (C.c_int, [_p, _p]),
     "dsv4_slotcache_snapshot": (C.c_int, [_p, _p, _p, _p, _i64, _p]),
     "dsv4_slotcache_clear": (C.c_int, [_p]),
+    "dsv4_slotdir_workspace_bytes": (_i64, [_i32, _i32, _i64]),
+    "dsv4_slotdir_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _p, _i64, _i64, _p, _i64]),
+    "dsv4_slotdir_destroy": (C.c_int, [_p]),
+    "dsv4_slotdir_set_sources": (C.c_int, [_p, _i64, _p, _p, _p]),
+    "dsv4_slotdir_acquire": (C.c_int, [_p, _i32, _p, _i64, _i32, _p]),
+    "dsv4_slotdir_table": (C.c_int, [_p, _i32, C.POINTER(_p)]),
+    "dsv4_slotdir_stats": (C.c_int, [_p, _p, _p]),
+    "dsv4_slotdir_status": (C.c_int, [_p, _p]),
+    "dsv4_slotdir_snapshot": (C.c_int, [_p, _p, _p, _p]),
+    "dsv4_slotdir_clear": (C.c_int, [_p, _p]),
     "dsv4_ep_dispatch_pack": (C.c_int, [_p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p]),
     "dsv4_ep_ipc_handle_bytes": (C.c_int, []),
     "dsv4_ep_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i64, _i32, _p]),

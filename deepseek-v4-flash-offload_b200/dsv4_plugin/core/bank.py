@@ -118,6 +118,108 @@ class SlotLRU:
         return int(self._stats()[3])
 
 
+class _DevView:
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+class SlotDirectory:
+    """The bank's LRU kept on the device (``dsv4_slotdir_*``,
+    csrc/slotdir.cu): same semantics as ``SlotLRU``, but the router's expert
+    ids never leave the GPU.  ``acquire`` enqueues, on a stream, the lookup of
+    a layer's batch and the GPU's own copies of the missed experts from the
+    page-locked host pool, so an offloaded layer has no host synchronisation
+    and can be captured in a CUDA graph.  ``table(layer)`` is the device
+    expert -> slot table the grouped GEMM reads."""
+
+    DEMAND, PREFETCH = 0, 1
+    MAX_SLOTS = 32768
+
+    def __init__(self, arena: torch.Tensor, n_layers: int, n_experts: int):
+        from dsv4_plugin._lib import check, lib
+        self.n_layers, self.n_experts = int(n_layers), int(n_experts)
+        self.n_slots, self.slot_bytes = int(arena.shape[0]), int(arena.shape[1])
+        self.device = arena.device
+        nb = lib().dsv4_slotdir_workspace_bytes(self.n_layers, self.n_experts, self.n_slots)
+        if nb < 0:
+            check(int(nb))
+        self.workspace = torch.empty(int(nb), dtype=torch.uint8, device=self.device)
+        h = ctypes.c_void_p()
+        check(lib().dsv4_slotdir_create(ctypes.byref(h), self.n_layers, self.n_experts, arena.data_ptr(),
+                                        self.n_slots, self.slot_bytes, self.workspace.data_ptr(), int(nb)))
+        self._h = h
+        self._arena = arena
+        self._tables = {}
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                from dsv4_plugin._lib import lib
+                lib().dsv4_slotdir_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    def set_sources(self, items):
+        """items: iterable of (layer, expert, page-locked host slot tensor)."""
+        from dsv4_plugin._lib import check, lib
+        items = [(int(L), int(e), t) for L, e, t in items if 0 <= int(L) < self.n_layers]
+        if not items:
+            return
+        lay = np.array([i[0] for i in items], dtype=np.int32)
+        exp = np.array([i[1] for i in items], dtype=np.int32)
+        ptrs = (ctypes.c_void_p * len(items))(*[i[2].data_ptr() for i in items])
+        check(lib().dsv4_slotdir_set_sources(self._h, len(items), lay.ctypes.data, exp.ctypes.data, ptrs))
+
+    def acquire(self, layer: int, indices: torch.Tensor, mode: int = 0, stream=None):
+        from dsv4_plugin._lib import check, lib
+        idx = indices if indices.dtype == torch.int32 and indices.is_contiguous() else \
+            indices.contiguous().to(torch.int32)
+        st = stream or torch.cuda.current_stream(self.device)
+        check(lib().dsv4_slotdir_acquire(self._h, int(layer), idx.data_ptr(), idx.numel(), int(mode),
+                                         st.cuda_stream))
+        return idx
+
+    def table(self, layer: int) -> torch.Tensor:
+        t = self._tables.get(int(layer))
+        if t is None:
+            from dsv4_plugin._lib import check, lib
+            p = ctypes.c_void_p()
+            check(lib().dsv4_slotdir_table(self._h, int(layer), ctypes.byref(p)))
+            t = torch.as_tensor(_DevView(p.value, self.n_experts, "<i4"), device=self.device)
+            self._tables[int(layer)] = t
+        return t
+
+    def counters(self, stream=None) -> dict:
+        from dsv4_plugin._lib import check, lib
+        out = np.zeros(8, dtype=np.int64)
+        st = stream or torch.cuda.current_stream(self.device)
+        check(lib().dsv4_slotdir_stats(self._h, out.ctypes.data, st.cuda_stream))
+        names = ("hits", "misses", "evictions", "prefetch_hits", "prefetch_fetched", "prefetch_evictions",
+                 "prefetch_skipped", "acquires")
+        return dict(zip(names, (int(v) for v in out)))
+
+    def status(self, stream=None) -> None:
+        from dsv4_plugin._lib import check, lib
+        st = stream or torch.cuda.current_stream(self.device)
+        check(lib().dsv4_slotdir_status(self._h, st.cuda_stream))
+
+    def snapshot(self, stream=None):
+        """(keys [S] int32 = layer * n_experts + expert or -1, stamps [S] int64)."""
+        from dsv4_plugin._lib import check, lib
+        keys = np.empty(self.n_slots, dtype=np.int32)
+        stamps = np.empty(self.n_slots, dtype=np.int64)
+        st = stream or torch.cuda.current_stream(self.device)
+        check(lib().dsv4_slotdir_snapshot(self._h, keys.ctypes.data, stamps.ctypes.data, st.cuda_stream))
+        return keys, stamps
+
+    def clear(self, stream=None):
+        from dsv4_plugin._lib import check, lib
+        st = stream or torch.cuda.current_stream(self.device)
+        check(lib().dsv4_slotdir_clear(self._h, st.cuda_stream))
+
+
 class ExpertBank:
     """Host-resident packed experts + device LRU slot cache.
 
@@ -157,6 +259,11 @@ class ExpertBank:
         self._tables = {}               # layer -> (epoch, device slot table)
         self._epoch = 0
         self._all_event = None
+        self._dir = None                # SlotDirectory when the bank offloads with device-side lookups
+        self._prefetch_stream = None
+        self._prefetch_done = None      # event: the last prefetch enqueued on the side stream
+        # DSV4_DEVICE_LRU=0 keeps the host LRU (one synchronisation per layer)
+        self.device_lru = os.environ.get("DSV4_DEVICE_LRU", "1") != "0"
 
     # -- host pool ----------------------------------------------------------
     @property
@@ -194,6 +301,7 @@ class ExpertBank:
             dst = self._new_host_slot()
         ops.pack_expert(w1p, w1s, w2p, w2s, w3p, w3s, self.hidden, self.inter, out=dst)
         self._host[key] = dst
+        self._new_source(key, dst)
         if key in self._lru:        # stale device copy
             self.invalidate()
 
@@ -210,6 +318,7 @@ class ExpertBank:
             dst = self._new_host_slot()
         dst.copy_(slot.reshape(-1))
         self._host[key] = dst
+        self._new_source(key, dst)
         if key in self._lru:
             self.invalidate()
 
@@ -271,6 +380,88 @@ class ExpertBank:
             (stream or torch.cuda.current_stream(self.device)).wait_event(done)
         return slots
 
+    # -- device-side LRU ------------------------------------------------------
+    def _new_source(self, key, host_slot):
+        if self._dir is not None:
+            if key[0] >= self._dir.n_layers:
+                self._dir = None            # rebuilt, larger, at the next acquire
+                self.invalidate()
+            else:
+                self._dir.set_sources([(key[0], key[1], host_slot)])
+                if key[0] in self._dir_touched:   # an older copy of the expert may be resident
+                    self.invalidate()
+
+    def offloading(self) -> bool:
+        """True when the registered experts do not all fit the HBM budget,
+        so slots get evicted and refilled during forwards."""
+        return len(self._host) > self.packed_capacity
+
+    def device_directory(self, n_experts: int):
+        """The device-side LRU (created on first use), or None when the pool
+        is not page-locked (the GPU can only read pinned host memory) or
+        ``DSV4_DEVICE_LRU=0``."""
+        if not (self.device_lru and self.pin and self.device.type == "cuda"):
+            return None
+        if self.packed_capacity > SlotDirectory.MAX_SLOTS:
+            return None
+        if self._dir is None:
+            if not all(t.is_pinned() for t in self._host.values()):
+                return None
+            n_layers = max([k[0] for k in self._host if k[0] >= 0] + [0]) + 1
+            self._lru.clear()               # the directory starts empty: one owner of the arena
+            self._tables.clear()
+            torch.cuda.synchronize(self.device)
+            self._dir = SlotDirectory(self.arena, n_layers, n_experts)
+            self._dir.set_sources((L, e, t) for (L, e), t in self._host.items() if L >= 0)
+            self._dir_touched = set()
+        return self._dir
+
+    def acquire(self, layer: int, indices: torch.Tensor, stream=None) -> torch.Tensor:
+        """Device path of ``ensure_resident``: make the experts named by the
+        router's ``indices`` (device [T, k]) resident, on ``stream``, without
+        reading them on the host.  Waits (on the device) for the last
+        prefetch first.  Returns the layer's device expert -> slot table."""
+        d = self._dir
+        st = stream or torch.cuda.current_stream(self.device)
+        if self._prefetch_done is not None:
+            st.wait_event(self._prefetch_done)
+            self._prefetch_done = None
+        d.acquire(layer, indices, SlotDirectory.DEMAND, st)
+        self._dir_touched.add(int(layer))
+        return d.table(layer)
+
+    def prefetch_stream(self):
+        if self._prefetch_stream is None:
+            self._prefetch_stream = torch.cuda.Stream(device=self.device)
+        return self._prefetch_stream
+
+    def prefetch(self, layer: int, predict, stream=None) -> None:
+        """Copy the experts that ``predict()`` (called on the side stream,
+        returns device [T, k] expert ids) names for ``layer`` while the
+        current stream keeps computing.  The next ``acquire`` waits for it on
+        the device.  The prefetch never evicts the experts of the demand batch
+        in flight."""
+        d = self._dir
+        if d is None or not 0 <= int(layer) < d.n_layers:
+            return
+        cur = stream or torch.cuda.current_stream(self.device)
+        side = self.prefetch_stream()
+        fork = torch.cuda.Event()
+        fork.record(cur)
+        side.wait_event(fork)
+        with torch.cuda.stream(side):
+            idx = predict()
+            d.acquire(layer, idx, SlotDirectory.PREFETCH, side)
+            done = torch.cuda.Event()
+            done.record(side)
+        self._dir_touched.add(int(layer))
+        self._prefetch_done = done
+
+    def join_prefetch(self, stream=None) -> None:
+        if self._prefetch_done is not None:
+            (stream or torch.cuda.current_stream(self.device)).wait_event(self._prefetch_done)
+            self._prefetch_done = None
+
     def resident_table(self, layer, n_experts):
         """Device int32 [n_experts] expert -> slot table of ``layer`` when
         every expert of the layer is resident, else None.  Built once per
@@ -294,6 +485,8 @@ class ExpertBank:
         self._need_cuda()
         torch.cuda.synchronize(self.device)
         self._arena = None
+        self._dir = None
+        self._prefetch_done = None
         self.packed_capacity = int(packed_capacity)
         self._lru = SlotLRU(self.packed_capacity)
         self._slot_events.clear()
@@ -363,23 +556,39 @@ class ExpertBank:
     def invalidate(self):
         self._cache.clear()
         self._lru.clear()
+        if self._dir is not None:
+            self.join_prefetch()
+            self._dir.clear()
+            self._dir_touched = set()
         self._slot_events.clear()
         self._all_event = None
         self._tables.clear()
         self._epoch += 1
 
     def stats(self):
+        """offload.py:135-146 keys; the packed_* counters come from the
+        device directory when the bank offloads through it (synchronises)."""
         tot = self.hits + self.misses
         lru = self._lru
-        ptot = lru.hits + lru.misses
+        ph, pm, pe, pc = lru.hits, lru.misses, lru.evictions, len(lru)
+        h2d_b, h2d_n = self.h2d_bytes, self.h2d_copies
+        extra = {}
+        if self._dir is not None:
+            c = self._dir.counters()
+            keys, _ = self._dir.snapshot()
+            ph, pm, pe, pc = ph + c["hits"], pm + c["misses"], pe + c["evictions"], int((keys >= 0).sum())
+            fetched = c["misses"] + c["prefetch_fetched"]
+            h2d_b, h2d_n = h2d_b + fetched * self.slot_bytes, h2d_n + fetched
+            extra = {"device_lru": True, **{k: v for k, v in c.items() if k.startswith("prefetch")}}
+        ptot = ph + pm
         return {"hits": self.hits, "misses": self.misses, "evictions": self.evictions,
                 "hit_rate": (self.hits / tot) if tot else 0.0,
                 "cached": len(self._cache), "capacity": self.capacity,
-                "packed_hits": lru.hits, "packed_misses": lru.misses,
-                "packed_hit_rate": (lru.hits / ptot) if ptot else 0.0,
-                "packed_cached": len(lru), "packed_capacity": self.packed_capacity,
-                "packed_evictions": lru.evictions,
-                "pinned": self.pin, "h2d_bytes": self.h2d_bytes, "h2d_copies": self.h2d_copies}
+                "packed_hits": ph, "packed_misses": pm,
+                "packed_hit_rate": (ph / ptot) if ptot else 0.0,
+                "packed_cached": pc, "packed_capacity": self.packed_capacity,
+                "packed_evictions": pe,
+                "pinned": self.pin, "h2d_bytes": h2d_b, "h2d_copies": h2d_n, **extra}
 
     def __repr__(self):
         s = self.stats()

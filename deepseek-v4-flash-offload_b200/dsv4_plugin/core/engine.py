@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import os
 import re
+import weakref
 
 import torch
 
@@ -51,6 +52,9 @@ class ExpertOffloadEngine:
         self._pending = {}
         self.captured = 0
         self._plans = {}
+        self._layers = {}
+        # DSV4_PREFETCH=0: no next-layer prefetch on the side stream
+        self.prefetch = os.environ.get("DSV4_PREFETCH", "1") != "0"
 
     def capture(self, name: str, tensor: torch.Tensor) -> bool:
         """Park one expert tensor; register the expert once all six arrived."""
@@ -65,6 +69,14 @@ class ExpertOffloadEngine:
             del self._pending[(layer, eid)]
             self.captured += 1
         return True
+
+    def register_layer(self, layer: int, module) -> None:
+        """MoE layers register here so that a layer can warm the next one."""
+        self._layers[int(layer)] = weakref.ref(module)
+
+    def layer(self, layer: int):
+        r = self._layers.get(int(layer))
+        return r() if r is not None else None
 
     def get(self, layer: int, eid: int):
         return self.bank.get(layer, eid)

@@ -125,10 +125,11 @@ class OffloadDeepseekV4MoE(nn.Module):
             self.gate.e_score_correction_bias = nn.Parameter(
                 torch.zeros(config.n_routed_experts, dtype=torch.float32), requires_grad=False)
         self.engine = get_engine()
+        self.engine.register_layer(self.layer_idx, self)
         self.experts = _ExpertsFacade(self)
 
     # -- routing ------------------------------------------------------------
-    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None):
+    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None, out=None):
         """(weights fp32 [T, k], indices int32 [T, k]); deepseek_v4.py:118-148."""
         tid2eid = getattr(self.gate, "tid2eid", None) if self.hash else None
         if self.hash and input_ids is None:
@@ -136,11 +137,19 @@ class OffloadDeepseekV4MoE(nn.Module):
         bias = None if self.hash else getattr(self.gate, "e_score_correction_bias", None)
         return ops.route_topk(hs, self.gate.weight, bias, self.topk, self.scoring_func, self.renormalize,
                               self.routed_scaling_factor, tid2eid=tid2eid,
-                              input_ids=input_ids if self.hash else None)
+                              input_ids=input_ids if self.hash else None, out=out)
 
     # -- routed experts -------------------------------------------------------
     def _slot_table(self, indices: torch.Tensor):
+        """(device expert -> slot table, slots to mark as read or None).
+
+        Every expert resident: the bank's static table.  Offloading with a
+        page-locked pool: the device-side LRU (``ExpertBank.acquire``), no
+        host synchronisation.  Otherwise the host LRU, which needs the active
+        experts on the host (one synchronisation per layer)."""
         bank = self.engine.bank
+        if bank.offloading() and bank.device_directory(self.n_routed_experts) is not None:
+            return bank.acquire(self.layer_idx, indices), None
         table = bank.resident_table(self.layer_idx, self.n_routed_experts)
         if table is not None:
             return table, None
@@ -150,22 +159,42 @@ class OffloadDeepseekV4MoE(nn.Module):
         host[torch.tensor(active, dtype=torch.long)] = torch.tensor(slots, dtype=torch.int32)
         return host.to(indices.device, non_blocking=True), slots
 
-    def _routed_experts(self, hs, weights, indices, profile):
+    def _prefetch_next(self, hs: torch.Tensor, input_ids):
+        """Warm the next layer's predicted experts while this layer computes
+        (the reference's planned prefetch, DESIGN.md:82 there): the next
+        layer's gate applied to this layer's hidden states, or its hash table
+        on the same token ids, on the bank's side stream."""
+        bank = self.engine.bank
+        nxt = self.engine.layer(self.layer_idx + 1) if self.engine.prefetch else None
+        if nxt is None or bank._dir is None or (nxt.hash and input_ids is None):
+            return
+        t, k = hs.shape[0], nxt.topk
+        # outputs allocated on this stream (graph-capture safe), used on the side stream
+        pw = torch.empty((t, k), dtype=torch.float32, device=hs.device)
+        pi = torch.empty((t, k), dtype=torch.int32, device=hs.device)
+        side = bank.prefetch_stream()
+        for x in (hs, pw, pi):
+            x.record_stream(side)
+        bank.prefetch(self.layer_idx + 1, lambda: nxt._route(hs, input_ids, out=(pw, pi))[1])
+
+    def _routed_experts(self, hs, weights, indices, profile, input_ids=None):
         slot_of, slots = self._slot_table(indices)
+        if slots is None and self.engine.bank._dir is not None:
+            self._prefetch_next(hs, input_ids)
         plan = self.engine.plan_for(self.n_routed_experts, self.topk, hs.shape[0], self.swiglu_limit or 0.0)
         y = plan.forward(hs, weights, indices, slot_of, profile)
-        if not torch.cuda.is_current_stream_capturing():
+        if slots is not None and not torch.cuda.is_current_stream_capturing():
             self.engine.bank.mark_used(slots)
         return y
 
     def _routed(self, hs: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
         """Routed-expert output [T, H] bf16; profile from ``_MXFP4_GMM``."""
         weights, indices = self._route(hs, input_ids)
-        return self._routed_experts(hs, weights, indices, "a4w4" if _MXFP4_GMM else "bf16")
+        return self._routed_experts(hs, weights, indices, "a4w4" if _MXFP4_GMM else "bf16", input_ids)
 
     def _routed_mxfp4(self, hs: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
         weights, indices = self._route(hs, input_ids)
-        return self._routed_experts(hs, weights, indices, "a4w4")
+        return self._routed_experts(hs, weights, indices, "a4w4", input_ids)
 
     def forward(self, hidden_states: torch.Tensor, input_ids=None) -> torch.Tensor:
         num_tokens, hidden_dim = hidden_states.shape

@@ -83,8 +83,9 @@ def dynamic_mx_quant(x: torch.Tensor):
 def route_topk(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor | None, topk: int,
                score_func: str = "sqrtsoftplus", renormalize: bool = True, route_scale: float = 1.5,
                tid2eid: torch.Tensor | None = None, input_ids: torch.Tensor | None = None,
-               workspace: torch.Tensor | None = None):
-    """Router of the MoE layer.  Returns (weights fp32 [T,k], indices int32 [T,k])."""
+               workspace: torch.Tensor | None = None, out=None):
+    """Router of the MoE layer.  Returns (weights fp32 [T,k], indices int32 [T,k]),
+    written into ``out`` = (weights, indices) when given."""
     _need_cuda(x, gate_weight, bias, tid2eid, input_ids)
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
@@ -103,8 +104,14 @@ def route_topk(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor | 
     need = lib().dsv4_route_workspace_bytes(t, h, e)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=x.device)
-    wo = torch.empty((t, topk), dtype=torch.float32, device=x.device)
-    io = torch.empty((t, topk), dtype=torch.int32, device=x.device)
+    if out is not None:
+        wo, io = out
+        if (wo.shape != (t, topk) or io.shape != (t, topk) or wo.dtype != torch.float32 or io.dtype != torch.int32
+                or not (wo.is_contiguous() and io.is_contiguous())):
+            raise ValueError("out must be contiguous (float32 [T, k], int32 [T, k]) tensors")
+    else:
+        wo = torch.empty((t, topk), dtype=torch.float32, device=x.device)
+        io = torch.empty((t, topk), dtype=torch.int32, device=x.device)
     check(lib().dsv4_route_topk(
         x.data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(),
         None if tid2eid is None else tid2eid.data_ptr(), None if input_ids is None else input_ids.data_ptr(),

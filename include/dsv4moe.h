@@ -222,6 +222,54 @@ int dsv4_slotcache_snapshot(const dsv4_slotcache* cache, int64_t* layer_out, int
 int dsv4_slotcache_clear(dsv4_slotcache* cache);
 
 /* ------------------------------------------------------------------------ *
+ * Device-resident slot directory: the same LRU as the dsv4_slotcache_*
+ * calls (the packed-expert cache of ExpertBank.get_packed,
+ * offload.py:103-129, one layer's batch at a time), kept in HBM so that an
+ * offloaded layer never waits for the host.  dsv4_slotdir_acquire enqueues on `stream`:
+ *   resolve: the layer's [T*k] expert ids (-1 = empty) are walked in
+ *     ascending id order; hits move to the most-recently-used end, misses
+ *     take a free slot (lowest first) or evict the least recently used key
+ *     outside the batch; the (layer, expert) -> slot table is updated;
+ *   fetch: each missed expert is copied by the GPU from its page-locked host
+ *     slot (registered with dsv4_slotdir_set_sources; the host memory must be
+ *     mapped for the device, as all cudaHostAlloc memory is under unified
+ *     addressing) into its arena slot.
+ * dsv4_slotdir_table gives the device table of a layer (int32 [n_experts],
+ * slot or -1), the slot_of_expert argument of dsv4_moe_forward.
+ * Mode DSV4_SLOTDIR_PREFETCH (predicted experts of a later layer, typically
+ * on a side stream while the current layer computes) evicts only slots older
+ * than the last DEMAND batch and skips what does not fit; the caller orders
+ * each demand acquire after the previous prefetch (an event) and each
+ * prefetch after the demand acquire it must not disturb.  Counters (int64 x 8):
+ * demand hits, misses, evictions; prefetch hits, fetched, evictions,
+ * skipped; acquire calls.  A demand batch with more distinct experts than
+ * slots records DSV4_ENOMEM (dsv4_slotdir_status) and changes nothing.
+ * ------------------------------------------------------------------------ */
+#define DSV4_SLOTDIR_DEMAND 0
+#define DSV4_SLOTDIR_PREFETCH 1
+#define DSV4_SLOTDIR_MAX_SLOTS 32768
+typedef struct dsv4_slotdir dsv4_slotdir;
+int64_t dsv4_slotdir_workspace_bytes(int32_t n_layers, int32_t n_experts, int64_t n_slots);
+int dsv4_slotdir_create(dsv4_slotdir** out, int32_t n_layers, int32_t n_experts, uint8_t* slot_arena,
+                        int64_t n_slots, int64_t slot_bytes, void* workspace, int64_t workspace_bytes);
+int dsv4_slotdir_destroy(dsv4_slotdir* dir);
+/* host (page-locked) address of each (layer, expert) packed slot; host arrays */
+int dsv4_slotdir_set_sources(dsv4_slotdir* dir, int64_t n, const int32_t* layers, const int32_t* experts,
+                             const void* const* host_slots);
+int dsv4_slotdir_acquire(dsv4_slotdir* dir, int32_t layer, const int32_t* indices, int64_t n_assign, int32_t mode,
+                         void* stream);
+int dsv4_slotdir_table(dsv4_slotdir* dir, int32_t layer, int32_t** slot_of_out);
+/* synchronises `stream`, then reads the eight counters */
+int dsv4_slotdir_stats(dsv4_slotdir* dir, int64_t* out8, void* stream);
+/* synchronises `stream`; returns and clears the directory's status word */
+int dsv4_slotdir_status(dsv4_slotdir* dir, void* stream);
+/* synchronises `stream`; per slot the key (layer * n_experts + expert, or -1)
+ * and the recency stamp (larger = more recent, 0 = free) */
+int dsv4_slotdir_snapshot(dsv4_slotdir* dir, int32_t* slot_key_out, int64_t* stamp_out, void* stream);
+/* forget every resident key (asynchronous on `stream`); counters are kept */
+int dsv4_slotdir_clear(dsv4_slotdir* dir, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Expert-parallel dispatch packing (no counterpart in the reference, whose
  * expert-parallel size is 1, deepseek_v4.py:82).  Expert e lives on rank
  * e / (n_experts / world).  Every rank sends cap = n_tokens * topk rows to

@@ -150,3 +150,64 @@ def test_offload_miss_path_matches_oracle_and_lru_model(dev):
     assert model.evictions > 0, "the trace must evict"
     assert (st["packed_hits"], st["packed_misses"], st["packed_evictions"]) == \
         (model.hits, model.misses, model.evictions)
+
+
+def _dir_fixture(dev, n_layers, n_experts, n_slots, slot_bytes=4096):
+    from dsv4_plugin.core.bank import SlotDirectory
+    arena = torch.zeros((n_slots, slot_bytes), dtype=torch.uint8, device=dev)
+    g = torch.Generator().manual_seed(5)
+    pool = torch.randint(0, 256, (n_layers * n_experts, slot_bytes), dtype=torch.uint8, generator=g).pin_memory()
+    d = SlotDirectory(arena, n_layers, n_experts)
+    d.set_sources((k // n_experts, k % n_experts, pool[k]) for k in range(n_layers * n_experts))
+    return d, arena, pool
+
+
+def test_device_lru_matches_host_lru_model(dev):
+    """The device directory against the batch LRU model: same slot for every
+    key of every batch, same counters, and each resident slot holds the
+    bytes of its key, copied by the GPU from page-locked host memory."""
+    L, E, S = 3, 64, 40
+    d, arena, pool = _dir_fixture(dev, L, E, S)
+    model = O.SlotLruModel(S)
+    rng = np.random.default_rng(8)
+    for it in range(60):
+        layer = int(rng.integers(0, L))
+        t, k = int(rng.integers(1, 6)), 8
+        idx = rng.integers(0, E, size=(t, k)).astype(np.int32)
+        idx[rng.random(idx.shape) < 0.05] = -1          # empty assignments are ignored
+        d.acquire(layer, torch.from_numpy(idx).to(dev))
+        keys = sorted(set(int(e) for e in idx.reshape(-1) if e >= 0))
+        slots, _ = model.lookup([(layer, e) for e in keys])
+        table = d.table(layer).cpu().numpy()
+        assert [int(table[e]) for e in keys] == slots, f"batch {it}"
+    c = d.counters()
+    assert (c["hits"], c["misses"], c["evictions"]) == (model.hits, model.misses, model.evictions)
+    assert model.self_evictions_avoided > 0
+    skeys, _ = d.snapshot()
+    host = arena.cpu()
+    for s, key in enumerate(skeys.tolist()):
+        if key >= 0:
+            assert torch.equal(host[s], pool[key]), f"slot {s}"
+    assert sorted(model.od.values()) == sorted(int(s) for s in np.nonzero(skeys >= 0)[0])
+    d.status()
+
+
+def test_device_lru_prefetch_spares_the_batch_in_flight(dev):
+    """A prefetch may only evict slots older than the last demand batch: with
+    the arena full, a prefetch after a demand batch skips what it cannot
+    place instead of evicting that batch."""
+    from dsv4_plugin.core.bank import SlotDirectory
+    E, S = 32, 12
+    d, arena, pool = _dir_fixture(dev, 2, E, S)
+    d.acquire(0, torch.arange(0, 4, dtype=torch.int32, device=dev))        # old residents 0..3
+    demand = torch.arange(4, 12, dtype=torch.int32, device=dev)            # fills the arena
+    d.acquire(0, demand)
+    d.acquire(1, torch.arange(0, 8, dtype=torch.int32, device=dev), SlotDirectory.PREFETCH)
+    c = d.counters()
+    assert c["prefetch_fetched"] == 4 and c["prefetch_skipped"] == 4 and c["prefetch_evictions"] == 4
+    t0 = d.table(0).cpu().numpy()
+    assert np.all(t0[4:12] >= 0) and np.all(t0[0:4] < 0)   # the in-flight batch survived
+    skeys, _ = d.snapshot()
+    host = arena.cpu()
+    for s, key in enumerate(skeys.tolist()):
+        assert key >= 0 and torch.equal(host[s], pool[key])
