@@ -395,6 +395,26 @@ def run_ours(a):
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": 7 * a.steps, "launch_mode": "CUDA graph replay per step (7 kernels)",
             "detail": detail}
+    if not a.no_detail:
+        # the other BASELINE configurations on this GPU, after the headline's
+        # resources are released: config 4 at one GPU (the strong-scaling base
+        # of --gpus N) and config 3 (offloaded decode through the plugin's forward)
+        from dsv4_plugin.core import engine as ENG
+        del g, xs, ys, moe, eng, plan
+        ENG.reset_engine(None)
+        torch.cuda.synchronize(device)
+        torch.cuda.empty_cache()
+        for key, fn in (("config4_1gpu", lambda: ep_config4(a, 0, 1, device, steps=max(3, a.steps // 2), warmup=3)),
+                        ("config3_offload", lambda: offload_bench(device))):
+            try:
+                detail[key] = fn()
+            except Exception as exc:   # a detail must not cost the headline line
+                import traceback
+                traceback.print_exc()
+                detail[key] = {"error": f"{type(exc).__name__}: {exc}"[:500]}
+            ENG.reset_engine(None)
+            torch.cuda.synchronize(device)
+            torch.cuda.empty_cache()
     print(json.dumps(line), flush=True)
 
 
@@ -581,134 +601,231 @@ def pinned_h2d_gbs(device, nbytes=1 << 30):
     return 3 * nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9
 
 
-def run_offload(a):
-    """8 MoE layers (config-1 dims), every expert of every
-    layer in a pinned host pool, HBM slot budgets of 512 and 2048 packed
-    slots with LRU eviction, routing from the trace above (256 decode steps
-    x 8 sequences).  A step runs the 8 layers on the 8 tokens; each layer
-    makes its experts resident (misses: one H2D copy per expert on the copy
-    stream, which the compute stream waits for) and runs the routed-expert
-    kernels.  With --prefetch the next layer's misses are issued before the
-    current layer's kernels, so the copies overlap them (the experts are
-    taken from the trace, i.e. a perfect predictor: an upper bound for a
-    prefetch driven by the next layer's gate)."""
-    import numpy as np
+def _offload_layers(device, L: int, E: int, budget: int, base_payloads: int = 16):
+    """Engine with every expert of L layers in the page-locked host pool
+    (``base_payloads`` distinct synthetic experts copied into every host
+    slot) and an HBM budget of ``budget`` slots, plus one
+    OffloadDeepseekV4MoE per layer built through the plugin's constructor.
+    Gate l has a one-hot row per expert on the hidden columns
+    [256 l, 256 l + E), so a hidden state with value 4 on the columns of a
+    set of experts routes exactly that set at layer l."""
+    import types
+
     import torch
 
     from dsv4_plugin import synthetic as S
     from dsv4_plugin.core import engine as ENG
-    rank, world, local = _dist()
-    device = torch.device(f"cuda:{local}")
-    torch.cuda.set_device(device)
+    from dsv4_plugin.models import deepseek_v4 as DV4
     c = _cfg()
-    L, T, E, K = 8, 8, c.n_experts, c.topk
-    n_steps = 256
-    slot = c.packed_expert_bytes()
-    need = L * E * slot
-    note = ""
-    try:
-        import psutil
-        avail = psutil.virtual_memory().available
-        if avail < 1.5 * need:
-            L = max(1, int(avail / 1.5 / (E * slot)))
-            note = f"host pool reduced to {L} layers: {avail / 2**30:.0f} GiB host memory available"
-    except ImportError:
-        pass
-    eng = ENG.ExpertOffloadEngine(slot_capacity=0, device=device, packed_capacity=2048)
+    eng = ENG.ExpertOffloadEngine(slot_capacity=0, device=device, packed_capacity=budget)
     bank = eng.bank
     bank.pin = True
     base = []
-    t0 = time.perf_counter()
-    for b in range(16):   # 16 distinct experts, copied into every (layer, expert) host slot
+    for b in range(base_payloads):
         ex = S.make_expert(c, 0, b, 0)
         bank.register(0, b, *[torch.from_numpy(ex[k]) for k in ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
         base.append(bank.host_slot(0, b).clone())
     for l in range(L):
         for e in range(E):
-            if l == 0 and e < 16:
+            if l == 0 and e < base_payloads:
                 continue
-            bank.register_packed(l, e, base[(e * 7 + l) % 16])
+            bank.register_packed(l, e, base[(e * 7 + l) % base_payloads])
+    ENG.reset_engine(eng)
+    hf = types.SimpleNamespace(
+        n_routed_experts=E, n_shared_experts=None, num_experts_per_tok=c.topk, norm_topk_prob=True,
+        scoring_func="sqrtsoftplus", routed_scaling_factor=c.route_scale, swiglu_limit=c.swiglu_limit,
+        num_hash_layers=0, vocab_size=129280, hidden_size=c.hidden, moe_intermediate_size=c.inter,
+        hidden_act="silu")
+    pc = types.SimpleNamespace(use_sequence_parallel_moe=False, eplb_config=None, enable_eplb=False)
+    mods = []
+    for l in range(L):
+        m = DV4.OffloadDeepseekV4MoE(hf, pc, prefix=f"model.layers.{l}.mlp").to(device)
+        w = torch.zeros((E, c.hidden), dtype=torch.float32)
+        w[torch.arange(E), 256 * l + torch.arange(E)] = 1.0
+        m.gate.weight.data.copy_(w)
+        m.gate.e_score_correction_bias.data.zero_()
+        mods.append(m)
+    return eng, mods
+
+
+def _trace_tokens(tr, E: int, hidden: int):
+    """Hidden states [steps, T, H] (bf16, pinned) that route trace[step, l,
+    token] at every layer l through the one-hot gates of _offload_layers."""
+    import torch
+    n_steps, L, T, K = tr.shape
+    x = torch.zeros((n_steps, T, hidden), dtype=torch.bfloat16)
+    for l in range(L):
+        cols = torch.from_numpy(tr[:, l].astype("int64")) + 256 * l          # [steps, T, K]
+        x.scatter_(2, cols.reshape(n_steps, T, K), 4.0)
+    return x.pin_memory()
+
+
+def offload_bench(device, budgets=(512, 2048), n_steps: int = 256, warm: int = 16, L: int = 8,
+                  host_lru_budget: int | None = 512):
+    """BASELINE config 3 through the plugin's own forward: 8 MoE layers
+    (config-1 dims), every expert of every layer in a page-locked host pool,
+    HBM budgets of 512 and 2048 packed slots, routing from the seeded trace
+    (256 decode steps x 8 sequences; Zipf 1.1 popularity, 70 % reuse).  A
+    step copies the 8 tokens' hidden states in and runs the 8 layers.
+
+    Modes, per budget:
+      device  the device-side LRU: the GPU looks the experts up and copies
+              its misses from the pinned pool itself; no host synchronisation,
+              so the 8-layer step is one CUDA graph;
+      device+prefetch  the same, and each layer warms the next layer's
+              experts on a side stream (the next layer's gate applied to this
+              layer's hidden state; the synthetic hidden states encode every
+              layer's trace, so the predictor is perfect here: an upper bound);
+      host    the host LRU of the reference's design (one synchronisation per
+              layer, cudaMemcpyAsync of each miss on a copy stream), eager.
+    Reports tok/s, hit rate, H2D GB/s against the measured pinned peak, and
+    for device+prefetch the share of prefetch time that overlapped the
+    compute stream (CUDA-event timestamps of an eager pass)."""
+    import numpy as np
+    import torch
+
+    c = _cfg()
+    E, T, K = c.n_experts, 8, c.topk
+    slot = c.packed_expert_bytes()
+    note = ""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+        if avail < 1.5 * L * E * slot:
+            L = max(2, int(avail / 1.5 / (E * slot)))
+            note = f"host pool reduced to {L} layers: {avail / 2**30:.0f} GiB host memory available"
+    except ImportError:
+        pass
+    t0 = time.perf_counter()
+    eng, mods = _offload_layers(device, L, E, max(budgets))
+    bank = eng.bank
     setup_s = time.perf_counter() - t0
     tr = offload_trace(n_steps, L, T, E, K)
-    x0 = torch.from_numpy(S.to_bf16_bits(S.make_tokens(c, 11, T)).astype("int16")).view(torch.bfloat16).to(device)
-    g = np.random.default_rng(5)
-    wts = torch.from_numpy(g.random((n_steps, L, T, K), dtype=np.float32) + 0.1)
-    wts = (wts / wts.sum(-1, keepdim=True)).pin_memory()
-    idx_host = torch.from_numpy(tr).pin_memory()
+    xs_host = _trace_tokens(tr, E, c.hidden)
     stream = torch.cuda.current_stream(device)
     peak_h2d = pinned_h2d_gbs(device)
-    results = []
-    for budget in (512, 2048):
+    xs = torch.empty((T, c.hidden), dtype=torch.bfloat16, device=device)
+
+    def layers():
+        out = None
+        for m in mods:
+            out = m.forward(xs)
+        return out
+
+    def run_mode(budget, mode):
         eng.resize_slots(budget)
-        plan = eng.plan_for(E, K, T, c.swiglu_limit)
-        slot_host = torch.full((L, E), -1, dtype=torch.int32).pin_memory()
-        slot_dev = torch.empty((L, E), dtype=torch.int32, device=device)
-        idx_dev = torch.empty((L, T, K), dtype=torch.int32, device=device)
-        w_dev = torch.empty((L, T, K), dtype=torch.float32, device=device)
-
-        def resident(l, st):
-            act = sorted(set(tr[st, l].reshape(-1).tolist()))
-            return act, bank.ensure_resident(l, act, stream=stream)
-
-        def one_step(st):
-            idx_dev.copy_(idx_host[st], non_blocking=True)
-            w_dev.copy_(wts[st], non_blocking=True)
-            x = x0
-            nxt = resident(0, st) if a.prefetch else None
-            for l in range(L):
-                if a.prefetch:
-                    act, slots = nxt
-                else:
-                    # on demand, as the reference: the layer's routing reaches
-                    # the host (one sync), then its misses are copied
-                    stream.synchronize()
-                    act, slots = resident(l, st)
-                slot_host[l].fill_(-1)
-                slot_host[l, torch.tensor(act, dtype=torch.long)] = torch.tensor(slots, dtype=torch.int32)
-                slot_dev[l].copy_(slot_host[l], non_blocking=True)
-                if a.prefetch and l + 1 < L:
-                    nxt = resident(l + 1, st)   # its copies overlap this layer's kernels
-                x = plan.forward(x, w_dev[l], idx_dev[l], slot_dev[l], "bf16")
-                bank.mark_used(slots, stream)
-            return x
-
-        w_steps = 16
-        for st in range(w_steps):
-            one_step(st)
-            torch.cuda.synchronize(device)   # the host slot table is reused next step
+        bank.device_lru = mode != "host"
+        eng.prefetch = mode == "device+prefetch"
+        for st in range(warm):
+            xs.copy_(xs_host[st], non_blocking=True)
+            layers()
+        torch.cuda.synchronize(device)
+        g = None
+        if mode != "host":
+            gs = torch.cuda.Stream(device=device)
+            gs.wait_stream(stream)
+            with torch.cuda.stream(gs):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=gs):
+                    layers()
+            stream.wait_stream(gs)
+            torch.cuda.synchronize(device)
         s0 = bank.stats()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h0 = time.perf_counter()
         e0.record(stream)
-        for st in range(w_steps, n_steps):
-            one_step(st)
-            torch.cuda.synchronize(device)   # the host slot table is reused next step
+        for st in range(warm, n_steps):
+            xs.copy_(xs_host[st], non_blocking=True)
+            if g is not None:
+                g.replay()
+            else:
+                layers()
         e1.record(stream)
         e1.synchronize()
-        wall = time.perf_counter() - h0
         ms = e0.elapsed_time(e1)
         s1 = bank.stats()
+        n = n_steps - warm
         hits = s1["packed_hits"] - s0["packed_hits"]
         miss = s1["packed_misses"] - s0["packed_misses"]
         h2d = s1["h2d_bytes"] - s0["h2d_bytes"]
-        n = n_steps - w_steps
-        results.append({"slots": budget, "tok_s": round(T * n / (ms / 1e3), 1),
-                        "ms_per_step": round(ms / n, 4), "hit_rate": round(hits / max(1, hits + miss), 4),
-                        "misses_per_step": round(miss / n, 2), "h2d_gbs": round(h2d / (ms / 1e3) / 1e9, 2),
-                        "h2d_frac_of_pinned_peak": round(h2d / (ms / 1e3) / 1e9 / peak_h2d, 4),
-                        "host_wall_ms_per_step": round(wall / n * 1e3, 4)})
-    best = results[0]
-    line = {"metric": METRIC, "value": best["tok_s"], "unit": UNIT, "n_gpus": 1, "steps": n_steps - 16,
+        r = {"slots": budget, "mode": mode, "tok_s": round(T * n / (ms / 1e3), 1), "ms_per_step": round(ms / n, 4),
+             "hit_rate": round(hits / max(1, hits + miss), 4), "misses_per_step": round(miss / n, 2),
+             "h2d_gbs": round(h2d / (ms / 1e3) / 1e9, 2),
+             "h2d_frac_of_pinned_peak": round(h2d / (ms / 1e3) / 1e9 / peak_h2d, 4),
+             "graph": g is not None}
+        if mode == "device+prefetch":
+            r["prefetch_fetched_per_step"] = round((s1.get("prefetch_fetched", 0) - s0.get("prefetch_fetched", 0)) / n, 2)
+            # overlap of the side stream's prefetch with the compute stream (eager pass, events)
+            bank.trace = []
+            spans = []
+            for st in range(warm, warm + 8):
+                xs.copy_(xs_host[st], non_blocking=True)
+                for m in mods:
+                    a0 = torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
+                    m.forward(xs)
+                    a1 = torch.cuda.Event(enable_timing=True)
+                    a1.record(stream)
+                    spans.append((a0, a1))
+            torch.cuda.synchronize(device)
+            ref = spans[0][0]
+            comp = [(ref.elapsed_time(a), ref.elapsed_time(b)) for a, b in spans]
+            # prefetch i warms layer l of step i // (L - 1) and was issued by
+            # layer l - 1: the part of it inside that layer's span ran under
+            # its compute; the rest is time the next layer waits for
+            tot = ov = 0.0
+            for i, (l, a, b) in enumerate(bank.trace):
+                pa, pb = ref.elapsed_time(a), ref.elapsed_time(b)
+                ca, cb = comp[(i // (L - 1)) * L + l - 1]
+                tot += pb - pa
+                ov += max(0.0, min(pb, cb) - max(pa, ca))
+            n_pf = len(bank.trace)
+            bank.trace = None
+            r["prefetch_overlap_frac"] = round(ov / tot, 4) if tot > 0 else None
+            r["prefetch_ms_per_layer"] = round(tot / max(1, n_pf), 4)
+        del g
+        return r
+
+    results = []
+    for budget in budgets:
+        for mode in ("device", "device+prefetch"):
+            results.append(run_mode(budget, mode))
+    if host_lru_budget:
+        results.append(run_mode(host_lru_budget, "host"))
+    plan = eng.plan_for(E, K, T, c.swiglu_limit)
+    plan.status()
+    if bank._dir is not None:
+        bank._dir.status()
+    out = {"results": results, "pinned_h2d_peak_gbs": round(peak_h2d, 2), "setup_s": round(setup_s, 1),
+           "layers": L, "note": note,
+           "api": "OffloadDeepseekV4MoE.forward per layer (device modes: the 8-layer step replayed as one CUDA graph)"}
+    del mods, eng
+    from dsv4_plugin.core import engine as ENG
+    ENG.reset_engine(None)
+    torch.cuda.synchronize(device)
+    return out
+
+
+def run_offload(a):
+    """--workload offload: BASELINE config 3 as its own JSON line."""
+    import torch
+    rank, world, local = _dist()
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    clk = Clocks(local)
+    clk.start()
+    r = offload_bench(device)
+    clocks = clk.stop()
+    best = max((x for x in r["results"] if x["slots"] == 512), key=lambda x: x["tok_s"])
+    line = {"metric": METRIC, "value": best["tok_s"], "unit": UNIT, "n_gpus": 1, "steps": 240,
             "warmup": 16, "ms_per_step": best["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "e2m1 x e4m3 block-scaled (bf16 profile), fp32 accumulate, bf16 out",
             "data": "synthetic routing trace (seeded; BASELINE config 3), 16 distinct expert payloads",
-            "config": {"workload": f"cfg3 offloaded decode: {L} layers x {E} experts in pinned host memory, "
-                                   f"T={T} tokens (8 sequences), LRU slot budgets 512 and 2048, "
-                                   + ("next-layer prefetch" if a.prefetch else "on-demand copies"),
-                       "tokens_per_step": T, "global_batch": T, "parallelism": "single GPU",
+            "config": {"workload": f"cfg3 offloaded decode: {r['layers']} layers x 256 experts in pinned host "
+                                   "memory, T=8 tokens (8 sequences), LRU slot budgets 512 and 2048; value: "
+                                   f"512 slots, {best['mode']}",
+                       "tokens_per_step": 8, "global_batch": 8, "parallelism": "single GPU",
                        "l2": "working set (misses stream from host) larger than L2"},
-            "offload": results, "pinned_h2d_peak_gbs": round(peak_h2d, 2), "setup_s": round(setup_s, 1),
-            "note": note}
+            "offload": r, "clocks": clocks}
     print(json.dumps(line), flush=True)
 
 
@@ -755,12 +872,203 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# config 4: expert parallel on N GPUs (strong scaling of a fixed 8192-token step)
+# ---------------------------------------------------------------------------
+CFG4_TOKENS = 8192
+
+
+def _cfg4_batches(device, rank: int, world: int, n: int = 2):
+    """n seeded global batches of 8192 tokens; this rank's contiguous share
+    (T/world tokens) of each, pinned on the host and on the device."""
+    import torch
+
+    from dsv4_plugin import synthetic as S
+    c = _cfg()
+    t = CFG4_TOKENS // world
+    host, dev = [], []
+    for b in range(n):
+        x = S.make_tokens(c, 77, CFG4_TOKENS, step=b)[rank * t:(rank + 1) * t]
+        h = torch.from_numpy(S.to_bf16_bits(x).astype("int16")).view(torch.bfloat16).pin_memory()
+        host.append(h)
+        dev.append(h.to(device))
+    return host, dev
+
+
+def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), steps=None, warmup=None):
+    """BASELINE config 4: E=256 experts sharded e // (E/N) over N ranks, a
+    fixed step of 8192 tokens split evenly (T/N per rank), Zipf-skewed
+    routing, both profiles.  world == 1 runs the plain single-GPU layer (all
+    256 experts resident) on all 8192 tokens: the strong-scaling base.  For
+    N > 1 each rank routes its tokens, dispatches rows to the owners of their
+    experts over NVLink peer memory (DSV4_EP_EXCHANGE=static: NCCL
+    all-to-all), runs its experts and returns the rows; the step is one CUDA
+    graph.  Per profile: tokens/s over the whole step (8192 tokens / the
+    slowest rank's step time) and the per-segment times of an eager pass."""
+    import torch
+    import torch.distributed as dist
+
+    from dsv4_plugin.models import deepseek_v4 as DV4
+    steps = steps or a.steps
+    warmup = warmup or a.warmup
+    moe, eng = build_layer(device, rank, world)
+    host, dev = _cfg4_batches(device, rank, world)
+    T = CFG4_TOKENS // world
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    exchange = os.environ.get("DSV4_EP_EXCHANGE", "p2p")
+    epm = None
+    if world > 1:
+        from dsv4_plugin.parallel_ep import ExpertParallelMoE
+        epm = ExpertParallelMoE(moe, rank, world)
+
+    def fwd(x, profile):
+        if epm is None:
+            DV4._MXFP4_GMM = profile == "a4w4"
+            try:
+                return moe.forward(x)
+            finally:
+                DV4._MXFP4_GMM = False
+        return (epm.forward_p2p if exchange == "p2p" else epm.forward_static)(x, profile)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    out = {}
+    for profile in profiles:
+        xs = torch.empty_like(dev[0])
+        xs.copy_(dev[0])
+        for _ in range(2):
+            fwd(xs, profile)
+        torch.cuda.synchronize(device)
+        barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ys = fwd(xs, profile)
+        torch.cuda.synchronize(device)
+        y_host = torch.empty(tuple(ys.shape), dtype=ys.dtype).pin_memory()
+
+        def run(n, src, e2e=False):
+            ms = []
+            for s in range(n):
+                flush.zero_()
+                barrier()
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                xs.copy_(src[s % len(src)], non_blocking=True)
+                g.replay()
+                if e2e:
+                    y_host.copy_(ys, non_blocking=True)
+                e1.record(stream)
+                e1.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            return ms
+
+        run(warmup, dev)
+        ms = max_over_ranks(run(steps, dev))
+        run(2, host, e2e=True)
+        me = max_over_ranks(run(steps, host, e2e=True))
+        # eager pass: segment times (route / dispatch / experts / return / combine)
+        seg = {}
+        if epm is not None:
+            epm.segment_times = {}
+            for s in range(3):
+                flush.zero_()
+                barrier()
+                fwd(dev[s % len(dev)], profile)
+            seg = dict(epm.segment_times)
+            epm.segment_times = None
+            names = sorted(seg)
+            seg_max = max_over_ranks([seg[k] for k in names])
+            seg = {k: round(v, 5) for k, v in zip(names, seg_max)}
+        # this rank's routed-expert rows and active experts (load balance)
+        plan = epm.plan if epm is not None else eng.plan_for(_cfg().n_experts, _cfg().topk, T, _cfg().swiglu_limit)
+        load = [float(plan.n_active())]
+        if epm is not None:
+            load.append(float(int((epm._p2p[T].recv_meta[:, 0] >= 0).sum().item())) if exchange == "p2p" else 0.0)
+        loads = [load]
+        if world > 1:
+            buf = torch.tensor(load, dtype=torch.float64, device=device)
+            allb = [torch.empty_like(buf) for _ in range(world)]
+            dist.all_gather(allb, buf)
+            loads = [b.tolist() for b in allb]
+        tot = sum(ms)
+        out[profile] = {"tok_s": round(CFG4_TOKENS * steps / (tot / 1e3), 1), "ms_per_step": round(tot / steps, 5),
+                        "e2e_tok_s": round(CFG4_TOKENS * steps / (sum(me) / 1e3), 1),
+                        "step_ms_median": round(statistics.median(ms), 5),
+                        "segments_ms_max_over_ranks": seg,
+                        "active_experts_per_rank": [int(l[0]) for l in loads],
+                        "rows_received_per_rank": [int(l[1]) for l in loads] if world > 1 else None}
+        del g
+        torch.cuda.synchronize(device)
+    if epm is not None:
+        for ex in epm._p2p.values():
+            ex.check_status()
+    if epm is not None:
+        epm.plan.status()
+        epm.close()
+    return out
+
+
 def run_ep(a, rank, world, device):
-    from dsv4_plugin.parallel_ep import run_ep_bench
-    line = run_ep_bench(a, rank, world, device, METRIC, UNIT, build_layer, _token_batches, Clocks,
-                        L2_FLUSH_BYTES, gemm_bytes=_gemm_bytes, peaks=_peaks())
-    if rank == 0 and line is not None:
-        print(json.dumps(line), flush=True)
+    """--gpus N under torchrun: BASELINE config 4 at N ranks.  value = bf16
+    tokens/s of the whole 8192-token step (slowest rank); rank 0 then runs
+    the same 8192 tokens on its GPU alone (all 256 experts) so that the line
+    carries the strong-scaling ratio of this exact workload."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
+    clk = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    clk.start()
+    r = ep_config4(a, rank, world, device)
+    clocks = clk.stop()
+    dist.barrier()
+    one = None
+    if rank == 0:
+        from dsv4_plugin.core import engine as ENG
+        ENG.reset_engine(None)
+        torch.cuda.empty_cache()
+        one = ep_config4(a, 0, 1, device, steps=max(3, a.steps // 2), warmup=3)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    c = _cfg()
+    h = c.hidden
+    T = CFG4_TOKENS // world
+    bf = r["bf16"]
+    scal = {p: round(r[p]["tok_s"] / one[p]["tok_s"], 3) for p in r}
+    line = {"metric": METRIC, "value": bf["tok_s"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": bf["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e2m1 x e4m3 block-scaled (bf16 profile), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded; BASELINE config 4 distributions)",
+            "config": {"workload": f"cfg4 expert parallel: 8192 tokens per step split over {world} ranks "
+                                   f"({T} each), E=256 experts, {c.n_experts // world} per rank, top-8, Zipf bias; "
+                                   "value: bf16 profile", "tokens_per_step": CFG4_TOKENS,
+                       "global_batch": CFG4_TOKENS,
+                       "parallelism": f"ep{world} (" + ("NVLink peer-memory exchange" if
+                                                        os.environ.get("DSV4_EP_EXCHANGE", "p2p") == "p2p"
+                                                        else "NCCL all-to-all") + ", one CUDA graph per step)",
+                       "l2": "256 MiB flush before every timed step"},
+            "e2e": {"value": bf["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": CFG4_TOKENS * h * 2,
+                    "d2h_bytes_per_step": CFG4_TOKENS * h * 2},
+            "clocks": clocks, "gpu_launches": 9 * a.steps,
+            "detail": {"profiles": r, "same_workload_on_1_gpu": one,
+                       "strong_scaling_vs_1_gpu": scal,
+                       "note": "the N=1 line of bench.py is BASELINE config 1 (decode, T=64); this line's base "
+                               "for scaling is same_workload_on_1_gpu, run by rank 0 in this job"}}
+    print(json.dumps(line), flush=True)
 
 
 def main(argv=None):

@@ -262,6 +262,7 @@ class ExpertBank:
         self._dir = None                # SlotDirectory when the bank offloads with device-side lookups
         self._prefetch_stream = None
         self._prefetch_done = None      # event: the last prefetch enqueued on the side stream
+        self.trace = None               # list: (layer, start, end) timing events of each prefetch
         # DSV4_DEVICE_LRU=0 keeps the host LRU (one synchronisation per layer)
         self.device_lru = os.environ.get("DSV4_DEVICE_LRU", "1") != "0"
 
@@ -450,10 +451,16 @@ class ExpertBank:
         fork.record(cur)
         side.wait_event(fork)
         with torch.cuda.stream(side):
+            t0 = None
+            if self.trace is not None:   # timing events: eager runs only
+                t0 = torch.cuda.Event(enable_timing=True)
+                t0.record(side)
             idx = predict()
             d.acquire(layer, idx, SlotDirectory.PREFETCH, side)
-            done = torch.cuda.Event()
+            done = torch.cuda.Event(enable_timing=t0 is not None)
             done.record(side)
+            if t0 is not None:
+                self.trace.append((int(layer), t0, done))
         self._dir_touched.add(int(layer))
         self._prefetch_done = done
 

@@ -129,7 +129,7 @@ class OffloadDeepseekV4MoE(nn.Module):
         self.experts = _ExpertsFacade(self)
 
     # -- routing ------------------------------------------------------------
-    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None, out=None):
+    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None, out=None, workspace=None):
         """(weights fp32 [T, k], indices int32 [T, k]); deepseek_v4.py:118-148."""
         tid2eid = getattr(self.gate, "tid2eid", None) if self.hash else None
         if self.hash and input_ids is None:
@@ -137,7 +137,7 @@ class OffloadDeepseekV4MoE(nn.Module):
         bias = None if self.hash else getattr(self.gate, "e_score_correction_bias", None)
         return ops.route_topk(hs, self.gate.weight, bias, self.topk, self.scoring_func, self.renormalize,
                               self.routed_scaling_factor, tid2eid=tid2eid,
-                              input_ids=input_ids if self.hash else None, out=out)
+                              input_ids=input_ids if self.hash else None, out=out, workspace=workspace)
 
     # -- routed experts -------------------------------------------------------
     def _slot_table(self, indices: torch.Tensor):
@@ -169,13 +169,15 @@ class OffloadDeepseekV4MoE(nn.Module):
         if nxt is None or bank._dir is None or (nxt.hash and input_ids is None):
             return
         t, k = hs.shape[0], nxt.topk
-        # outputs allocated on this stream (graph-capture safe), used on the side stream
+        # buffers allocated on this stream (graph-capture safe), used on the side stream
         pw = torch.empty((t, k), dtype=torch.float32, device=hs.device)
         pi = torch.empty((t, k), dtype=torch.int32, device=hs.device)
+        ws = torch.empty(max(ops.route_workspace_bytes(t, hs.shape[1], nxt.n_routed_experts), 4),
+                         dtype=torch.uint8, device=hs.device)
         side = bank.prefetch_stream()
-        for x in (hs, pw, pi):
+        for x in (hs, pw, pi, ws):
             x.record_stream(side)
-        bank.prefetch(self.layer_idx + 1, lambda: nxt._route(hs, input_ids, out=(pw, pi))[1])
+        bank.prefetch(self.layer_idx + 1, lambda: nxt._route(hs, input_ids, out=(pw, pi), workspace=ws)[1])
 
     def _routed_experts(self, hs, weights, indices, profile, input_ids=None):
         slot_of, slots = self._slot_table(indices)

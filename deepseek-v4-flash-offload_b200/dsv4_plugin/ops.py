@@ -121,6 +121,13 @@ def route_topk(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor | 
     return wo, io
 
 
+def route_workspace_bytes(n_tokens: int, hidden: int, n_experts: int) -> int:
+    n = lib().dsv4_route_workspace_bytes(n_tokens, hidden, n_experts)
+    if n < 0:
+        check(int(n))
+    return int(n)
+
+
 def moe_align(indices: torch.Tensor, n_experts: int) -> dict:
     """Stable counting sort of the [T,k] expert indices (int32) on the GPU."""
     _need_cuda(indices)

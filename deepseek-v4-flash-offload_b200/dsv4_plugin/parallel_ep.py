@@ -19,9 +19,6 @@ reference has no expert parallelism (``ep_size = 1``, deepseek_v4.py:82).
 
 from __future__ import annotations
 
-import statistics
-import time
-
 import torch
 import torch.distributed as dist
 
@@ -248,7 +245,7 @@ class ExpertParallelMoE:
         self.plan = None
         self._static = {}
         self._p2p = {}
-        self.segment_times = None   # set to {} to time the segments of eager forward_static calls
+        self.segment_times = None   # set to {} to time the segments of eager forward_static / forward_p2p calls
 
     def forward_static(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         """The same layer through ``StaticExchange``: no host synchronisation,
@@ -304,13 +301,32 @@ class ExpertParallelMoE:
             ex = P2PExchange(moe.n_routed_experts, self.ep.rank, self.ep.world, t, moe.topk, hs.shape[1],
                              hs.device, self.ep.group)
             self._p2p[t] = ex
+        marks = [] if self.segment_times is not None else None
+
+        def mark():
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        mark()
         w, idx = moe._route(hs, None)
+        mark()
         x_recv, e_recv, w_recv = ex.dispatch(hs, w, idx)
+        mark()
         plan = moe.engine.plan_for(moe.n_routed_experts, 1, x_recv.shape[0], moe.swiglu_limit or 0.0)
         self.plan = plan
         y_recv = plan.forward(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile)
+        mark()
         back = ex.give_back(y_recv)
-        return ops.combine_ordered(back, ex.ordered)
+        mark()
+        y = ops.combine_ordered(back, ex.ordered)
+        mark()
+        if marks is not None:
+            marks[-1].synchronize()
+            names = ("route", "dispatch", "experts", "return", "combine")
+            self.segment_times = {n: marks[i].elapsed_time(marks[i + 1]) for i, n in enumerate(names)}
+        return y
 
     def close(self):
         """Collective: release the peer-memory exchanges."""
@@ -331,132 +347,3 @@ class ExpertParallelMoE:
         moe.engine.bank.mark_used(None)
         rows, order = self.ep.combine_rows(y_recv, ctx)
         return ops.combine_ordered(rows, order)
-
-
-def run_ep_bench(a, rank, world, device, metric, unit, build_layer, token_batches, Clocks, flush_bytes,
-                 gemm_bytes=None, peaks=None):
-    """Weak-scaling bench: T tokens per rank, E/R experts per rank.  The layer
-    runs through the fixed-capacity exchange and is replayed as one CUDA
-    graph per step (router, NCCL dispatch, experts, NCCL return, combine)."""
-    import os
-
-    if not dist.is_initialized():
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
-    moe, eng = build_layer(device, rank, world)
-    epm = ExpertParallelMoE(moe, rank, world)
-    T = a.tokens
-    host, dev = token_batches(8, T, device, rank)
-    flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device)
-    stream = torch.cuda.current_stream(device)
-    exchange = os.environ.get("DSV4_EP_EXCHANGE", "p2p")
-    fwd = epm.forward_p2p if exchange == "p2p" else epm.forward_static
-    xs = torch.empty_like(dev[0])
-    xs.copy_(dev[0])
-    for _ in range(2):
-        fwd(xs)
-    torch.cuda.synchronize(device)
-    dist.barrier()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        ys = fwd(xs)
-    torch.cuda.synchronize(device)
-
-    def steps(n, src, record=True, e2e=False):
-        ms = []
-        for s in range(n):
-            flush.zero_()
-            dist.barrier()
-            torch.cuda.synchronize(device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            xs.copy_(src[s % len(src)], non_blocking=True)
-            g.replay()
-            if e2e:
-                y_host.copy_(ys, non_blocking=True)
-            e1.record(stream)
-            e1.synchronize()
-            if record:
-                ms.append(e0.elapsed_time(e1))
-        return ms
-
-    y_host = torch.empty((T, moe.gate.weight.shape[1]), dtype=torch.bfloat16).pin_memory()
-    steps(a.warmup, dev, record=False)
-    clk = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
-    dist.barrier()
-    torch.cuda.synchronize(device)
-    clk.start()
-    ms = steps(a.steps, dev)
-    dist.barrier()
-    torch.cuda.synchronize(device)
-    clocks = clk.stop()
-    # per-step max over ranks (device time)
-    t = torch.tensor(ms, dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    tot_ms = float(t.sum().item())
-    value = world * T * a.steps / (tot_ms / 1e3)
-    steps(2, host, record=False, e2e=True)
-    te = torch.tensor(steps(a.steps, host, e2e=True), dtype=torch.float64, device=device)
-    dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.sum().item())
-    # per-rank gate/up GEMM roofline from an eager pass with stage timing
-    plan = epm.plan
-    plan.enable_timing(True)
-    g1 = []
-    for s in range(3):
-        flush.zero_()
-        dist.barrier()
-        fwd(dev[s % len(dev)])
-        torch.cuda.synchronize(device)
-        st = plan.stage_times()
-        g1.append((st["gate_up_gemm"], plan.n_active(), st))
-    plan.enable_timing(False)
-    epm.segment_times = {}
-    for s in range(3):
-        flush.zero_()
-        dist.barrier()
-        epm.forward_static(dev[s % len(dev)])
-    seg = dict(epm.segment_times)
-    epm.segment_times = None
-    for ex in epm._p2p.values():
-        ex.check_status()
-    plan.status()
-    roof = None
-    if gemm_bytes is not None and peaks is not None:
-        hbm, kind = peaks
-        p_rows = int(epm._static[T].recv_meta.shape[0])
-        ach = [gemm_bytes(d, T * moe.topk, "gate_up") / (ms_ / 1e3) / 1e9 for ms_, d, _ in g1]
-        worst = torch.tensor([min(ach)], dtype=torch.float64, device=device)
-        dist.all_reduce(worst, op=dist.ReduceOp.MIN)
-        roof = {"bound": "hbm", "kernel": "moe_gemm_kernel (gate/up) of the slowest rank",
-                "achieved": round(float(worst.item()), 1), "peak": hbm, "peak_kind": f"{kind} HBM copy",
-                "unit": "GB/s", "frac": round(float(worst.item()) / hbm, 4), "traffic": None,
-                "exchange_rows_per_rank": p_rows}
-    del g
-    torch.cuda.synchronize(device)
-    epm.close()
-    del epm
-    dist.barrier()
-    dist.destroy_process_group()
-    if rank != 0:
-        return None
-    h = moe.gate.weight.shape[1]
-    return {"metric": metric, "value": round(value, 1), "unit": unit, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(tot_ms / a.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "e2m1 x e4m3 block-scaled (bf16 profile), fp32 accumulate, bf16 out",
-            "data": "synthetic (seeded; BASELINE config 1 distributions)",
-            "config": {"workload": f"cfg1 decode bf16 profile, expert parallel: T={T} tokens per rank, "
-                                   f"E={moe.n_routed_experts} experts, {moe.n_routed_experts // world} per rank",
-                       "tokens_per_step": T * world, "global_batch": T * world,
-                       "parallelism": (f"ep{world} (" + ("NVLink peer-memory exchange" if exchange == "p2p" else
-                                                         "NCCL all-to-all") +
-                                       f", fixed capacity {T * moe.topk} rows per peer, one CUDA graph per step)"),
-                       "l2": "256 MiB flush before every timed step; 8 rotating token batches per rank"},
-            "roofline": roof,
-            "e2e": {"value": round(world * T * a.steps / (e2e_ms / 1e3), 1), "unit": unit,
-                    "h2d_bytes_per_step": T * h * 2, "d2h_bytes_per_step": T * h * 2},
-            "clocks": clocks, "gpu_launches": 8 * a.steps,
-            "detail": {"step_ms_median": round(statistics.median(t.tolist()), 5),
-                       "rank0_eager_segments_ms": {k: round(v, 5) for k, v in seg.items()},
-                       "rank0_stage_ms": {k: round(v, 5) for k, v in g1[-1][2].items()}}}

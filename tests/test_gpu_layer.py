@@ -7,10 +7,9 @@ against the CPU oracle of the reference's per-expert path.
   GEMM tile and experts with many row chunks at full K.  Every token's
   routing is checked; the outputs of a subset of tokens are checked against
   the oracle (a token's output depends only on its own row and routing), and
-  the a4w4 output is compared with the bf16 profile's by the reference's own
-  acceptance statistic (test_moe_align.py:55-56, 180-191), scaled by the
-  bf16 output's largest magnitude because the synthetic weights are not the
-  checkpoint's;
+  the reference's own a4w4-vs-bf16 statistic (test_moe_align.py:55-56,
+  180-191) of the GPU is held to the oracle's on the same tokens (its
+  thresholds belong to the checkpoint's weights, not the synthetic ones);
 * the offload miss path: fewer HBM slots than experts, several steps issued
   back to back with changing routing, so that slots are evicted and
   refilled while earlier steps' kernels may still run; every step's output
@@ -114,12 +113,19 @@ def test_plugin_forward_cfg2_a4w4_prefill(dev):
     ref16 = O.moe_routed(x[sub], w[sub], idx[sub], experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=deq)
     assert rel_err(y16[sub], ref16) <= TOL
     deq.clear()
-    # the reference's a4w4-vs-bf16 acceptance (max_abs < 0.35, mean < 0.08 on
-    # the checkpoint), relative to the bf16 output's largest magnitude
-    d = np.abs(y4.astype(np.float64) - y16)
-    scale = float(np.abs(y16).max())
-    print(f"a4w4 vs bf16 at T={T}: max_abs/ref_absmax={d.max() / scale:.4f} mean/ref_absmax={d.mean() / scale:.4f}")
-    assert d.max() / scale < 0.35 and d.mean() / scale < 0.08
+    # The reference's a4w4-vs-bf16 statistic (max and mean |a4w4 - bf16|;
+    # thresholds 0.35 / 0.08 on the checkpoint, test_moe_align.py:55-56).
+    # Its size is a property of the weights and activations, so with
+    # synthetic weights it is compared with the same statistic of the oracle
+    # on the same tokens: the kernels must not add quantisation error of
+    # their own.  Both are scaled by the bf16 output's largest magnitude.
+    scale = float(np.abs(ref16).max())
+    d_gpu = np.abs(y4[sub].astype(np.float64) - y16[sub]) / scale
+    d_orc = np.abs(ref4.astype(np.float64) - ref16) / scale
+    print(f"a4w4 vs bf16 at T={T} (scaled): gpu max {d_gpu.max():.4f} mean {d_gpu.mean():.4f}; "
+          f"oracle max {d_orc.max():.4f} mean {d_orc.mean():.4f}")
+    assert d_gpu.max() <= d_orc.max() + 0.02
+    assert d_gpu.mean() <= 1.1 * d_orc.mean() + 1e-3
 
 
 def test_offload_miss_path_matches_oracle_and_lru_model(dev):
