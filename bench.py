@@ -452,6 +452,22 @@ FP8_DENSE_TFLOPS = 4500.0   # nominal dense B200 rate of kind::mxf8f6f4 (the bf1
 FP4_DENSE_TFLOPS = 9000.0   # nominal dense B200 rate of kind::mxf4 (the a4w4 profile's MMA)
 
 
+def mma_peaks(device) -> dict:
+    """Measured dense rate (TFLOP/s) of the two MMA kinds of the grouped GEMM
+    on this GPU (dsv4_mma_peak: one CTA per SM issuing M=128, N=256
+    block-scaled MMAs back to back from shared memory, CUDA events)."""
+    import ctypes as C
+
+    from dsv4_plugin._lib import check, lib
+    out = {}
+    for name, kind in (("mxf4", 0), ("mxf8f6f4", 1)):
+        tf, ms = C.c_double(), C.c_double()
+        check(lib().dsv4_mma_peak(kind, 256, 200000, device.index or 0, C.byref(tf), C.byref(ms)))
+        out[name] = round(tf.value, 1)
+    out["how"] = "dsv4_mma_peak: 148 CTAs x 200000 k-tiles of 128, M=128 N=256, CUDA events"
+    return out
+
+
 def run_prefill(a):
     """T=2048 tokens, a4w4, every expert resident; one
     step = one layer forward (router, align, MXFP4 quant, two GEMMs,
@@ -533,13 +549,15 @@ def run_prefill(a):
     byts = _layer_bytes(d, T) + P * (c.hidden // 2 + c.hidden // 32) + P * (c.inter // 2 + c.inter // 32) \
         + 2 * P * c.hidden * 2
     ms = tot_ms / a.steps
+    peaks = mma_peaks(device)
+    fp4_peak, fp8_peak = peaks["mxf4"], peaks["mxf8f6f4"]
     t_hbm = byts / (hbm * 1e9) * 1e3
-    t_fp8 = flops / (FP8_DENSE_TFLOPS * 1e12) * 1e3
-    t_fp4 = flops / (FP4_DENSE_TFLOPS * 1e12) * 1e3
+    t_fp8 = flops / (fp8_peak * 1e12) * 1e3
+    t_fp4 = flops / (fp4_peak * 1e12) * 1e3
     sm = {k: round(statistics.mean(x[k] for x in st_list), 5) for k in st_list[0]}
     g1_flops, g2_flops = 4.0 * c.hidden * c.inter * P, 2.0 * c.hidden * c.inter * P
     g1_bytes = _gemm_bytes(d, P, "gate_up") - P * (c.hidden + c.hidden // 32) + P * (c.hidden // 2 + c.hidden // 32)
-    g1_bound = max(g1_bytes / (hbm * 1e9), g1_flops / (FP4_DENSE_TFLOPS * 1e12)) * 1e3
+    g1_bound = max(g1_bytes / (hbm * 1e9), g1_flops / (fp4_peak * 1e12)) * 1e3
     line = {"metric": METRIC, "value": round(T * a.steps / (tot_ms / 1e3), 1), "unit": UNIT, "n_gpus": 1,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
@@ -552,7 +570,8 @@ def run_prefill(a):
                          "layer_bound_ms": round(max(t_hbm, t_fp4), 5), "frac": round(max(t_hbm, t_fp4) / ms, 4),
                          "hbm_ms": round(t_hbm, 5), "fp8_rate_ms": round(t_fp8, 5), "fp4_rate_ms": round(t_fp4, 5),
                          "bytes": round(byts), "flops": flops, "peak_hbm_gbs": hbm, "peak_kind": peak_kind,
-                         "tensor_peak": f"{FP4_DENSE_TFLOPS:.0f} TFLOP/s nominal dense (kind::mxf4, the a4w4 MMA)",
+                         "tensor_peak": f"{fp4_peak:.0f} TFLOP/s measured (kind::mxf4, the a4w4 MMA; "
+                                        f"nominal {FP4_DENSE_TFLOPS:.0f})", "mma_peaks_tflops": peaks,
                          "gate_up_frac": round(g1_bound / sm["gate_up_gemm"], 4)},
             "e2e": {"value": round(T * a.steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
@@ -829,45 +848,121 @@ def run_offload(a):
     print(json.dumps(line), flush=True)
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _reference_moe(cfg, layer: int = 3):
+    """The reference's own per-expert MoE (model_npu.MoE over an
+    offload.ExpertBank on device "cpu"), imported from the unmodified
+    install in baseline/_ref.  Two shims, as the golden-fixture generator
+    uses: the privateuse1 backend is named "npu" (model_npu builds
+    torch.device("npu:0") at import) and model_npu.DEVICE is set to the CPU.
+    The shared expert is replaced by zero: the path under test is the routed
+    experts (this build's layer does not run the shared expert either)."""
+    import torch
+    from torch import nn
+
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        torch.utils.rename_privateuse1_backend("npu")
+    except RuntimeError:
+        pass   # already renamed in this process
+    os.environ["DSV4_PIN_HOST"] = "0"
+    import model_npu as MN
+    import offload as OFF
+    MN.DEVICE = torch.device("cpu")
+    args = MN.ModelArgs(dim=cfg.hidden, moe_inter_dim=cfg.inter, n_routed_experts=cfg.n_experts,
+                        n_activated_experts=cfg.topk, score_func=cfg.score_func, route_scale=cfg.route_scale,
+                        swiglu_limit=cfg.swiglu_limit, n_hash_layers=0)
+    bank = OFF.ExpertBank(capacity=cfg.n_experts, device="cpu", pin=False)
+    moe = MN.MoE(layer, args, bank=bank)
+
+    class _Zero(nn.Module):
+        def forward(self, x):
+            return torch.zeros((), dtype=x.dtype)
+
+    moe.shared_experts = _Zero()
+    return moe, bank
+
+
 def run_reference(a):
+    """The reference arm: the reference's own CPU per-expert path
+    (model_npu.MoE.forward with ExpertBank(device="cpu"), every used expert
+    resident dequantised after the warm-up: its hot state) on the host
+    cores, for the ours arm's workload: config 1 (T=64) at N=1; at N>1 a
+    bounded sample (512 of the 8192 tokens per step) of config 4.  When
+    baseline/_ref is absent the numpy restatement in oracle/ runs instead
+    (kind "port")."""
     rank, world, _ = _dist()
     if rank != 0:
         return
     import numpy as np
+    import torch
 
     from dsv4_plugin import synthetic as S
-    from oracle import moe_oracle as O
     cfg = _cfg()
-    T = a.tokens
-    gw, bias = S.make_gate(cfg, 0, 3)
-    x = S.make_tokens(cfg, 7, T, step=0)
-    w, idx = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
-    need = sorted(set(idx.reshape(-1).tolist()))
-    experts = {e: S.make_expert(cfg, 0, e, 3) for e in need}
-    cache = {e: O.expert_weights_f32(experts[e]) for e in need}
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    if world > 1:
+        T = 512
+        x = S.make_tokens(cfg, 77, CFG4_TOKENS, step=0)[:T]
+        workload = (f"cfg4 expert parallel on {world} ranks (8192 tokens per step, E=256, top-8); reference arm: "
+                    f"{T} of the step's tokens per timed step on the host cores")
+        gw, bias = S.make_gate(cfg, 0, 3)
+    else:
+        T = a.tokens
+        x = S.make_tokens(cfg, 7, T, step=0)
+        workload = f"cfg1 decode bf16 profile: T={T} tokens, H=4096, I=2048, E=256, top-8, all experts resident"
+        gw, bias = S.make_gate(cfg, 0, 3)
+    kind = "reference" if os.path.isfile(os.path.join(REF_DIR, "model_npu.py")) else "port"
+    if kind == "reference":
+        torch.set_num_threads(cores)
+        moe, bank = _reference_moe(cfg)
+        moe.gate.weight.data.copy_(torch.from_numpy(gw))
+        moe.gate.bias.data.copy_(torch.from_numpy(bias))
+        xt = torch.from_numpy(S.to_bf16_bits(x).astype(np.int16)).view(torch.bfloat16)
+        ids = torch.zeros(T, dtype=torch.int64)
+        with torch.no_grad():
+            _, idx = moe.gate(xt, ids)
+        need = sorted(set(idx.reshape(-1).tolist()))
+        for e in need:
+            ex = S.make_expert(cfg, 0, e, 3)
+            bank.register(3, e, *[torch.from_numpy(ex[k]) for k in ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
 
-    def step():
-        ww, ii = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
-        O.moe_routed(x, ww, ii, experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=cache)
+        def step():
+            with torch.no_grad():
+                moe(xt, ids)
+        sample = (f"model_npu.MoE.forward (router + per-expert bf16 loop, baseline/_ref), T={T}, {len(need)} experts "
+                  f"resident dequantised, torch {torch.get_num_threads()} threads")
+        n_threads = torch.get_num_threads()
+    else:
+        from oracle import moe_oracle as O
+        w, idx = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+        need = sorted(set(idx.reshape(-1).tolist()))
+        experts = {e: S.make_expert(cfg, 0, e, 3) for e in need}
+        cache = {e: O.expert_weights_f32(experts[e]) for e in need}
 
-    for _ in range(a.warmup):
+        def step():
+            ww, ii = O.route(x, gw, bias, cfg.topk, cfg.score_func, cfg.renormalize)
+            O.moe_routed(x, ww, ii, experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=cache)
+        sample = f"numpy restatement (oracle/), T={T}, {len(need)} experts resident dequantised"
+        n_threads = cores
+
+    for _ in range(max(1, a.warmup)):
         step()
     t0 = time.perf_counter()
     for _ in range(a.steps):
         step()
     dt = time.perf_counter() - t0
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     value = T * a.steps / dt
     line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16-rounded like the reference)",
-            "data": "synthetic (seeded; BASELINE config 1 distributions)", "impl": "reference",
-            "config": {"workload": f"cfg1 decode bf16 profile: T={T} tokens, H=4096, I=2048, E=256, top-8, "
-                                   "all experts resident", "tokens_per_step": T, "global_batch": T,
-                       "parallelism": "host cores"},
-            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{a.steps} layer forwards (router + per-expert loop) of cfg1 T={T}; "
-                                       f"{len(need)} experts resident dequantised"},
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16 (the reference's CPU path)" if kind == "reference" else "fp32 (bf16-rounded like the reference)",
+            "data": "synthetic (seeded; BASELINE config distributions)", "impl": "reference",
+            "config": {"workload": workload, "tokens_per_step": T, "global_batch": T, "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": n_threads, "kind": kind,
+                             "sample": f"{a.steps} timed layer forwards: {sample}"},
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

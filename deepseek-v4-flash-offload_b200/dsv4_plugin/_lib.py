@@ -43,6 +43,7 @@ SIGNATURES = {
                                   _i64, _p]),
     "dsv4_route_topk_noalloc": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _p,
                                           _p, _p]),
+    "dsv4_mma_peak": (C.c_int, [_i32, _i32, _i64, _i32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "dsv4_moe_align": (C.c_int, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32, _i64]),
     "dsv4_moe_plan_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i32, _i64, _f32, _p, _i64, _p, _i64]),

@@ -392,11 +392,6 @@ class ExpertBank:
                 if key[0] in self._dir_touched:   # an older copy of the expert may be resident
                     self.invalidate()
 
-    def offloading(self) -> bool:
-        """True when the registered experts do not all fit the HBM budget,
-        so slots get evicted and refilled during forwards."""
-        return len(self._host) > self.packed_capacity
-
     def device_directory(self, n_experts: int):
         """The device-side LRU (created on first use), or None when the pool
         is not page-locked (the GPU can only read pinned host memory) or

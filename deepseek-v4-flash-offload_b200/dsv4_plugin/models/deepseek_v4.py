@@ -143,16 +143,18 @@ class OffloadDeepseekV4MoE(nn.Module):
     def _slot_table(self, indices: torch.Tensor):
         """(device expert -> slot table, slots to mark as read or None).
 
-        Every expert resident: the bank's static table.  Offloading with a
-        page-locked pool: the device-side LRU (``ExpertBank.acquire``), no
-        host synchronisation.  Otherwise the host LRU, which needs the active
+        Every expert of the layer resident (``preload_all``): the bank's static
+        table.  Otherwise, with a page-locked pool: the device-side LRU
+        (``ExpertBank.acquire``), no host synchronisation; once created it
+        owns the arena.  Otherwise the host LRU, which needs the active
         experts on the host (one synchronisation per layer)."""
         bank = self.engine.bank
-        if bank.offloading() and bank.device_directory(self.n_routed_experts) is not None:
+        if bank._dir is None:
+            table = bank.resident_table(self.layer_idx, self.n_routed_experts)
+            if table is not None:
+                return table, None
+        if bank.device_directory(self.n_routed_experts) is not None:
             return bank.acquire(self.layer_idx, indices), None
-        table = bank.resident_table(self.layer_idx, self.n_routed_experts)
-        if table is not None:
-            return table, None
         active = torch.unique(indices).tolist()            # one host sync per layer
         slots = bank.ensure_resident(self.layer_idx, active)
         host = torch.full((self.n_routed_experts,), -1, dtype=torch.int32)

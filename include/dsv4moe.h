@@ -130,6 +130,14 @@ int dsv4_route_topk_noalloc(const void* x_bf16, const float* gate_w, const float
                             int32_t n_experts, int32_t topk, int32_t score_func, int32_t renormalize,
                             float route_scale, float* weights_out, int32_t* indices_out, void* stream);
 
+/* Tensor-core rate of the grouped GEMM's MMA kinds on `device` (no
+ * counterpart in the reference, which quotes no tensor peak): kind 0 =
+ * tcgen05 kind::mxf4 block-scaled (the a4w4 profile), 1 = kind::mxf8f6f4
+ * with E2M1 x E4M3 (the bf16 profile); M = 128, N = n, `iters` k-tiles of 128
+ * per SM, back to back from shared memory.  Synchronous; writes dense TFLOP/s
+ * and the timed milliseconds. */
+int dsv4_mma_peak(int32_t kind, int32_t n, int64_t iters, int32_t device, double* tflops_out, double* ms_out);
+
 /* ------------------------------------------------------------------------ *
  * moe_align (deepseek_v4.py:154-164): stable counting sort of the T*k
  * (token, slot) assignments by expert id.  sorted_flat[pos] = t*k + j,

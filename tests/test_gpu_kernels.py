@@ -212,3 +212,16 @@ def test_align_rejects_out_of_range_expert(ops):
     idx = torch.tensor([[0, 1], [2, 99]], dtype=torch.int32).cuda()
     res = ops.moe_align(idx, 16)
     assert int(res["status"].item()) == -1
+
+
+def test_mma_peak_probe_reports_a_plausible_rate(ops):
+    """The tensor-core rate probe behind the prefill roofline: positive, and
+    below twice the nominal dense rate of each kind (9 PF/s mxf4, 4.5 PF/s
+    mxf8f6f4) -- far above it would mean the MMAs did not run."""
+    import ctypes as C
+
+    from dsv4_plugin._lib import check, lib
+    for kind, nominal in ((0, 9000.0), (1, 4500.0)):
+        tf, ms = C.c_double(), C.c_double()
+        check(lib().dsv4_mma_peak(kind, 256, 20000, 0, C.byref(tf), C.byref(ms)))
+        assert 0.05 * nominal < tf.value < 2.0 * nominal, (kind, tf.value)
