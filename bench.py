@@ -128,9 +128,10 @@ def _cfg():
     return S.CFG1
 
 
-def build_layer(device, rank: int, world: int, seed: int = 0, layer_idx: int = 3):
+def build_layer(device, rank: int, world: int, seed: int = 0, layer_idx: int = 3, owner=None):
     """Engine + OffloadDeepseekV4MoE for one synthetic layer; the experts
-    owned by this rank (all of them at world=1) are resident."""
+    owned by this rank (owner[e] == rank; default contiguous, all of them at
+    world=1) are registered."""
     import types
 
     import torch
@@ -140,11 +141,13 @@ def build_layer(device, rank: int, world: int, seed: int = 0, layer_idx: int = 3
     from dsv4_plugin.models import deepseek_v4 as DV4
 
     cfg = _cfg()
-    e_loc = cfg.n_experts // world
-    lo = rank * e_loc
+    if owner is None:
+        owner = [e // (cfg.n_experts // world) for e in range(cfg.n_experts)]
+    mine = [e for e in range(cfg.n_experts) if owner[e] == rank]
+    e_loc = len(mine)
     eng = ENG.ExpertOffloadEngine(slot_capacity=e_loc, device=device, packed_capacity=e_loc)
     eng.bank.pin = True
-    for e in range(lo, lo + e_loc):
+    for e in mine:
         ex = S.make_expert(cfg, seed, e, layer_idx)
         eng.bank.register(layer_idx, e, *[torch.from_numpy(ex[k]) for k in
                                           ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
@@ -990,6 +993,26 @@ def _cfg4_batches(device, rank: int, world: int, n: int = 2):
     return host, dev
 
 
+def _calibrated_placement(device, world: int):
+    """Load-balanced expert placement from a calibration batch (a separate
+    seeded 8192-token batch, not one of the timed ones): its per-expert row
+    counts from the router, then ``parallel_ep.balanced_placement``.  Every
+    rank computes the same placement (same inputs, deterministic kernels)."""
+    import torch
+
+    from dsv4_plugin import ops
+    from dsv4_plugin import synthetic as S
+    from dsv4_plugin.parallel_ep import balanced_placement
+    c = _cfg()
+    gw, bias = S.make_gate(c, 0, 3)
+    x = S.make_tokens(c, 91, CFG4_TOKENS, step=0)
+    xt = torch.from_numpy(S.to_bf16_bits(x).astype("int16")).view(torch.bfloat16).to(device)
+    _, idx = ops.route_topk(xt, torch.from_numpy(gw).to(device), torch.from_numpy(bias).to(device), c.topk,
+                            c.score_func, c.renormalize, c.route_scale)
+    counts = torch.bincount(idx.reshape(-1).to(torch.int64), minlength=c.n_experts).cpu().tolist()
+    return balanced_placement(counts, world)
+
+
 def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), steps=None, warmup=None):
     """BASELINE config 4: E=256 experts sharded e // (E/N) over N ranks, a
     fixed step of 8192 tokens split evenly (T/N per rank), Zipf-skewed
@@ -1006,7 +1029,10 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
     from dsv4_plugin.models import deepseek_v4 as DV4
     steps = steps or a.steps
     warmup = warmup or a.warmup
-    moe, eng = build_layer(device, rank, world)
+    owner = None
+    if world > 1 and os.environ.get("DSV4_EP_PLACEMENT", "balanced") == "balanced":
+        owner = _calibrated_placement(device, world)
+    moe, eng = build_layer(device, rank, world, owner=owner)
     host, dev = _cfg4_batches(device, rank, world)
     T = CFG4_TOKENS // world
     stream = torch.cuda.current_stream(device)
@@ -1015,7 +1041,7 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
     epm = None
     if world > 1:
         from dsv4_plugin.parallel_ep import ExpertParallelMoE
-        epm = ExpertParallelMoE(moe, rank, world)
+        epm = ExpertParallelMoE(moe, rank, world, owner=owner)
 
     def fwd(x, profile):
         if epm is None:
@@ -1088,7 +1114,7 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
         plan = epm.plan if epm is not None else eng.plan_for(_cfg().n_experts, _cfg().topk, T, _cfg().swiglu_limit)
         load = [float(plan.n_active())]
         if epm is not None:
-            load.append(float(int((epm._p2p[T].recv_meta[:, 0] >= 0).sum().item())) if exchange == "p2p" else 0.0)
+            load.append(float(int(epm._p2p[T].n_recv.item())) if exchange == "p2p" else 0.0)
         loads = [load]
         if world > 1:
             buf = torch.tensor(load, dtype=torch.float64, device=device)
@@ -1152,9 +1178,11 @@ def run_ep(a, rank, world, device):
                                    f"({T} each), E=256 experts, {c.n_experts // world} per rank, top-8, Zipf bias; "
                                    "value: bf16 profile", "tokens_per_step": CFG4_TOKENS,
                        "global_batch": CFG4_TOKENS,
-                       "parallelism": f"ep{world} (" + ("NVLink peer-memory exchange" if
+                       "parallelism": f"ep{world} (" + ("NVLink peer-memory exchange, exact counts" if
                                                         os.environ.get("DSV4_EP_EXCHANGE", "p2p") == "p2p"
-                                                        else "NCCL all-to-all") + ", one CUDA graph per step)",
+                                                        else "NCCL all-to-all") +
+                                           ", " + os.environ.get("DSV4_EP_PLACEMENT", "balanced") +
+                                           " expert placement, one CUDA graph per step)",
                        "l2": "256 MiB flush before every timed step"},
             "e2e": {"value": bf["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": CFG4_TOKENS * h * 2,
                     "d2h_bytes_per_step": CFG4_TOKENS * h * 2},

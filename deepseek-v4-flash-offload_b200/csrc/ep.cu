@@ -1,7 +1,8 @@
 // Expert parallelism: packing of the fixed-capacity dispatch (no counterpart
 // in the reference, whose expert-parallel size is 1, deepseek_v4.py:82).
 //
-// Expert e lives on rank e / e_loc.  Every rank sends `cap` rows to every
+// Expert e lives on rank owner[e] (a placement map; without one, e / e_loc).
+// Every rank sends `cap` rows to every
 // peer (cap = T*k, the worst case), so the exchange has a shape known in
 // advance and the layer can be captured in a CUDA graph.  For assignment
 // a = t*k + j with destination d, its slot in the send buffer is
@@ -31,8 +32,9 @@ constexpr int EP_MAX_WORLD = 64;
 // plus the count of earlier rounds.
 __global__ void __launch_bounds__(EP_THREADS, 1)
     ep_pack_index_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int64_t P, int topk,
-                         int e_loc, int world, int64_t cap, int32_t* __restrict__ pos, int32_t* __restrict__ meta,
-                         int32_t* __restrict__ ordered, int* __restrict__ status) {
+                         int E, int e_loc, const int32_t* __restrict__ owner, int world, int64_t cap,
+                         int32_t* __restrict__ pos, int32_t* __restrict__ meta, int32_t* __restrict__ ordered,
+                         int* __restrict__ status) {
   __shared__ int wc[32][EP_MAX_WORLD];
   __shared__ int base[EP_MAX_WORLD];
   __shared__ int round_tot[EP_MAX_WORLD];
@@ -47,11 +49,15 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
     int e = -1, d = -1;
     if (a < P) {
       e = idx[a];
-      if (e < 0 || e >= e_loc * world) {
-        set_status(status, DSV4_EINVAL);
+      if (e < 0 || e >= E) {
+        if (e != -1) set_status(status, DSV4_EINVAL);
         e = -1;
       } else {
-        d = e / e_loc;
+        d = owner ? owner[e] : e / e_loc;
+        if (d < 0 || d >= world) {
+          set_status(status, DSV4_EINVAL);
+          e = d = -1;
+        }
       }
     }
     const unsigned same = __match_any_sync(0xffffffffu, d);
@@ -132,15 +138,16 @@ using namespace dsv4;
 
 extern "C" int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weights, const int32_t* route_indices,
                                      int64_t n_tokens, int32_t topk, int32_t hidden, int32_t n_experts,
-                                     int32_t world, void* send_x_bf16, int32_t* send_meta, int32_t* slot_of_assignment,
-                                     int32_t* ordered_slots, int* status, void* stream) {
+                                     int32_t world, const int32_t* expert_owner, void* send_x_bf16,
+                                     int32_t* send_meta, int32_t* slot_of_assignment, int32_t* ordered_slots,
+                                     int* status, void* stream) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && send_x_bf16 && send_meta && slot_of_assignment &&
                      ordered_slots && status,
                  "null pointer");
   DSV4_CHECK_ARG(n_tokens >= 0 && topk > 0 && topk <= 16, "topk must be in [1, 16]");
-  DSV4_CHECK_ARG(world > 0 && world <= EP_MAX_WORLD && n_experts > 0 && n_experts % world == 0,
-                 "world must be in [1, 64] and divide n_experts");
+  DSV4_CHECK_ARG(world > 0 && world <= EP_MAX_WORLD && n_experts > 0 && (expert_owner || n_experts % world == 0),
+                 "world must be in [1, 64] and divide n_experts (or pass expert_owner)");
   DSV4_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "hidden must be a positive multiple of 8");
   DSV4_CHECK_ARG(n_tokens * topk < (1LL << 31) / world, "too many assignments");
   DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)send_x_bf16 % 16) == 0, "rows must be 16-byte aligned");
@@ -151,8 +158,8 @@ extern "C" int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weig
   const int64_t P = n_tokens * topk;
   const int64_t cap = P;
   DSV4_CUDA_CHECK(launch_k(ep_pack_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, route_weights,
-                           P, (int)topk, (int)(n_experts / world), (int)world, cap, slot_of_assignment, send_meta,
-                           ordered_slots, status));
+                           P, (int)topk, (int)n_experts, (int)(n_experts / world), expert_owner, (int)world, cap,
+                           slot_of_assignment, send_meta, ordered_slots, status));
   const int64_t blocks = std::min<int64_t>((P * 32 + 255) / 256, 148 * 8);
   DSV4_CUDA_CHECK(launch_k(ep_pack_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
                            (const uint16_t*)x_bf16, (const int32_t*)slot_of_assignment, P, (int)topk, (int)hidden,
@@ -164,34 +171,51 @@ extern "C" int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weig
 namespace dsv4 {
 
 // ---------------------------------------------------------------------------
-// Exchange over NVLink peer memory (CUDA IPC).  Each rank owns one device
-// block: recv_x [world*cap, H] bf16 and recv_meta [world*cap] (expert,
-// weight) that the peers write their dispatched rows into (source s fills
-// rows s*cap..), back [world*cap, H] bf16 that the peers write the expert
-// outputs of this rank's assignments into (owner d fills rows d*cap..),
-// and flags.  Only real rows cross NVLink; padding is marked in the
-// metadata.  Every step increments a device epoch; a rank publishes
-// "dispatch done" / "return done" by storing the epoch into its slot of each
-// peer's flags (release, system scope) after its rows are fenced, and a
-// receiver waits (acquire, bounded) until every source's flag has reached
-// the epoch.  A peer writes into this rank's receive buffers for step e+1
-// only after it received this rank's step-e return, which this rank sends
-// after consuming step e, so one buffer set suffices.
+// Exchange over NVLink peer memory (CUDA IPC), with exact per-peer counts.
+// Each rank owns one device block that its peers write into:
+//   recv_x [world*cap, H] bf16, recv_e [world*cap] int32, recv_w [world*cap]
+//     fp32, recv_src [world*cap] int2 (source rank, source slot): the rows
+//     dispatched to this rank, COMPACT: source s fills rows
+//     off[s] .. off[s] + n[s->me), off[s] = sum over s' < s of n[s'->me];
+//   back [world*cap, H] bf16: expert outputs of this rank's assignments,
+//     owner d fills rows d*cap + r (r = rank of the assignment among this
+//     rank's assignments to d);
+//   cnt [world][world] int32: row s = the per-destination counts of source s;
+//   flags [3][world]: per source, the epoch of its published counts, rows
+//     and returned rows; ctrl: epoch, arrival counters, rows received.
+// A step: (1) one CTA ranks the assignments per destination (stable), writes
+// its count row into every peer's cnt and publishes; (2) a wait for every
+// source's counts; (3) the rows, straight into the owners' blocks at their
+// compact offsets, then "rows published"; (4) a wait for every source's rows,
+// which also sums the received count (the layer's device-side token count);
+// after the layer (5) each received row goes back to its source's `back`,
+// read from the layer's sorted output rows through inv, and (6) a wait.
+// Publishing is a system-scope release of the epoch after the writes are
+// fenced; waiting is an acquire, bounded (DSV4_ETIMEOUT in *status).  A peer
+// writes into this rank's block for step e+1 only after it received this
+// rank's step-e return, which this rank sends after consuming step e, so one
+// buffer set suffices.  After a timeout the step's data are undefined and a
+// late peer may still write: the handle must be destroyed and recreated.
 // ---------------------------------------------------------------------------
 struct EpBlock {
-  int64_t off_back, off_meta, off_flags, off_ctrl, bytes;
+  int64_t off_back, off_e, off_w, off_src, off_cnt, off_flags, off_ctrl, bytes;
 };
 static EpBlock ep_block(int world, int64_t cap, int hidden) {
   auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
   EpBlock b;
   const int64_t rows = (int64_t)world * cap;
   b.off_back = al(rows * hidden * 2);
-  b.off_meta = b.off_back + al(rows * hidden * 2);
-  b.off_flags = b.off_meta + al(rows * 8);
-  b.off_ctrl = b.off_flags + al(2 * (int64_t)world * 4);
+  b.off_e = b.off_back + al(rows * hidden * 2);
+  b.off_w = b.off_e + al(rows * 4);
+  b.off_src = b.off_w + al(rows * 4);
+  b.off_cnt = b.off_src + al(rows * 8);
+  b.off_flags = b.off_cnt + al((int64_t)world * world * 4);
+  b.off_ctrl = b.off_flags + al(3 * (int64_t)world * 4);
   b.bytes = b.off_ctrl + 256;
   return b;
 }
+// ctrl words
+constexpr int EPC_EPOCH = 0, EPC_ROWS = 1, EPC_BACK = 2, EPC_NRECV = 3;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -202,34 +226,42 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// One CTA: epoch += 1, slots of the assignments (as ep_pack_index_kernel),
-// metadata straight into the owners' recv_meta (padding included), the
-// combine order, and a system fence.
+__device__ __forceinline__ int ep_dest(int e, int e_loc, const int32_t* __restrict__ owner) {
+  return owner ? owner[e] : e / e_loc;
+}
+
+// One CTA: epoch += 1, each assignment's destination slot d*cap + r (stable
+// rank among this rank's assignments to d), the combine order, then this
+// rank's count row into every peer's cnt, fenced and published.
 __global__ void __launch_bounds__(EP_THREADS, 1)
-    ep_p2p_index_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int64_t P, int topk,
-                        int e_loc, int world, int my_rank, int64_t cap, uint8_t* const* __restrict__ peers,
-                        int64_t off_meta, uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos,
-                        int32_t* __restrict__ ordered, int* __restrict__ status) {
+    ep_p2p_index_kernel(const int32_t* __restrict__ idx, int64_t P, int topk, int E, int e_loc,
+                        const int32_t* __restrict__ owner, int world, int my_rank, int64_t cap,
+                        uint8_t* const* __restrict__ peers, int64_t off_cnt, int64_t off_flags,
+                        uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos, int32_t* __restrict__ ordered,
+                        int* __restrict__ status) {
   __shared__ int wc[32][EP_MAX_WORLD];
   __shared__ int base[EP_MAX_WORLD];
   __shared__ int round_tot[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) ctrl[0] = ctrl[0] + 1u;   // this step's epoch
+  if (tid == 0) ctrl[EPC_EPOCH] = ctrl[EPC_EPOCH] + 1u;   // this step's epoch
   if (tid < world) base[tid] = 0;
   for (int64_t r0 = 0; r0 < P; r0 += EP_THREADS) {
     for (int i = tid; i < 32 * EP_MAX_WORLD; i += EP_THREADS) (&wc[0][0])[i] = 0;
     __syncthreads();
     const int64_t a = r0 + tid;
-    int e = -1, d = -1;
+    int d = -1;
     if (a < P) {
-      e = idx[a];
-      if (e < 0 || e >= e_loc * world) {
+      const int e = idx[a];
+      if (e >= 0 && e < E) {
+        d = ep_dest(e, e_loc, owner);
+        if (d < 0 || d >= world) {
+          set_status(status, DSV4_EINVAL);
+          d = -1;
+        }
+      } else if (e != -1) {
         set_status(status, DSV4_EINVAL);
-        e = -1;
-      } else {
-        d = e / e_loc;
       }
     }
     const unsigned same = __match_any_sync(0xffffffffu, d);
@@ -246,22 +278,13 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
       round_tot[tid] = s;
     }
     __syncthreads();
-    if (d >= 0) {
-      const int64_t r = base[d] + wc[warp][d] + rank;
-      pos[a] = (int32_t)((int64_t)d * cap + r);
-      int2* m = reinterpret_cast<int2*>(peers[d] + off_meta) + (int64_t)my_rank * cap + r;
-      *m = make_int2(e, __float_as_int(w[a]));
-    } else if (a < P) {
+    if (d >= 0)
+      pos[a] = (int32_t)((int64_t)d * cap + base[d] + wc[warp][d] + rank);
+    else if (a < P)
       pos[a] = -1;
-    }
     __syncthreads();
     if (tid < world) base[tid] += round_tot[tid];
     __syncthreads();
-  }
-  for (int64_t s = tid; s < (int64_t)world * cap; s += EP_THREADS) {
-    const int d = (int)(s / cap);
-    const int64_t r = s - (int64_t)d * cap;
-    if (r >= base[d]) *(reinterpret_cast<int2*>(peers[d] + off_meta) + (int64_t)my_rank * cap + r) = make_int2(-1, 0);
   }
   for (int64_t t = tid; t < P / topk; t += EP_THREADS) {
     int ke[16], kp[16];
@@ -281,7 +304,18 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
     }
     for (int j = 0; j < topk; ++j) ordered[t * topk + j] = j < n ? kp[j] : -1;
   }
+  // this rank's counts into row my_rank of every peer's count matrix
+  for (int i = tid; i < world * world; i += EP_THREADS) {
+    const int d = i / world, c = i - d * world;
+    reinterpret_cast<int32_t*>(peers[d] + off_cnt)[my_rank * world + c] = base[c];
+  }
   __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t epoch = ctrl[EPC_EPOCH];
+    for (int d = 0; d < world; ++d)
+      st_release_sys(reinterpret_cast<uint32_t*>(peers[d] + off_flags) + 0 * world + my_rank, epoch);
+  }
 }
 
 // After every CTA fenced its peer writes, the last CTA to finish publishes
@@ -295,20 +329,30 @@ __device__ __forceinline__ void ep_publish(uint32_t* __restrict__ ctrl, int coun
     if (prev == gridDim.x - 1) {
       ctrl[counter] = 0u;
       __threadfence_system();
-      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctrl[0]);
+      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctrl[EPC_EPOCH]);
       for (int d = 0; d < world; ++d)
         st_release_sys(reinterpret_cast<uint32_t*>(peers[d] + off_flags) + flag_slot, epoch);
     }
   }
 }
 
-// One warp per assignment: the token's row straight into the owner's recv_x.
-__global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ pos, int64_t P,
-                                   int topk, int H, int world, int my_rank, int64_t cap,
-                                   uint8_t* const* __restrict__ peers, int64_t off_flags,
-                                   uint32_t* __restrict__ ctrl) {
+// One warp per assignment: the token's row, expert, weight and return slot
+// into the owner's block at the compact row off[my_rank -> d] + r.  The
+// offsets come from this rank's copy of the count matrix (every source wrote
+// its row before the wait that precedes this kernel).
+__global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
+                                   const float* __restrict__ w, const int32_t* __restrict__ pos, int64_t P, int topk,
+                                   int H, int world, int my_rank, int64_t cap, uint8_t* const* __restrict__ peers,
+                                   EpBlock blk, const int32_t* __restrict__ cnt, uint32_t* __restrict__ ctrl) {
+  __shared__ int64_t off[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
+  if (threadIdx.x < world) {
+    int64_t o = 0;
+    for (int s = 0; s < my_rank; ++s) o += cnt[s * world + threadIdx.x];
+    off[threadIdx.x] = o;
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -317,50 +361,67 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
     if (p < 0) continue;
     const int d = (int)(p / cap);
     const int64_t r = p - (int64_t)d * cap;
+    const int64_t row = off[d] + r;
     const uint4* src = reinterpret_cast<const uint4*>(x + (a / topk) * H);
-    uint4* dst = reinterpret_cast<uint4*>(peers[d]) + ((int64_t)my_rank * cap + r) * (H / 8);
+    uint4* dst = reinterpret_cast<uint4*>(peers[d]) + row * (H / 8);
     for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    if (lane == 0) {
+      reinterpret_cast<int32_t*>(peers[d] + blk.off_e)[row] = idx[a];
+      reinterpret_cast<float*>(peers[d] + blk.off_w)[row] = w[a];
+      reinterpret_cast<int2*>(peers[d] + blk.off_src)[row] = make_int2(my_rank, (int)r);
+    }
   }
-  ep_publish(ctrl, 1, peers, world, off_flags, my_rank);
+  ep_publish(ctrl, EPC_ROWS, peers, world, blk.off_flags, 1 * world + my_rank);
 }
 
-// One warp per received slot: the expert output row back into the source's
-// `back` (rows my_rank*cap.. of the source).
-__global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y_recv, const int2* __restrict__ meta, int world,
+// One warp per received row j < n_recv: its expert output (row inv[j] of the
+// layer's sorted output, or row j of y when inv is null) back into the
+// source's `back` at my_rank*cap + r.
+__global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ inv,
+                                     const int2* __restrict__ src_of, const uint32_t* __restrict__ n_recv, int world,
                                      int my_rank, int64_t cap, int H, uint8_t* const* __restrict__ peers,
                                      int64_t off_back, int64_t off_flags, uint32_t* __restrict__ ctrl) {
   griddep_wait();
   griddep_launch();
   const int lane = threadIdx.x & 31;
+  const int64_t n = (int64_t)*reinterpret_cast<const volatile uint32_t*>(n_recv);
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t s = warp0; s < (int64_t)world * cap; s += nwarps) {
-    if (meta[s].x < 0) continue;
-    const int src = (int)(s / cap);
-    const int64_t j = s - (int64_t)src * cap;
-    const uint4* from = reinterpret_cast<const uint4*>(y_recv + s * H);
-    uint4* dst = reinterpret_cast<uint4*>(peers[src] + off_back) + ((int64_t)my_rank * cap + j) * (H / 8);
+  for (int64_t j = warp0; j < n; j += nwarps) {
+    const int2 sr = src_of[j];
+    if (sr.x < 0 || sr.x >= world || sr.y < 0 || sr.y >= cap) continue;   // not written this step (after a timeout)
+    const int64_t from_row = inv ? (int64_t)inv[j] : j;
+    const uint4* from = reinterpret_cast<const uint4*>(y + from_row * H);
+    uint4* dst = reinterpret_cast<uint4*>(peers[sr.x] + off_back) + ((int64_t)my_rank * cap + sr.y) * (H / 8);
     for (int c = lane; c < H / 8; c += 32) dst[c] = from[c];
   }
-  ep_publish(ctrl, 2, peers, world, off_flags, world + my_rank);
+  ep_publish(ctrl, EPC_BACK, peers, world, off_flags, 2 * world + my_rank);
 }
 
 // One thread: wait (bounded) until every source has published this step's
-// epoch in flags[first .. first+world).
+// epoch in flags[first .. first+world).  With `cnt`, also writes the number
+// of rows this rank receives (column my_rank of the count matrix) to *n_recv.
 __global__ void ep_p2p_wait_kernel(const uint32_t* __restrict__ flags, const uint32_t* __restrict__ ctrl, int world,
-                                   int* __restrict__ status) {
+                                   int* __restrict__ status, const int32_t* __restrict__ cnt, int my_rank,
+                                   uint32_t* __restrict__ n_recv) {
   griddep_wait();
   griddep_launch();
   if (threadIdx.x != 0) return;
-  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(&ctrl[0]);
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(&ctrl[EPC_EPOCH]);
   const uint64_t t0 = globaltimer_ns();
   for (int s = 0; s < world; ++s) {
     while ((int32_t)(ld_acquire_sys(flags + s) - epoch) < 0) {
       if (globaltimer_ns() - t0 > DSV4_WAIT_NS) {
         set_status(status, DSV4_ETIMEOUT);
+        if (n_recv) *n_recv = 0u;   // the layer then runs on no rows
         return;
       }
     }
+  }
+  if (n_recv) {
+    uint32_t n = 0;
+    for (int s = 0; s < world; ++s) n += (uint32_t)cnt[s * world + my_rank];
+    *n_recv = n;
   }
 }
 
@@ -407,7 +468,7 @@ extern "C" int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32
   ep->hidden = hidden;
   ep->blk = ep_block(world, cap_rows, hidden);
   DSV4_CUDA_CHECK(cudaMalloc(&ep->base, (size_t)ep->blk.bytes));
-  DSV4_CUDA_CHECK(cudaMemset(ep->base + ep->blk.off_flags, 0, (size_t)(ep->blk.bytes - ep->blk.off_flags)));
+  DSV4_CUDA_CHECK(cudaMemset(ep->base + ep->blk.off_e, 0, (size_t)(ep->blk.bytes - ep->blk.off_e)));
   cudaIpcMemHandle_t h;
   DSV4_CUDA_CHECK(cudaIpcGetMemHandle(&h, ep->base));
   memcpy(ipc_handle_out, &h, sizeof(h));
@@ -440,50 +501,62 @@ extern "C" int dsv4_ep_connect(dsv4_ep* ep, const void* handles) {
   DSV4_API_END
 }
 
-extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_meta, void** back) {
+extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_expert, float** recv_weight,
+                               int32_t** n_recv, void** back) {
   DSV4_API_BEGIN
-  DSV4_CHECK_ARG(ep && recv_x && recv_meta && back, "null pointer");
+  DSV4_CHECK_ARG(ep && recv_x && recv_expert && recv_weight && n_recv && back, "null pointer");
   *recv_x = ep->base;
   *back = ep->base + ep->blk.off_back;
-  *recv_meta = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_meta);
+  *recv_expert = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_e);
+  *recv_weight = reinterpret_cast<float*>(ep->base + ep->blk.off_w);
+  *n_recv = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_ctrl) + EPC_NRECV;
   DSV4_API_END
 }
 
 extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights,
                                 const int32_t* route_indices, int64_t n_tokens, int32_t topk, int32_t n_experts,
-                                int32_t* slot_of_assignment, int32_t* ordered_slots, int* status, void* stream) {
+                                const int32_t* expert_owner, int32_t* slot_of_assignment, int32_t* ordered_slots,
+                                int* status, void* stream) {
   DSV4_API_BEGIN
   if (int rc = ep_check(ep)) return rc;
   DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && slot_of_assignment && ordered_slots && status,
                  "null pointer");
   DSV4_CHECK_ARG(topk > 0 && topk <= 16 && n_tokens >= 0 && n_tokens * topk <= ep->cap,
                  "n_tokens * topk must be in [0, capacity] and topk in [1, 16]");
-  DSV4_CHECK_ARG(n_experts > 0 && n_experts % ep->world == 0, "n_experts must divide over the ranks");
+  DSV4_CHECK_ARG(n_experts > 0 && (expert_owner || n_experts % ep->world == 0),
+                 "n_experts must divide over the ranks (or pass expert_owner)");
   DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0, "rows must be 16-byte aligned");
   DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
   const int64_t P = n_tokens * topk;
   uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
-  DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, route_weights, P,
-                           (int)topk, (int)(n_experts / ep->world), ep->world, ep->rank, ep->cap,
-                           (uint8_t* const*)ep->peers_dev, ep->blk.off_meta, ctrl, slot_of_assignment, ordered_slots,
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(ep->base + ep->blk.off_flags);
+  const int32_t* cnt = reinterpret_cast<const int32_t*>(ep->base + ep->blk.off_cnt);
+  uint8_t* const* peers = (uint8_t* const*)ep->peers_dev;
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, P, (int)topk,
+                           (int)n_experts, (int)(n_experts / ep->world), expert_owner, ep->world, ep->rank, ep->cap,
+                           peers, ep->blk.off_cnt, ep->blk.off_flags, ctrl, slot_of_assignment, ordered_slots,
                            status));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags, (const uint32_t*)ctrl,
+                           ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((P * 32 + 255) / 256, 148 * 8));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
-                           (const uint16_t*)x_bf16, (const int32_t*)slot_of_assignment, P, (int)topk, ep->hidden,
-                           ep->world, ep->rank, ep->cap, (uint8_t* const*)ep->peers_dev, ep->blk.off_flags, ctrl));
-  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
-                           (const uint32_t*)(ep->base + ep->blk.off_flags), (const uint32_t*)ctrl, ep->world, status));
+                           (const uint16_t*)x_bf16, route_indices, route_weights,
+                           (const int32_t*)slot_of_assignment, P, (int)topk, ep->hidden, ep->world, ep->rank, ep->cap,
+                           peers, ep->blk, cnt, ctrl));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags + ep->world,
+                           (const uint32_t*)ctrl, ep->world, status, cnt, ep->rank, ctrl + EPC_NRECV));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
 
-extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* y_recv_bf16, int* status, void* stream) {
+extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_recv, int* status,
+                              void* stream) {
   DSV4_API_BEGIN
   if (int rc = ep_check(ep)) return rc;
-  DSV4_CHECK_ARG(y_recv_bf16 && status, "null pointer");
-  DSV4_CHECK_ARG(((uintptr_t)y_recv_bf16 % 16) == 0, "rows must be 16-byte aligned");
+  DSV4_CHECK_ARG(rows_bf16 && status, "null pointer");
+  DSV4_CHECK_ARG(((uintptr_t)rows_bf16 % 16) == 0, "rows must be 16-byte aligned");
   DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
@@ -491,12 +564,12 @@ extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* y_recv_bf16, int* status,
   const int64_t rows = (int64_t)ep->world * ep->cap;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows * 32 + 255) / 256, 148 * 8));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_return_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
-                           (const uint16_t*)y_recv_bf16, (const int2*)(ep->base + ep->blk.off_meta), ep->world,
-                           ep->rank, ep->cap, ep->hidden, (uint8_t* const*)ep->peers_dev, ep->blk.off_back,
-                           ep->blk.off_flags, ctrl));
+                           (const uint16_t*)rows_bf16, row_of_recv, (const int2*)(ep->base + ep->blk.off_src),
+                           (const uint32_t*)(ctrl + EPC_NRECV), ep->world, ep->rank, ep->cap, ep->hidden,
+                           (uint8_t* const*)ep->peers_dev, ep->blk.off_back, ep->blk.off_flags, ctrl));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
-                           (const uint32_t*)(ep->base + ep->blk.off_flags) + ep->world, (const uint32_t*)ctrl,
-                           ep->world, status));
+                           (const uint32_t*)(ep->base + ep->blk.off_flags) + 2 * ep->world, (const uint32_t*)ctrl,
+                           ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

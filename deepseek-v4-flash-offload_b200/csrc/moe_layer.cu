@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                      int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
                      float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
-                     int pad, int* status) {
+                     int pad, int* status, const int32_t* __restrict__ n_tokens_dev) {
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
@@ -121,10 +121,13 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   int* sidx = scratch + 32;      // AL_THREADS ints: scan scratch of the one-pass path
   uint16_t* wc = reinterpret_cast<uint16_t*>(sidx + AL_THREADS);  // [32][E] u16 (one pass) or u32 (two passes)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool small = P <= AL_THREADS;
   const int ebits = 32 - __clz(max(E - 1, 1));   // bits of the largest expert id
   griddep_wait();
   griddep_launch();
+  // a token count known only on the device (rows received by expert
+  // parallelism): the first n tokens of the buffers
+  if (n_tokens_dev) P = min(P, max(0, *n_tokens_dev) * topk);
+  const bool small = P <= AL_THREADS;
 
   if (small) {
     // Decode-sized batch, one assignment per thread, five barriers: the
@@ -335,9 +338,11 @@ __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, i
 // rows' scale words.
 __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
                                         int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
-                                        uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+                                        uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                        const int32_t* __restrict__ n_tokens_dev) {
   griddep_wait();
   griddep_launch();
+  if (n_tokens_dev) n_tokens = min(n_tokens, (int64_t)max(0, *n_tokens_dev));
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
   const int64_t ntask = n_tokens * kblk;
@@ -371,9 +376,11 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
 // E2M1 codes, round to nearest even, saturating; lanes 8g..8g+7 own block g.
 __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
                                           int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
-                                          uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+                                          uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                          const int32_t* __restrict__ n_tokens_dev) {
   griddep_wait();
   griddep_launch();
+  if (n_tokens_dev) n_tokens = min(n_tokens, (int64_t)max(0, *n_tokens_dev));
   const int lane = threadIdx.x & 31;
   const int kblk = K / 128;
   const int64_t ntask = n_tokens * kblk;
@@ -414,11 +421,11 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
 // ---------------------------------------------------------------------------
 // grid (T, H / (8 * blockDim.x)): each CTA covers 8 * blockDim.x columns.
 __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* __restrict__ inv, int topk, int H,
-                               uint16_t* __restrict__ y, int64_t T) {
+                               uint16_t* __restrict__ y, int64_t T, const int32_t* __restrict__ n_tokens_dev) {
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
-  if (t >= T) return;
+  if (t >= T || (n_tokens_dev && t >= *n_tokens_dev)) return;
   int pos[16];
   int k = 0;
   for (int j = 0; j < topk; ++j) {
@@ -739,11 +746,11 @@ extern "C" int dsv4_moe_plan_destroy(dsv4_moe_plan* plan) {
   return DSV4_OK;
 }
 
-extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
-                                const float* route_weights, const int32_t* route_indices,
-                                const int32_t* slot_of_expert, void* y_bf16, void* stream) {
+static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                            const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
+                            const int32_t* slot_of_expert, void* y_bf16, void* stream) {
   DSV4_API_BEGIN
-  DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert && y_bf16, "null pointer");
+  DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert, "null pointer");
   DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= p->max_tokens, "n_tokens exceeds the plan's max_tokens");
   DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)y_bf16 % 16) == 0, "x and y must be 16-byte aligned");
@@ -768,7 +775,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, p->topk,
                            p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets), sorted_flat,
                            inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                           wsp<int4>(p, w.chunks), n_chunks, bn, status));
+                           wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev));
   mark(1);
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
   const int64_t rb_cap = (w.p_cap + bn - 1) / bn;   // BN-row scale blocks per k-tile
@@ -778,7 +785,7 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
     DSV4_CUDA_CHECK(launch_k(fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
                              dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, n_tokens,
-                             p->topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf));
+                             p->topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf, n_tokens_dev));
   }
   mark(2);
   GemmParams g1{};
@@ -820,16 +827,39 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
   else
     DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, g2)));
   mark(4);
-  {
+  if (y_bf16) {
     const int threads = std::min(128, p->H / 8);
     const unsigned gy = (unsigned)std::max(1, p->H / (8 * threads));
     DSV4_CUDA_CHECK(launch_k(combine_kernel, dim3((unsigned)n_tokens, gy), dim3(threads), 0, st, pdl,
                              (const uint16_t*)wsp<uint16_t>(p, w.out), (const int32_t*)inv, p->topk, p->H,
-                             (uint16_t*)y_bf16, (int64_t)n_tokens));
+                             (uint16_t*)y_bf16, (int64_t)n_tokens, n_tokens_dev));
   }
   mark(5);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
+}
+
+extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                                const float* route_weights, const int32_t* route_indices,
+                                const int32_t* slot_of_expert, void* y_bf16, void* stream) {
+  if (!y_bf16) return fail(DSV4_EINVAL, "dsv4_moe_forward: null pointer");
+  return moe_forward_impl(p, profile, x_bf16, n_tokens, nullptr, route_weights, route_indices, slot_of_expert,
+                          y_bf16, stream);
+}
+
+extern "C" int dsv4_moe_forward_rows(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t max_tokens,
+                                     const int32_t* n_tokens_dev, const float* route_weights,
+                                     const int32_t* route_indices, const int32_t* slot_of_expert, void* y_bf16,
+                                     void* stream) {
+  return moe_forward_impl(p, profile, x_bf16, max_tokens, n_tokens_dev, route_weights, route_indices,
+                          slot_of_expert, y_bf16, stream);
+}
+
+extern "C" int dsv4_moe_output_rows(dsv4_moe_plan* p, void** rows_bf16, int32_t** inv) {
+  if (!p || !rows_bf16 || !inv) return fail(DSV4_EINVAL, "dsv4_moe_output_rows: null pointer");
+  *rows_bf16 = p->ws + p->wl.out;
+  *inv = wsp<int32_t>(p, p->wl.inv);
+  return DSV4_OK;
 }
 
 extern "C" int dsv4_moe_enable_timing(dsv4_moe_plan* p, int32_t enable) {
@@ -905,7 +935,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
       indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-      nullptr, nullptr, nullptr, 1, status);
+      nullptr, nullptr, nullptr, 1, status, nullptr);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

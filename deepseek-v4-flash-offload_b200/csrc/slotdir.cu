@@ -42,7 +42,10 @@
 namespace dsv4 {
 
 constexpr int SD_THREADS = 1024;
-constexpr int SD_FETCH_THREADS = 256;
+// 128 threads of at most 40 registers: one fetch CTA fits beside a grouped-GEMM
+// CTA on an SM (352 threads x 168 registers, 221 KB of shared memory), so a
+// prefetch runs under the GEMM instead of waiting for its SMs
+constexpr int SD_FETCH_THREADS = 128;
 constexpr int SD_STAT_N = 8;   // hits, misses, evictions, pf_hits, pf_fetched, pf_evictions, pf_skipped, batches
 
 struct SdHeader {
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(SD_THREADS, 1)
 
 // Copies the listed misses from the pinned host pool into their HBM slots:
 // every CTA walks the list, each thread moves 4 x 16 bytes per round.
-__global__ void __launch_bounds__(SD_FETCH_THREADS)
+__global__ void __launch_bounds__(SD_FETCH_THREADS, 16)
     slotdir_fetch_kernel(SdPtrs d, int mode, uint8_t* __restrict__ arena, int64_t slot_bytes) {
   const int n = *reinterpret_cast<volatile const int*>(&d.h->n_fetch[mode]);
   const int64_t nv = slot_bytes / 16;

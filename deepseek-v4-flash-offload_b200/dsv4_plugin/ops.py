@@ -259,6 +259,42 @@ class MoEPlan:
                                      so.data_ptr(), out.data_ptr(), _stream(x.device)))
         return out
 
+    def forward_rows(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, slot_of: torch.Tensor,
+                     profile: str = "bf16", n_tokens_dev: torch.Tensor | None = None):
+        """The layer without its combine, for a token count that may be known
+        only on the device (``n_tokens_dev``: int32 [1]; the first n rows of
+        ``x`` / ``weights`` / ``indices`` are used, at most ``x.shape[0]``).
+        Returns (rows bf16 [row capacity, H], inv int32 [T * k]): the output of
+        assignment a is ``rows[inv[a]]``; both live in the plan's workspace
+        until its next forward."""
+        _need_cuda(x, weights, indices, slot_of)
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise TypeError("x must be contiguous bf16")
+        t = x.shape[0]
+        if t > self.max_tokens:
+            raise ValueError(f"{t} tokens exceed the plan's max_tokens={self.max_tokens}")
+        w = weights if weights.dtype == torch.float32 and weights.is_contiguous() else weights.contiguous().float()
+        idx = indices if indices.dtype == torch.int32 and indices.is_contiguous() else \
+            indices.contiguous().to(torch.int32)
+        so = slot_of.contiguous().to(torch.int32)
+        check(lib().dsv4_moe_forward_rows(self._h, PROFILES[profile], x.data_ptr(), t,
+                                          None if n_tokens_dev is None else n_tokens_dev.data_ptr(), w.data_ptr(),
+                                          idx.data_ptr(), so.data_ptr(), None, _stream(x.device)))
+        return self.output_rows(t * self.topk)
+
+    def output_rows(self, n_assign: int):
+        rp, ip = C.c_void_p(), C.c_void_p()
+        check(lib().dsv4_moe_output_rows(self._h, C.byref(rp), C.byref(ip)))
+        rows = torch.as_tensor(_DevArray(rp.value, (self._rows_cap(), self.hidden), "<i2"), device=self.device)
+        inv = torch.as_tensor(_DevArray(ip.value, (max(n_assign, 1),), "<i4"), device=self.device)
+        return rows.view(torch.bfloat16), inv[:n_assign]
+
+    def _rows_cap(self) -> int:
+        # padded row capacity of the plan (same rule as the library's workspace layout)
+        p = self.max_tokens * self.topk
+        bn = 128
+        return (p + (bn - 1) * min(self.n_experts, p) + bn - 1) // bn * bn + bn
+
     STAGES = ("align", "quant_gather", "gate_up_gemm", "down_gemm", "combine")
 
     def set_gemm_tile(self, tokens_per_tile: int = 0) -> None:
@@ -313,6 +349,12 @@ class MoEPlan:
             except Exception:
                 pass
             self._h = None
+
+
+class _DevArray:
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3}
 
 
 def _memcpy_d2h(dst, src_ptr: int, nbytes: int):

@@ -1,6 +1,10 @@
 """Expert parallelism: the routed-expert layer sharded over ranks by expert.
 
-Expert e lives on rank ``e // (E / R)``.  One forward on every rank:
+Expert e lives on rank ``owner[e]``: by default ``e // (E / R)``; a
+load-balanced placement (``balanced_placement``, the static counterpart of
+the EPLB hooks the reference's layer carries, deepseek_v4.py:74-85) puts
+E / R experts on every rank so that the expected rows per rank are as even
+as the expert loads allow.  One forward on every rank:
   1. route the rank's own tokens (the same router kernel as one GPU);
   2. dispatch: order the T*k assignments by destination rank (stable), swap
      per-destination counts with an all-to-all, then all-to-all the token
@@ -23,21 +27,57 @@ import torch
 import torch.distributed as dist
 
 
+def contiguous_placement(n_experts: int, world: int) -> list:
+    """owner[e] = e // (E / R)."""
+    if n_experts % world:
+        raise ValueError("n_experts must divide evenly over the ranks")
+    return [e // (n_experts // world) for e in range(n_experts)]
+
+
+def balanced_placement(loads, world: int) -> list:
+    """Experts to ranks, E / R per rank, evening out the expected rows per
+    rank: experts in descending load, each to the least-loaded rank that has
+    room (ties: lower rank; equal loads: lower expert id first).  ``loads``:
+    per-expert row counts of a calibration batch."""
+    loads = [float(v) for v in loads]
+    n = len(loads)
+    if n % world:
+        raise ValueError("n_experts must divide evenly over the ranks")
+    room = [n // world] * world
+    tot = [0.0] * world
+    owner = [0] * n
+    for e in sorted(range(n), key=lambda i: (-loads[i], i)):
+        r = min((r for r in range(world) if room[r] > 0), key=lambda r: (tot[r], r))
+        owner[e] = r
+        room[r] -= 1
+        tot[r] += loads[e]
+    return owner
+
+
 class ExpertParallel:
     """Dispatch / combine bookkeeping of one expert-parallel layer."""
 
-    def __init__(self, n_experts: int, rank: int, world: int, group=None):
-        if n_experts % world:
-            raise ValueError("n_experts must divide evenly over the ranks")
+    def __init__(self, n_experts: int, rank: int, world: int, group=None, owner=None):
         self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
-        self.e_loc = n_experts // world
-        self.expert_lo = rank * self.e_loc
+        self.owner = list(owner) if owner is not None else contiguous_placement(n_experts, world)
+        if len(self.owner) != n_experts or sorted(set(self.owner)) != list(range(world)):
+            raise ValueError("owner must map every expert to a rank in [0, world)")
+        self.local = [e for e in range(n_experts) if self.owner[e] == rank]
+        self.e_loc = len(self.local)
+        self._owner_dev = {}
+
+    def owner_tensor(self, device) -> torch.Tensor:
+        t = self._owner_dev.get(str(device))
+        if t is None:
+            t = torch.tensor(self.owner, dtype=torch.int32, device=device)
+            self._owner_dev[str(device)] = t
+        return t
 
     def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
         """-> (x_recv [N,H], expert_recv [N] int32 global ids, w_recv [N] fp32, ctx)."""
         t, k = indices.shape
         flat_e = indices.reshape(-1).to(torch.int64)
-        dest = torch.div(flat_e, self.e_loc, rounding_mode="floor")
+        dest = self.owner_tensor(flat_e.device).to(torch.int64).index_select(0, flat_e)
         order = torch.sort(dest, stable=True).indices
         send = torch.bincount(dest, minlength=self.world)
         recv = torch.empty_like(send)
@@ -80,11 +120,10 @@ class StaticExchange:
     host synchronisation (stable sort, scatter_add, cumsum, gathers)."""
 
     def __init__(self, n_experts: int, rank: int, world: int, tokens: int, topk: int, hidden: int, device,
-                 group=None, dtype=torch.bfloat16):
-        if n_experts % world:
-            raise ValueError("n_experts must divide evenly over the ranks")
+                 group=None, dtype=torch.bfloat16, owner=None):
         self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
-        self.e_loc = n_experts // world
+        self.owner = torch.tensor(owner if owner is not None else contiguous_placement(n_experts, world),
+                                  dtype=torch.int32, device=device)
         self.t, self.k, self.h = tokens, topk, hidden
         self.cap = tokens * topk
         n = world * self.cap
@@ -110,13 +149,14 @@ class StaticExchange:
             d = self._dev
             x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
             check(lib().dsv4_ep_dispatch_pack(x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.k, self.h,
-                                              self.n_experts, self.world, self.send_x.data_ptr(),
+                                              self.n_experts, self.world, self.owner.data_ptr(),
+                                              self.send_x.data_ptr(),
                                               self.send_meta.data_ptr(), d["pos"].data_ptr(),
                                               d["ordered"].data_ptr(), d["status"].data_ptr(),
                                               torch.cuda.current_stream(x.device).cuda_stream))
             return d["pos"]
         flat_e = indices.reshape(-1).to(torch.int64)
-        dest = torch.div(flat_e, self.e_loc, rounding_mode="floor")
+        dest = self.owner.to(torch.int64).index_select(0, flat_e)
         order = torch.sort(dest, stable=True).indices
         counts = torch.zeros(self.world, dtype=torch.int64, device=dest.device)
         counts.scatter_add_(0, dest, torch.ones_like(dest))
@@ -158,24 +198,27 @@ class _DevPtr:
 
 
 class P2PExchange:
-    """Exchange over NVLink peer memory (``dsv4_ep_*``): the same slots as
-    ``StaticExchange``, but each rank writes only its real rows straight
-    into the owners' receive blocks (mapped through CUDA IPC) and the owners
-    write the expert outputs straight back; device flags with a per-step
-    epoch replace the collectives.  No host synchronisation; capturable in a
-    CUDA graph.  Creating it is collective (the IPC handles are gathered)."""
+    """Exchange over NVLink peer memory (``dsv4_ep_*``) with exact per-peer
+    counts: each source first publishes how many rows it sends to every
+    owner, then writes only its real rows, compactly, straight into the
+    owners' receive blocks (mapped through CUDA IPC); the owners run the
+    layer on exactly the rows they received (a device-side count, no host
+    synchronisation) and write the expert outputs straight back.  Device
+    flags with a per-step epoch replace the collectives; the step can be
+    captured in a CUDA graph.  Creating it is collective (the IPC handles are
+    gathered)."""
 
     def __init__(self, n_experts: int, rank: int, world: int, tokens: int, topk: int, hidden: int, device,
-                 group=None):
+                 group=None, owner=None):
         import ctypes as C
 
         from dsv4_plugin._lib import check, lib
-        if n_experts % world:
-            raise ValueError("n_experts must divide evenly over the ranks")
         self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
         self.t, self.k, self.h = tokens, topk, hidden
         self.cap = tokens * topk
         self.device = torch.device(device)
+        self.owner = torch.tensor(owner if owner is not None else contiguous_placement(n_experts, world),
+                                  dtype=torch.int32, device=self.device)
         nb = lib().dsv4_ep_ipc_handle_bytes()
         handle = C.create_string_buffer(nb)
         self._h = C.c_void_p()
@@ -185,28 +228,36 @@ class P2PExchange:
         dist.all_gather_into_tensor(every, mine, group=group)
         allh = every.cpu().numpy().tobytes()
         check(lib().dsv4_ep_connect(self._h, C.create_string_buffer(allh, len(allh))))
-        rx, rm, bk = C.c_void_p(), C.c_void_p(), C.c_void_p()
-        check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(rm), C.byref(bk)))
+        rx, re_, rw, rn, bk = (C.c_void_p() for _ in range(5))
+        check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(re_), C.byref(rw), C.byref(rn), C.byref(bk)))
         rows = world * self.cap
-        self.recv_x = torch.as_tensor(_DevPtr(rx.value, (rows, hidden), "<i2"), device=self.device).view(torch.bfloat16)
-        self.recv_meta = torch.as_tensor(_DevPtr(rm.value, (rows, 2), "<i4"), device=self.device)
-        self.back = torch.as_tensor(_DevPtr(bk.value, (rows, hidden), "<i2"), device=self.device).view(torch.bfloat16)
-        self.pos = torch.empty(self.cap, dtype=torch.int32, device=self.device)
-        self.ordered = torch.empty((tokens, topk), dtype=torch.int32, device=self.device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        dev = self.device
+        self.recv_x = torch.as_tensor(_DevPtr(rx.value, (rows, hidden), "<i2"), device=dev).view(torch.bfloat16)
+        self.recv_e = torch.as_tensor(_DevPtr(re_.value, (rows,), "<i4"), device=dev)
+        self.recv_w = torch.as_tensor(_DevPtr(rw.value, (rows,), "<f4"), device=dev)
+        self.n_recv = torch.as_tensor(_DevPtr(rn.value, (1,), "<i4"), device=dev)
+        self.back = torch.as_tensor(_DevPtr(bk.value, (rows, hidden), "<i2"), device=dev).view(torch.bfloat16)
+        self.pos = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        self.ordered = torch.empty((tokens, topk), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
+        """-> (recv_x, recv_expert, recv_weight, n_recv): the received rows
+        (the first *n_recv of the buffers) and their device-side count."""
         from dsv4_plugin._lib import check, lib
         x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
         check(lib().dsv4_ep_dispatch(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.k,
-                                     self.n_experts, self.pos.data_ptr(), self.ordered.data_ptr(),
-                                     self.status.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
-        return self.recv_x, self.recv_meta[:, 0], self.recv_meta[:, 1].view(torch.float32)
+                                     self.n_experts, self.owner.data_ptr(), self.pos.data_ptr(),
+                                     self.ordered.data_ptr(), self.status.data_ptr(),
+                                     torch.cuda.current_stream(self.device).cuda_stream))
+        return self.recv_x, self.recv_e, self.recv_w, self.n_recv
 
-    def give_back(self, y_recv: torch.Tensor):
+    def give_back(self, rows: torch.Tensor, row_of_recv: torch.Tensor | None = None):
+        """Send the expert output of received row j (``rows[row_of_recv[j]]``,
+        or ``rows[j]``) back to its source; -> this rank's ``back`` rows."""
         from dsv4_plugin._lib import check, lib
-        y = y_recv.contiguous()
-        check(lib().dsv4_ep_return(self._h, y.data_ptr(), self.status.data_ptr(),
+        check(lib().dsv4_ep_return(self._h, rows.data_ptr(),
+                                   None if row_of_recv is None else row_of_recv.data_ptr(), self.status.data_ptr(),
                                    torch.cuda.current_stream(self.device).cuda_stream))
         return self.back
 
@@ -231,16 +282,16 @@ class P2PExchange:
 
 class ExpertParallelMoE:
     """Expert-parallel forward of an ``OffloadDeepseekV4MoE`` whose bank
-    holds this rank's experts."""
+    holds this rank's experts (``owner[e] == rank``; default contiguous)."""
 
-    def __init__(self, moe, rank: int, world: int, group=None):
+    def __init__(self, moe, rank: int, world: int, group=None, owner=None):
         self.moe = moe
-        self.ep = ExpertParallel(moe.n_routed_experts, rank, world, group)
+        self.ep = ExpertParallel(moe.n_routed_experts, rank, world, group, owner)
         bank = moe.engine.bank
-        lo, n = self.ep.expert_lo, self.ep.e_loc
-        slots = bank.ensure_resident(moe.layer_idx, list(range(lo, lo + n)))
+        local = self.ep.local
+        slots = bank.ensure_resident(moe.layer_idx, local)
         table = torch.full((moe.n_routed_experts,), -1, dtype=torch.int32)
-        table[lo:lo + n] = torch.tensor(slots, dtype=torch.int32)
+        table[torch.tensor(local, dtype=torch.long)] = torch.tensor(slots, dtype=torch.int32)
         self.slot_of = table.to(bank.device)
         self.plan = None
         self._static = {}
@@ -257,7 +308,7 @@ class ExpertParallelMoE:
         ex = self._static.get(t)
         if ex is None:
             ex = StaticExchange(moe.n_routed_experts, self.ep.rank, self.ep.world, t, moe.topk, hs.shape[1],
-                                hs.device, self.ep.group)
+                                hs.device, self.ep.group, owner=self.ep.owner)
             self._static[t] = ex
         marks = [] if self.segment_times is not None else None
 
@@ -289,17 +340,20 @@ class ExpertParallelMoE:
         return y
 
     def forward_p2p(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
-        """The same layer through ``P2PExchange`` (NVLink peer memory): no
-        collectives, no host synchronisation; capturable in a CUDA graph.
-        Equals ``forward`` bit for bit.  The first call with a new token
-        count is collective (it maps the peers' buffers)."""
+        """The same layer through ``P2PExchange`` (NVLink peer memory, exact
+        counts): no collectives, no host synchronisation; capturable in a
+        CUDA graph.  The owner runs the experts on exactly the rows it
+        received and returns each output row straight from the layer's sorted
+        output (no combine pass on the owner).  Equals ``forward`` bit for
+        bit.  The first call with a new token count is collective (it maps
+        the peers' buffers)."""
         from dsv4_plugin import ops
         moe = self.moe
         t = hs.shape[0]
         ex = self._p2p.get(t)
         if ex is None:
             ex = P2PExchange(moe.n_routed_experts, self.ep.rank, self.ep.world, t, moe.topk, hs.shape[1],
-                             hs.device, self.ep.group)
+                             hs.device, self.ep.group, owner=self.ep.owner)
             self._p2p[t] = ex
         marks = [] if self.segment_times is not None else None
 
@@ -312,13 +366,14 @@ class ExpertParallelMoE:
         mark()
         w, idx = moe._route(hs, None)
         mark()
-        x_recv, e_recv, w_recv = ex.dispatch(hs, w, idx)
+        x_recv, e_recv, w_recv, n_recv = ex.dispatch(hs, w, idx)
         mark()
         plan = moe.engine.plan_for(moe.n_routed_experts, 1, x_recv.shape[0], moe.swiglu_limit or 0.0)
         self.plan = plan
-        y_recv = plan.forward(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile)
+        rows, inv = plan.forward_rows(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile,
+                                      n_tokens_dev=n_recv)
         mark()
-        back = ex.give_back(y_recv)
+        back = ex.give_back(rows, inv)
         mark()
         y = ops.combine_ordered(back, ex.ordered)
         mark()

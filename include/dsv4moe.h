@@ -174,6 +174,18 @@ int dsv4_moe_plan_destroy(dsv4_moe_plan* plan);
 int dsv4_moe_forward(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t n_tokens,
                      const float* route_weights, const int32_t* route_indices, const int32_t* slot_of_expert,
                      void* y_bf16, void* stream);
+/* The same layer for a batch whose token count is known only on the device
+ * (the rows that expert parallelism received): the first *n_tokens_dev
+ * (<= max_tokens) rows of x and of the router outputs are used.  y_bf16 may
+ * be NULL: the combine is then skipped and the per-assignment output rows
+ * stay in the plan (dsv4_moe_output_rows), in sorted order: row inv[a] of
+ * `rows` is assignment a = t * topk + j.  No counterpart in the reference. */
+int dsv4_moe_forward_rows(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t max_tokens,
+                          const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
+                          const int32_t* slot_of_expert, void* y_bf16, void* stream);
+/* Device pointers of the last forward's per-assignment output rows (bf16
+ * [rows, hidden], sorted by expert) and of inv (int32 [n_tokens * topk]). */
+int dsv4_moe_output_rows(dsv4_moe_plan* plan, void** rows_bf16, int32_t** inv);
 /* Synchronises `stream`, returns the plan's device status word (0 or a
  * DSV4_E* code recorded by a kernel) and clears it. */
 int dsv4_moe_status(dsv4_moe_plan* plan, void* stream);
@@ -280,7 +292,8 @@ int dsv4_slotdir_clear(dsv4_slotdir* dir, void* stream);
 /* ------------------------------------------------------------------------ *
  * Expert-parallel dispatch packing (no counterpart in the reference, whose
  * expert-parallel size is 1, deepseek_v4.py:82).  Expert e lives on rank
- * e / (n_experts / world).  Every rank sends cap = n_tokens * topk rows to
+ * expert_owner[e] (device int32 [n_experts]; NULL: e / (n_experts / world),
+ * which then must divide).  Every rank sends cap = n_tokens * topk rows to
  * every peer, so the all-to-all has a fixed shape (graph-capturable).  For
  * assignment a = t*topk + j with destination d the slot is d*cap + its rank
  * among the assignments to d (stable):
@@ -291,42 +304,51 @@ int dsv4_slotdir_clear(dsv4_slotdir* dir, void* stream);
  * (-1 after the last), the order in which the returned rows are added.
  * send_x: [world*cap, hidden] bf16; send_meta: [world*cap, 2] int32;
  * slot_of_assignment, ordered_slots: [n_tokens*topk] int32.  An expert id
- * outside [0, n_experts) sets DSV4_EINVAL in *status and is dropped.
+ * of -1 is skipped; any other id outside [0, n_experts) (or an owner outside
+ * [0, world)) sets DSV4_EINVAL in *status and is dropped.
  * ------------------------------------------------------------------------ */
 int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weights, const int32_t* route_indices,
                           int64_t n_tokens, int32_t topk, int32_t hidden, int32_t n_experts, int32_t world,
-                          void* send_x_bf16, int32_t* send_meta, int32_t* slot_of_assignment,
-                          int32_t* ordered_slots, int* status, void* stream);
+                          const int32_t* expert_owner, void* send_x_bf16, int32_t* send_meta,
+                          int32_t* slot_of_assignment, int32_t* ordered_slots, int* status, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Expert-parallel exchange over NVLink peer memory (no counterpart in the
- * reference).  Each rank owns one device block (recv rows, their metadata,
- * returned rows, flags); peers map it through CUDA IPC and write into it
- * directly, only real rows crossing NVLink.  Per step:
- *   dsv4_ep_dispatch: slots as dsv4_ep_dispatch_pack; metadata and rows
- *     written into the owners' blocks (source s fills rows s*cap.. of the
- *     owner); then waits (bounded, DSV4_ETIMEOUT in *status) until every
- *     source published this step;
- *   (the routed-expert layer runs on recv_x / recv_meta, world*cap rows)
- *   dsv4_ep_return: each received real row back into its source's `back`
- *     (owner d fills rows d*cap..), then waits for every owner;
+ * reference).  Each rank owns one device block; peers map it through CUDA
+ * IPC and write into it directly, only real rows crossing NVLink.  Per step:
+ *   dsv4_ep_dispatch: per-destination slots as dsv4_ep_dispatch_pack (with
+ *     the same expert_owner map); each source first publishes its per-peer
+ *     counts to every peer, then writes its rows, experts and weights into
+ *     the owners' blocks, compact: owner d holds the rows of source s at
+ *     sum_{s'<s} n[s'->d] + r; waits (bounded, DSV4_ETIMEOUT in *status)
+ *     until every source published; the number of rows received is then in
+ *     the device word *n_recv (dsv4_ep_buffers);
+ *   (the routed-expert layer runs on recv_x / recv_expert / recv_weight,
+ *     topk = 1, with the device count: dsv4_moe_forward_rows)
+ *   dsv4_ep_return: each received row j < *n_recv back into its source's
+ *     `back` (owner d fills rows d*cap + r), read as row row_of_recv[j] of
+ *     `rows` (the layer's sorted output rows and its inv; NULL: row j), then
+ *     waits for every owner;
  *   dsv4_moe_combine_ordered(back, ordered_slots, ...) gives the output.
- * Every call is an asynchronous device operation with a fixed shape, so a
- * step can be captured in a CUDA graph.  All ranks must make the same calls
- * in the same order.  cap = capacity rows per source (n_tokens * topk).
- * The IPC handle is dsv4_ep_ipc_handle_bytes() bytes; dsv4_ep_connect takes
- * all ranks' handles, rank-major.
+ * Every call is an asynchronous device operation with a fixed launch shape,
+ * so a step can be captured in a CUDA graph.  All ranks must make the same
+ * calls in the same order.  cap = capacity rows per source (n_tokens*topk).
+ * After a DSV4_ETIMEOUT the step's data are undefined and a late peer may
+ * still write into this rank's block: destroy the handle and create a new
+ * one.  The IPC handle is dsv4_ep_ipc_handle_bytes() bytes; dsv4_ep_connect
+ * takes all ranks' handles, rank-major.
  * ------------------------------------------------------------------------ */
 typedef struct dsv4_ep dsv4_ep;
 int dsv4_ep_ipc_handle_bytes(void);
 int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t cap_rows, int32_t hidden,
                    void* ipc_handle_out);
 int dsv4_ep_connect(dsv4_ep* ep, const void* all_handles);
-int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_meta, void** back_bf16);
+int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_expert, float** recv_weight, int32_t** n_recv,
+                    void** back_bf16);
 int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights, const int32_t* route_indices,
-                     int64_t n_tokens, int32_t topk, int32_t n_experts, int32_t* slot_of_assignment,
-                     int32_t* ordered_slots, int* status, void* stream);
-int dsv4_ep_return(dsv4_ep* ep, const void* y_recv_bf16, int* status, void* stream);
+                     int64_t n_tokens, int32_t topk, int32_t n_experts, const int32_t* expert_owner,
+                     int32_t* slot_of_assignment, int32_t* ordered_slots, int* status, void* stream);
+int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_recv, int* status, void* stream);
 int dsv4_ep_destroy(dsv4_ep* ep);
 
 #ifdef __cplusplus

@@ -8,6 +8,7 @@ same computation done locally on one rank, bit for bit."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
@@ -48,7 +49,18 @@ def _local_reference(x, w, idx):
     return y.to(torch.bfloat16)
 
 
-def _worker(rank, world, port, n_experts, tokens, topk, out):
+def _owner(kind, n_experts, world):
+    if kind is None:
+        return None
+    g = torch.Generator().manual_seed(7)
+    perm = torch.randperm(n_experts, generator=g).tolist()   # a scattered placement, E / R per rank
+    owner = [0] * n_experts
+    for i, e in enumerate(perm):
+        owner[e] = i % world
+    return owner
+
+
+def _worker(rank, world, port, n_experts, tokens, topk, out, placement=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -61,9 +73,9 @@ def _worker(rank, world, port, n_experts, tokens, topk, out):
         if tokens:
             idx[: tokens // 2, 0] = n_experts - 1          # skew toward the last rank
         w = torch.rand(tokens, topk, generator=g)
-        ep = ExpertParallel(n_experts, rank, world)
+        ep = ExpertParallel(n_experts, rank, world, owner=_owner(placement, n_experts, world))
         x_recv, e_recv, w_recv, ctx = ep.dispatch(x, w, idx)
-        assert bool(((e_recv >= ep.expert_lo) & (e_recv < ep.expert_lo + ep.e_loc)).all())
+        assert set(e_recv.tolist()) <= set(ep.local)
         y_recv = _expert_fn(x_recv, e_recv, w_recv)
         rows, order = ep.combine_rows(y_recv, ctx)
         y = _combine_py(rows, order)
@@ -73,16 +85,32 @@ def _worker(rank, world, port, n_experts, tokens, topk, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tokens", [0, 1, 37])
-def test_ep_dispatch_combine_gloo_world2(tokens):
+@pytest.mark.parametrize("tokens,placement", [(0, None), (1, None), (37, None), (37, "scattered")])
+def test_ep_dispatch_combine_gloo_world2(tokens, placement):
     world, n_experts, topk = 2, 16, 4
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker, args=(world, _free_port(), n_experts, tokens, topk, out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), n_experts, tokens, topk, out, placement), nprocs=world, join=True)
     assert dict(out) == {0: True, 1: True}
 
 
-def _worker_static(rank, world, port, n_experts, tokens, topk, out):
+def test_balanced_placement_evens_the_rows_per_rank():
+    from dsv4_plugin.parallel_ep import balanced_placement, contiguous_placement
+    rng = np.random.default_rng(0)
+    loads = (1.0 / (1 + rng.permutation(256)) ** 1.1) * 10000     # Zipf(1.1) over a random permutation
+    for world in (2, 4, 8):
+        own = balanced_placement(loads, world)
+        assert [own.count(r) for r in range(world)] == [256 // world] * world
+        per = np.bincount(own, weights=loads, minlength=world)
+        cont = np.bincount(contiguous_placement(256, world), weights=loads, minlength=world)
+        assert per.max() / per.mean() <= cont.max() / cont.mean()
+        # no rank above the mean by more than 5 %, except the one that must
+        # hold the heaviest expert, which then carries the lightest others
+        fill = np.sort(loads)[: 256 // world - 1].sum()
+        assert per.max() <= max(loads.max() + fill, 1.05 * per.mean())
+
+
+def _worker_static(rank, world, port, n_experts, tokens, topk, out, placement=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -93,14 +121,15 @@ def _worker_static(rank, world, port, n_experts, tokens, topk, out):
         idx = torch.stack([torch.randperm(n_experts, generator=g)[:topk] for _ in range(tokens)]).to(torch.int32)
         idx[: tokens // 2, 0] = n_experts - 1
         w = torch.rand(tokens, topk, generator=g)
-        ex = StaticExchange(n_experts, rank, world, tokens, topk, 64, "cpu")
+        owner = _owner(placement, n_experts, world)
+        ex = StaticExchange(n_experts, rank, world, tokens, topk, 64, "cpu", owner=owner)
+        own = torch.tensor(owner if owner is not None else [e // (n_experts // world) for e in range(n_experts)])
         pos = ex.pack(x, w, idx)
         x_recv, e_recv, w_recv = ex.exchange()
         valid = e_recv >= 0
-        e_loc = n_experts // world
-        ok = bool(((e_recv[valid] >= rank * e_loc) & (e_recv[valid] < (rank + 1) * e_loc)).all())
+        ok = bool((own[e_recv[valid].to(torch.int64)] == rank).all())
         # every assignment destined to this rank arrives exactly once
-        to_rank = torch.bincount(idx.reshape(-1).to(torch.int64) // e_loc, minlength=world)
+        to_rank = torch.bincount(own[idx.reshape(-1).to(torch.int64)], minlength=world)
         dist.all_reduce(to_rank)
         ok = ok and int(valid.sum()) == int(to_rank[rank])
         y_recv = torch.zeros_like(x_recv)
@@ -113,12 +142,13 @@ def _worker_static(rank, world, port, n_experts, tokens, topk, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tokens", [1, 29])
-def test_ep_static_exchange_gloo_world2(tokens):
+@pytest.mark.parametrize("tokens,placement", [(1, None), (29, None), (29, "scattered")])
+def test_ep_static_exchange_gloo_world2(tokens, placement):
     """Fixed-capacity exchange (padding rows with expert -1): same result as
     the local computation, and every assignment reaches its owner once."""
     world, n_experts, topk = 2, 16, 4
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker_static, args=(world, _free_port(), n_experts, tokens, topk, out), nprocs=world, join=True)
+    mp.spawn(_worker_static, args=(world, _free_port(), n_experts, tokens, topk, out, placement), nprocs=world,
+             join=True)
     assert dict(out) == {0: True, 1: True}

@@ -24,7 +24,16 @@ def _port():
     return p
 
 
-def _run(rank, world, port, tokens, out):
+def _scattered(n_experts, world):
+    g = torch.Generator().manual_seed(11)
+    perm = torch.randperm(n_experts, generator=g).tolist()
+    owner = [0] * n_experts
+    for i, e in enumerate(perm):
+        owner[e] = i % world
+    return owner
+
+
+def _run(rank, world, port, tokens, out, scattered=False):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
@@ -48,10 +57,11 @@ def _run(rank, world, port, tokens, out):
         xt = torch.from_numpy(S.to_bf16_bits(x).astype(np.int16)).view(torch.bfloat16).to(dev)
         full.engine.bank.preload_all(3)
         ref = full.forward(xt).clone()
-        e_loc = cfg.n_experts // world
-        mine = {e: allx[e] for e in range(rank * e_loc, (rank + 1) * e_loc)}
+        owner = _scattered(cfg.n_experts, world) if scattered else \
+            [e // (cfg.n_experts // world) for e in range(cfg.n_experts)]
+        mine = {e: allx[e] for e in range(cfg.n_experts) if owner[e] == rank}
         part, _ = make_plugin_layer(cfg, mine, dev)
-        epm = ExpertParallelMoE(part, rank, world)
+        epm = ExpertParallelMoE(part, rank, world, owner=owner if scattered else None)
         for profile in ("bf16", "a4w4"):
             from dsv4_plugin.models import deepseek_v4 as DV4
             DV4._MXFP4_GMM = profile == "a4w4"
@@ -111,17 +121,20 @@ def test_ep_world1_equals_single_gpu(tokens):
                          (0, "p2p"): True, (0, "p2p_graph"): True}
 
 
-def test_ep_world2_equals_single_gpu():
+@pytest.mark.parametrize("scattered", [False, True])
+def test_ep_world2_equals_single_gpu(scattered):
+    """World 2, contiguous and scattered expert placement (expert_owner map)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_run, args=(2, _port(), 33, out), nprocs=2, join=True)
+    mp.spawn(_run, args=(2, _port(), 33, out, scattered), nprocs=2, join=True)
     assert all(out.values()) and len(out) == 12
 
 
-@pytest.mark.parametrize("world,tokens,topk", [(2, 33, 8), (8, 64, 8), (4, 300, 6)])
-def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk):
+@pytest.mark.parametrize("world,tokens,topk,scattered", [(2, 33, 8, False), (8, 64, 8, False), (4, 300, 6, False),
+                                                       (4, 300, 6, True)])
+def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk, scattered):
     """dsv4_ep_dispatch_pack against the same bookkeeping in torch ops (the
     CPU path of StaticExchange.pack): slots, metadata, rows, combine order."""
     if not torch.cuda.is_available():
@@ -132,10 +145,11 @@ def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk):
     x = torch.randn(tokens, h, generator=g).to(torch.bfloat16)
     idx = torch.stack([torch.randperm(n_experts, generator=g)[:topk] for _ in range(tokens)]).to(torch.int32)
     w = torch.rand(tokens, topk, generator=g)
-    ref = StaticExchange(n_experts, 0, world, tokens, topk, h, "cpu")
+    owner = _scattered(n_experts, world) if scattered else None
+    ref = StaticExchange(n_experts, 0, world, tokens, topk, h, "cpu", owner=owner)
     pos_ref = ref.pack(x, w, idx)
     ord_ref = ref.order(pos_ref, idx)
-    dev = StaticExchange(n_experts, 0, world, tokens, topk, h, "cuda")
+    dev = StaticExchange(n_experts, 0, world, tokens, topk, h, "cuda", owner=owner)
     pos = dev.pack(x.cuda(), w.cuda(), idx.cuda())
     torch.cuda.synchronize()
     assert torch.equal(pos.cpu().to(torch.int64), pos_ref)
@@ -146,10 +160,11 @@ def test_dispatch_pack_kernel_matches_torch_bookkeeping(world, tokens, topk):
     assert int(dev._dev["status"].item()) == 0
 
 
-def test_ep_world4_equals_single_gpu():
+@pytest.mark.parametrize("scattered", [False, True])
+def test_ep_world4_equals_single_gpu(scattered):
     if torch.cuda.device_count() < 4:
         pytest.skip("needs four GPUs")
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_run, args=(4, _port(), 40, out), nprocs=4, join=True)
+    mp.spawn(_run, args=(4, _port(), 40, out, scattered), nprocs=4, join=True)
     assert all(out.values()) and len(out) == 24
