@@ -111,3 +111,43 @@ extern "C" int dsv4_unpack_expert_host(const uint8_t* slot, int32_t hidden, int3
   unpack_matrix(slot + L.w2p, slot + L.sf2, H, I, w2p, w2s, [](int64_t r) { return r; });
   DSV4_API_END
 }
+
+// ---------------------------------------------------------------------------
+// Shared expert (deepseek_v4.py:87-100; model_npu.py:469-491 Expert in "fp8"
+// mode): w1 / w3 [I, H] and w2 [H, I] E4M3 with one E8M0 scale per 128 x 128
+// block (npu_ops.py:161-167 dequant_fp8_weight), packed into the FP8 slot the
+// grouped GEMM reads (slot_layout.h w8_pair_offset): the block scale is
+// written as the per-32 scale of each of its four 32-element groups.
+// ---------------------------------------------------------------------------
+namespace dsv4 {
+template <typename RowMap>
+static void pack_matrix_fp8(const uint8_t* w, const uint8_t* s, int64_t rows, int64_t k, uint8_t* wdst, uint8_t* sdst,
+                            RowMap row_of) {
+  const int64_t kb_n = k / 32, sk = (k + 127) / 128;
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t R = row_of(r);
+    for (int64_t kt = 0; kt < k / 128; ++kt) memcpy(wdst + w8_pair_offset(R, kt * 128, k), w + r * k + kt * 128, 128);
+    for (int64_t kb = 0; kb < kb_n; ++kb) sdst[sf_pair_offset(R, kb, k)] = s[(r / 128) * sk + kb / 4];
+  }
+}
+}  // namespace dsv4
+
+extern "C" int64_t dsv4_shared_slot_bytes(int32_t hidden, int32_t inter) {
+  if (hidden <= 0 || inter <= 0 || hidden % 256 || inter % 128) return DSV4_EINVAL;
+  return shared_slot_layout(hidden, inter).bytes;
+}
+
+extern "C" int dsv4_pack_shared_host(const uint8_t* w1, const uint8_t* s1, const uint8_t* w2, const uint8_t* s2,
+                                     const uint8_t* w3, const uint8_t* s3, int32_t hidden, int32_t inter,
+                                     uint8_t* slot) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(w1 && s1 && w2 && s2 && w3 && s3 && slot, "null pointer");
+  DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 256 == 0 && inter % 128 == 0,
+                 "hidden must be a positive multiple of 256 and inter of 128");
+  const SlotLayout L = shared_slot_layout(hidden, inter);
+  const int64_t H = hidden, I = inter;
+  pack_matrix_fp8(w1, s1, I, H, slot + L.w13p, slot + L.sf13, [](int64_t r) { return w13_pair_row(r, 0); });
+  pack_matrix_fp8(w3, s3, I, H, slot + L.w13p, slot + L.sf13, [](int64_t r) { return w13_pair_row(r, 1); });
+  pack_matrix_fp8(w2, s2, H, I, slot + L.w2p, slot + L.sf2, [](int64_t r) { return r; });
+  DSV4_API_END
+}

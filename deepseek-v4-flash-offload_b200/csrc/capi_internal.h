@@ -65,6 +65,18 @@ inline SlotLayout slot_layout(int64_t hidden, int64_t inter) {
   return L;
 }
 
+// Byte layout of the shared expert's FP8 slot: [w13 E4M3 | w2 E4M3 | w13
+// scale atoms | w2 scale atoms], blocks as the packed slot but 1 B / element.
+inline SlotLayout shared_slot_layout(int64_t hidden, int64_t inter) {
+  SlotLayout L;
+  L.w13p = 0;
+  L.w2p = L.w13p + 2 * inter * hidden;
+  L.sf13 = L.w2p + hidden * inter;
+  L.sf2 = L.sf13 + 2 * inter * hidden / 32;
+  L.bytes = L.sf2 + hidden * inter / 32;
+  return L;
+}
+
 }  // namespace dsv4
 
 #define DSV4_API_BEGIN try {

@@ -378,12 +378,13 @@ __device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
   d |= (uint64_t)1u << 46;
   return d;
 }
-// Instruction descriptor of kind::mxf8f6f4.block_scale with A = E2M1,
-// B = E4M3 (b_fp4 = false) or E2M1, M = 128, E8M0 scales, both K-major.
-__host__ __device__ __forceinline__ uint32_t idesc_mxf8f6f4(int n, bool b_fp4, uint32_t sf_id) {
+// Instruction descriptor of kind::mxf8f6f4.block_scale with A = E2M1 (or
+// E4M3 with a_e4m3: the shared expert's FP8 weights), B = E4M3 (b_fp4 =
+// false) or E2M1, M = 128, E8M0 scales, both K-major.
+__host__ __device__ __forceinline__ uint32_t idesc_mxf8f6f4(int n, bool b_fp4, uint32_t sf_id, bool a_e4m3 = false) {
   uint32_t d = 0;
   d |= (sf_id & 3u) << 4;              // B scale-factor id
-  d |= 5u << 7;                        // A format E2M1
+  d |= (a_e4m3 ? 0u : 5u) << 7;        // A format E4M3 / E2M1
   d |= (b_fp4 ? 5u : 0u) << 10;        // B format E2M1 / E4M3
   d |= ((uint32_t)(n >> 3) & 63u) << 17;
   d |= 1u << 23;                       // scale format UE8M0

@@ -102,6 +102,11 @@ struct GemmParams {
   int out_ld;                // elements per output row (I or H)
   float swiglu_limit;
   int* status;
+  // the shared expert (bf16 profile): chunks of expert `shared_expert` read
+  // E4M3 weights from the FP8 slot at `shared_slot` (tensor map tmAsh)
+  int shared_expert;         // -1: none
+  const uint8_t* shared_slot;
+  int64_t shared_sfa_off;    // byte offset of its A scale atoms
 };
 
 __device__ __forceinline__ float warp_max_f(float v) {
@@ -120,15 +125,21 @@ struct TileInfo {
   int row0;   // first row of the 64-row chunk
   int nrows;  // valid rows in the chunk
   int mt;     // 128-row tile of the weight matrix
+  bool sh;    // the shared expert (FP8 weights)
 };
 
 __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_tiles) {
-  TileInfo ti{-1, 0, 0, 0};
+  TileInfo ti{-1, 0, 0, 0, false};
   if (t < n_tiles) {
     const int c = t / p.a_row_tiles;
     const int4 ch = p.chunks[c];
-    const int s = p.slot_of[ch.x];
-    ti.slot = (s >= 0 && s < p.n_slots) ? s : -1;
+    if (ch.x == p.shared_expert) {
+      ti.sh = true;
+      ti.slot = 0;
+    } else {
+      const int s = p.slot_of[ch.x];
+      ti.slot = (s >= 0 && s < p.n_slots) ? s : -1;
+    }
     ti.row0 = ch.y;
     ti.nrows = ch.z;
     ti.mt = t - c * p.a_row_tiles;
@@ -170,7 +181,8 @@ template <int NUM_A, bool B_FP4, int EPI, int BN>
 __global__ void __launch_bounds__(G_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB16,
                     const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
-                    const __grid_constant__ CUtensorMap tmBwide, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmBwide, const __grid_constant__ CUtensorMap tmAsh,
+                    const GemmParams p) {
   static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
   using C = GemmCfg<NUM_A, BN, B_FP4>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -207,6 +219,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     prefetch_tensormap(&tmB32);
     prefetch_tensormap(&tmB64);
     if (BN > 64) prefetch_tensormap(&tmBwide);
+    if (!B_FP4 && p.shared_expert >= 0) prefetch_tensormap(&tmAsh);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, G_TMEM_COLS);
@@ -223,7 +236,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   const int n_tiles = (*p.n_chunks) * p.a_row_tiles;
   const int k_tiles = p.k_tiles;
   const int step = gridDim.x;
-  constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;  // packed bytes of the 256-row A box
+  constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;      // packed bytes of the 256-row A box
+  constexpr uint32_t a_tx_sh = 2 * G_BM * G_BK;       // the shared expert's E4M3 box
+  // the shared expert exists only with FP8 activations (the bf16 profile)
+  auto a_map = [&](const TileInfo& ti) -> const CUtensorMap* { return (!B_FP4 && ti.sh) ? &tmAsh : &tmA; };
+  auto a_bytes = [&](const TileInfo& ti) -> uint32_t { return (!B_FP4 && ti.sh) ? a_tx_sh : a_tx; };
+  auto a_sf = [&](const TileInfo& ti) -> const uint8_t* {
+    return (!B_FP4 && ti.sh) ? p.shared_slot + p.shared_sfa_off
+                             : p.arena + (int64_t)ti.slot * p.slot_bytes + p.sfa_off;
+  };
   // The weights do not depend on the predecessor kernel: the producer puts
   // the first tile's first ring stages of weights and weight scales in
   // flight before it waits; that tile's activations follow after the wait.
@@ -232,13 +253,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const TileInfo first = load_tile(p, blockIdx.x, n_tiles);
     if (first.slot >= 0) {
       const uint64_t pol_w = policy_evict_first();
-      const uint8_t* sf_base = p.arena + (int64_t)first.slot * p.slot_bytes + p.sfa_off;
+      const uint8_t* sf_base = a_sf(first);
       const uint32_t b_tx = (uint32_t)b_rows_for<BN>(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
       pre = k_tiles < C::STAGES ? k_tiles : C::STAGES;
       for (int kt = 0; kt < pre; ++kt) {   // stage kt, first phase: the ring is empty
         uint8_t* st = smem + kt * C::STAGE_BYTES;
-        mbar_expect_tx(&full[kt], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
-        tma_load_5d(st, &tmA, &full[kt], 0, 0, kt, first.mt, first.slot, pol_w);
+        mbar_expect_tx(&full[kt], a_bytes(first) + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+        tma_load_5d(st, a_map(first), &full[kt], 0, 0, kt, first.mt, first.slot, pol_w);
         bulk_load(st + NUM_A * C::A_BYTES + C::B_BYTES,
                   sf_base + ((int64_t)first.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES, &full[kt], pol_w);
       }
@@ -264,7 +285,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           cur = nxt;
           continue;
         }
-        const uint8_t* sf_base = p.arena + (int64_t)cur.slot * p.slot_bytes + p.sfa_off;
+        const uint8_t* sf_base = a_sf(cur);
+        const CUtensorMap* mA = a_map(cur);
+        const uint32_t atx = a_bytes(cur);
         const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
         const int nb = b_rows_for<BN>(cur.nrows);
         const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmBwide));
@@ -281,8 +304,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               break;
             }
             const uint32_t b_tx = (uint32_t)nb * (B_FP4 ? G_BK / 2 : G_BK);
-            mbar_expect_tx(&full[stage], a_tx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
-            tma_load_5d(sA, &tmA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
+            mbar_expect_tx(&full[stage], atx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+            tma_load_5d(sA, mA, &full[stage], 0, 0, kt, cur.mt, cur.slot, pol_w);
             bulk_load(sSFA, sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES,
                       &full[stage], pol_w);
           }
@@ -334,6 +357,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           continue;
         }
         const int nb = b_rows_for<BN>(cur.nrows);
+        const bool a_e4m3 = !B_FP4 && cur.sh;
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
@@ -366,7 +390,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             const uint64_t dA = desc_sw128(aA), dB = desc_sw128(aB);
 #pragma unroll
             for (int kb = 0; kb < G_BK / 32; ++kb) {
-              const uint32_t idesc = idesc_mxf8f6f4(nb, false, (uint32_t)kb);
+              const uint32_t idesc = idesc_mxf8f6f4(nb, false, (uint32_t)kb, a_e4m3);
               const uint32_t sel = (uint32_t)kb << 30;
               const uint32_t acc = (kt | kb) != 0 ? 1u : 0u;
               // +32 bytes of K per step inside the 128-byte swizzle row

@@ -108,12 +108,27 @@ __device__ __forceinline__ int3 block_scan3(int a, int b, int c, int* scratch, i
                    xc - c + (warp > 0 ? scratch[63 + warp] : 0));
 }
 
+// Assignment a = t * topk + j of the layer: the router's pick j of token t
+// for j < k_in; with a shared expert (shared_e >= 0, topk = k_in + 1) the
+// last assignment of every token is the shared expert with weight 1.
+__device__ __forceinline__ int assign_expert(const int32_t* __restrict__ idx, int a, int topk, int k_in,
+                                             int shared_e) {
+  if (shared_e < 0) return idx[a];
+  const int t = a / topk, j = a - t * topk;
+  return j < k_in ? idx[t * k_in + j] : shared_e;
+}
+__device__ __forceinline__ float assign_weight(const float* __restrict__ w, int a, int topk, int k_in, int shared_e) {
+  if (shared_e < 0) return w[a];
+  const int t = a / topk, j = a - t * topk;
+  return j < k_in ? w[t * k_in + j] : 1.0f;
+}
+
 __global__ void __launch_bounds__(AL_THREADS, 1)
     moe_align_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, const float* __restrict__ w_flat,
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                      int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
                      float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
-                     int pad, int* status, const int32_t* __restrict__ n_tokens_dev) {
+                     int pad, int* status, const int32_t* __restrict__ n_tokens_dev, int k_in, int shared_e) {
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
@@ -139,7 +154,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     int e = -1;
     float wv = 0.f;
     if (tid < P) {
-      e = idx[tid];
+      e = assign_expert(idx, tid, topk, k_in, shared_e);
       if (e == -1) {   // an empty assignment (padding of the expert-parallel exchange)
         inv[tid] = -1;
       } else if (e < 0 || e >= E) {
@@ -147,7 +162,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
         inv[tid] = -1;
         e = -1;
       } else if (sorted_w) {
-        wv = w_flat[tid];
+        wv = assign_weight(w_flat, tid, topk, k_in, shared_e);
       }
     }
     __syncthreads();
@@ -220,7 +235,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int p = b0 + r * 32 + lane;
-      ev[r] = p < s1 ? idx[p] : -1;
+      ev[r] = p < s1 ? assign_expert(idx, p, topk, k_in, shared_e) : -1;
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -276,8 +291,8 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int p = b0 + r * 32 + lane;
-      ev[r] = p < s1 ? idx[p] : -1;
-      wv[r] = (p < s1 && sorted_w) ? w_flat[p] : 0.f;
+      ev[r] = p < s1 ? assign_expert(idx, p, topk, k_in, shared_e) : -1;
+      wv[r] = (p < s1 && sorted_w) ? assign_weight(w_flat, p, topk, k_in, shared_e) : 0.f;
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -420,8 +435,11 @@ __global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const 
 // One block per token, eight columns per thread.
 // ---------------------------------------------------------------------------
 // grid (T, H / (8 * blockDim.x)): each CTA covers 8 * blockDim.x columns.
+// `extra` (bf16 [T, H] or null): a row added after the k expert rows (the
+// shared expert's output when it ran as a separate pass, model_npu.py:532).
 __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* __restrict__ inv, int topk, int H,
-                               uint16_t* __restrict__ y, int64_t T, const int32_t* __restrict__ n_tokens_dev) {
+                               uint16_t* __restrict__ y, int64_t T, const int32_t* __restrict__ n_tokens_dev,
+                               const uint16_t* __restrict__ extra) {
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
@@ -440,7 +458,7 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
   }
   // a token without any assignment (every id -1: padding of the expert-
   // parallel exchange) has no output row to write
-  if (k == 0) return;
+  if (k == 0 && !extra) return;
   for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < H; c += gridDim.y * blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     // the rows' loads are issued together (up to 8 in flight), then added
@@ -460,6 +478,15 @@ __global__ void combine_kernel(const uint16_t* __restrict__ out, const int32_t* 
             acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
           }
         }
+      }
+    }
+    if (extra) {
+      const uint4 r = *reinterpret_cast<const uint4*>(extra + t * H + c);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16_from_bits(w[q] & 0xffffu);
+        acc[2 * q + 1] += bf16_from_bits(w[q] >> 16);
       }
     }
     uint32_t o[4];
@@ -536,13 +563,15 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const
 
 struct WsLayout {
   int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
-  int64_t xq, xsf, hq, hsf, out, bytes;
+  int64_t xq, xsf, hq, hsf, out, ys, bytes;
   int64_t p_max, p_cap, max_chunks;
 };
 
 static int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
 
-static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens) {
+// E and topk count the shared expert when the plan has one; `shared`
+// adds the [max_tokens, H] bf16 output of its separate pass (a4w4 profile).
+static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t max_tokens, bool shared = false) {
   WsLayout w;
   w.p_max = max_tokens * topk;
   // every expert group is padded to a multiple of the GEMM tile (64 or 112
@@ -571,6 +600,7 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   w.hq = take(w.p_cap * I);
   w.hsf = take((I / 128) * (w.p_cap / G_BN) * 512);
   w.out = take(2 * w.p_cap * H);
+  w.ys = shared ? take(2 * max_tokens * H) : 0;
   w.bytes = o;
   return w;
 }
@@ -580,7 +610,8 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
 struct dsv4_moe_plan {
   int device = 0;
   int num_sms = 148;
-  int H = 0, I = 0, E = 0, topk = 0;
+  int H = 0, I = 0, E = 0, topk = 0;   // E and topk include the shared expert when the plan has one
+  bool shared = false;                  // expert E - 1 is the shared expert, every token's last assignment
   int64_t max_tokens = 0;
   float swiglu_limit = 0.f;
   uint8_t* arena = nullptr;
@@ -607,10 +638,16 @@ static T* wsp(dsv4_moe_plan* p, int64_t off) {
   return reinterpret_cast<T*>(p->ws + off);
 }
 
+extern "C" int64_t dsv4_moe_workspace_bytes_ex(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                                               int64_t max_tokens, int32_t with_shared) {
+  if (hidden <= 0 || inter <= 0 || n_experts <= 0 || topk <= 0 || max_tokens < 0) return DSV4_EINVAL;
+  const int sh = with_shared ? 1 : 0;
+  return ws_layout(hidden, inter, n_experts + sh, topk + sh, max_tokens, sh).bytes;
+}
+
 extern "C" int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
                                             int64_t max_tokens) {
-  if (hidden <= 0 || inter <= 0 || n_experts <= 0 || topk <= 0 || max_tokens < 0) return DSV4_EINVAL;
-  return ws_layout(hidden, inter, n_experts, topk, max_tokens).bytes;
+  return dsv4_moe_workspace_bytes_ex(hidden, inter, n_experts, topk, max_tokens, 0);
 }
 
 // The shared-memory opt-in is a per-device function attribute: set it for
@@ -647,28 +684,52 @@ static int gemm_bn(int plan_bn, int64_t assignments, int n_experts, bool packed)
 
 template <bool B_FP4, int EPI>
 static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, const CUtensorMap& tmA,
-                               const CUtensorMap* tmB, const GemmParams& g) {
+                               const CUtensorMap* tmB, const CUtensorMap& tmAsh, const GemmParams& g) {
   const dim3 grid(num_sms), block(G_THREADS);
   if (bn == 112)
     return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112>, grid, block, GemmCfg<2, 112, B_FP4>::SMEM_BYTES, st, pdl, tmA,
-                    tmB[0], tmB[1], tmB[2], tmB[3], g);
+                    tmB[0], tmB[1], tmB[2], tmB[3], tmAsh, g);
   return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64, B_FP4>::SMEM_BYTES, st, pdl, tmA,
-                  tmB[0], tmB[1], tmB[2], tmB[2], g);
+                  tmB[0], tmB[1], tmB[2], tmB[2], tmAsh, g);
 }
 
-extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts,
-                                    int32_t topk, int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena,
-                                    int64_t n_slots, void* workspace, int64_t workspace_bytes) {
+// Tensor maps of the shared expert's FP8 slot (w13 and w2 blocks, UINT8,
+// 128-byte swizzle): the same boxes as the packed weights expanded by TMA.
+static int shared_maps(const dsv4_moe_plan* p, const uint8_t* slot, CUtensorMap* m13, CUtensorMap* m2) {
+  const SlotLayout L = shared_slot_layout(p->H, p->I);
+  const uint64_t H = p->H, I = p->I, SB = (uint64_t)L.bytes;
+  const uint32_t box[5] = {G_BK, 2 * G_BM, 1, 1, 1};
+  const CUtensorMapDataType U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  {
+    const uint64_t kt = H / 128, np = I / 128;
+    const uint64_t dims[5] = {128, 256, kt, np, 1}, str[4] = {128, 32768, kt * 32768, SB};
+    if (int rc = make_map(m13, U8, 5, (void*)(slot + L.w13p), dims, str, box, "shared w13")) return rc;
+  }
+  {
+    const uint64_t kt = I / 128, np = H / 256;
+    const uint64_t dims[5] = {128, 256, kt, np, 1}, str[4] = {128, 32768, kt * 32768, SB};
+    if (int rc = make_map(m2, U8, 5, (void*)(slot + L.w2p), dims, str, box, "shared w2")) return rc;
+  }
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_moe_plan_create_ex(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts,
+                                       int32_t topk, int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena,
+                                       int64_t n_slots, void* workspace, int64_t workspace_bytes,
+                                       int32_t with_shared) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(out && slot_arena && workspace, "null pointer");
   DSV4_CHECK_ARG(hidden > 0 && inter > 0 && hidden % 256 == 0 && inter % 128 == 0,
                  "hidden must be a positive multiple of 256 and inter of 128");
-  DSV4_CHECK_ARG(n_experts > 0 && n_experts <= 1024, "n_experts must be in [1, 1024]");
-  DSV4_CHECK_ARG(topk > 0 && topk <= 16, "topk must be in [1, 16]");
+  const int sh = with_shared ? 1 : 0;
+  DSV4_CHECK_ARG(n_experts > 0 && n_experts + sh <= 1024, "n_experts must be in [1, 1024]");
+  DSV4_CHECK_ARG(topk > 0 && topk + sh <= 16, "topk must be in [1, 16]");
   DSV4_CHECK_ARG(max_tokens > 0 && n_slots > 0, "max_tokens and n_slots must be positive");
   DSV4_CHECK_ARG(((uintptr_t)slot_arena % 256) == 0 && ((uintptr_t)workspace % 256) == 0,
                  "slot arena and workspace must be 256-byte aligned");
-  const WsLayout wl = ws_layout(hidden, inter, n_experts, topk, max_tokens);
+  n_experts += sh;
+  topk += sh;
+  const WsLayout wl = ws_layout(hidden, inter, n_experts, topk, max_tokens, sh);
   DSV4_CHECK_ARG(workspace_bytes >= wl.bytes, "workspace too small");
   std::unique_ptr<dsv4_moe_plan> p(new dsv4_moe_plan());
   int rc0 = bind_device_of(slot_arena, &p->device);
@@ -678,6 +739,7 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   p->I = inter;
   p->E = n_experts;
   p->topk = topk;
+  p->shared = sh != 0;
   p->max_tokens = max_tokens;
   p->swiglu_limit = swiglu_limit;
   p->arena = slot_arena;
@@ -741,25 +803,38 @@ extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t
   DSV4_API_END
 }
 
+extern "C" int dsv4_moe_plan_create(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts,
+                                    int32_t topk, int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena,
+                                    int64_t n_slots, void* workspace, int64_t workspace_bytes) {
+  return dsv4_moe_plan_create_ex(out, hidden, inter, n_experts, topk, max_tokens, swiglu_limit, slot_arena, n_slots,
+                                 workspace, workspace_bytes, 0);
+}
+
 extern "C" int dsv4_moe_plan_destroy(dsv4_moe_plan* plan) {
   delete plan;
   return DSV4_OK;
 }
 
-static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
-                            const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
-                            const int32_t* slot_of_expert, void* y_bf16, void* stream) {
-  DSV4_API_BEGIN
-  DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert, "null pointer");
-  DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
-  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= p->max_tokens, "n_tokens exceeds the plan's max_tokens");
-  DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)y_bf16 % 16) == 0, "x and y must be 16-byte aligned");
-  if (n_tokens == 0) return DSV4_OK;
-  DSV4_CUDA_CHECK(cudaSetDevice(p->device));
-  cudaStream_t st = (cudaStream_t)stream;
+// One pass of the layer over `n_tokens` tokens with `topk` assignments each
+// (the router's k_in picks, plus the shared expert `shared_e` as the last one
+// when shared_e >= 0): align, activation quant + gather, the two GEMMs and
+// the combine into y (skipped when y is null), `extra` added last.
+struct PassArgs {
+  bool fp4;
+  int topk, k_in, shared_e;
+  const CUtensorMap* sh13;   // shared expert maps (with shared_e >= 0)
+  const CUtensorMap* sh2;
+  const uint8_t* shared_slot;
+  const uint16_t* extra;
+  bool timed;                // records the stage events
+};
+
+static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int64_t n_tokens,
+                    const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
+                    const int32_t* slot_of_expert, void* y_bf16, cudaStream_t st) {
   const WsLayout& w = p->wl;
-  const int P = (int)(n_tokens * p->topk);
-  const int bn = gemm_bn(p->gemm_tile, P, p->E, profile == DSV4_PROFILE_A4W4);   // GEMM tile = group padding
+  const int P = (int)(n_tokens * a.topk);
+  const int bn = gemm_bn(p->gemm_tile, P, p->E, a.fp4);   // GEMM tile = group padding
   int* status = wsp<int>(p, w.status);
   int32_t* sorted_flat = wsp<int32_t>(p, w.sorted_flat);
   int32_t* inv = wsp<int32_t>(p, w.inv);
@@ -767,25 +842,24 @@ static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf1
   int* n_chunks = wsp<int>(p, w.n_chunks);
   const size_t al_smem = (size_t)(2 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 4;
   auto mark = [&](int i) {
-    if (p->timing) cudaEventRecord(p->ev[i], st);
+    if (p->timing && a.timed) cudaEventRecord(p->ev[i], st);
   };
   // events between stages break the programmatic overlap: no PDL while timing
   const bool pdl = pdl_enabled() && !p->timing;
   mark(0);
-  DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, p->topk,
+  DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, a.topk,
                            p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets), sorted_flat,
                            inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                           wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev));
+                           wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e));
   mark(1);
-  const bool fp4 = profile == DSV4_PROFILE_A4W4;
   const int64_t rb_cap = (w.p_cap + bn - 1) / bn;   // BN-row scale blocks per k-tile
   {
     const int64_t warps = n_tokens * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
-    DSV4_CUDA_CHECK(launch_k(fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
+    DSV4_CUDA_CHECK(launch_k(a.fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
                              dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, n_tokens,
-                             p->topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf, n_tokens_dev));
+                             a.topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf, n_tokens_dev));
   }
   mark(2);
   GemmParams g1{};
@@ -807,8 +881,13 @@ static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf1
   g1.out_ld = p->I;
   g1.swiglu_limit = p->swiglu_limit;
   g1.status = status;
+  g1.shared_expert = a.shared_e;
+  g1.shared_slot = a.shared_slot;
+  const SlotLayout sl = shared_slot_layout(p->H, p->I);
+  g1.shared_sfa_off = sl.sf13;
   GemmParams g2 = g1;
   g2.sfa_off = p->slot.sf2;
+  g2.shared_sfa_off = sl.sf2;
   g2.k_tiles = p->I / 128;
   g2.a_row_tiles = p->H / 256;   // two 128-row tiles of w2 per work tile
   g2.out_tile_cols = 256;
@@ -817,24 +896,78 @@ static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf1
   g2.out_sf = nullptr;
   g2.out_bf16 = wsp<uint16_t>(p, w.out);
   g2.out_ld = p->H;
-  if (fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13p, p->tmB1_fp4, g1)));
+  // without a shared expert the kernels never read the shared maps; any
+  // valid map fills the parameter
+  const CUtensorMap& sh13 = a.sh13 ? *a.sh13 : p->tmA13;
+  const CUtensorMap& sh2 = a.sh2 ? *a.sh2 : p->tmA2;
+  if (a.fp4)
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13p, p->tmB1_fp4, sh13, g1)));
   else
-    DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp8, g1)));
+    DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp8, sh13, g1)));
   mark(3);
-  if (fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2p, p->tmB2_fp4, g2)));
+  if (a.fp4)
+    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2p, p->tmB2_fp4, sh2, g2)));
   else
-    DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, g2)));
+    DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, sh2, g2)));
   mark(4);
   if (y_bf16) {
     const int threads = std::min(128, p->H / 8);
     const unsigned gy = (unsigned)std::max(1, p->H / (8 * threads));
     DSV4_CUDA_CHECK(launch_k(combine_kernel, dim3((unsigned)n_tokens, gy), dim3(threads), 0, st, pdl,
-                             (const uint16_t*)wsp<uint16_t>(p, w.out), (const int32_t*)inv, p->topk, p->H,
-                             (uint16_t*)y_bf16, (int64_t)n_tokens, n_tokens_dev));
+                             (const uint16_t*)wsp<uint16_t>(p, w.out), (const int32_t*)inv, a.topk, p->H,
+                             (uint16_t*)y_bf16, (int64_t)n_tokens, n_tokens_dev, a.extra));
   }
   mark(5);
+  return DSV4_OK;
+}
+
+static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                            const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
+                            const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert, "null pointer");
+  DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= p->max_tokens, "n_tokens exceeds the plan's max_tokens");
+  DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)y_bf16 % 16) == 0, "x and y must be 16-byte aligned");
+  DSV4_CHECK_ARG(p->shared == (shared_slot != nullptr),
+                 "a plan created with a shared expert needs its FP8 slot, and only such a plan takes one");
+  DSV4_CHECK_ARG(((uintptr_t)shared_slot % 256) == 0, "the shared expert's slot must be 256-byte aligned");
+  if (n_tokens == 0) return DSV4_OK;
+  DSV4_CUDA_CHECK(cudaSetDevice(p->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool fp4 = profile == DSV4_PROFILE_A4W4;
+  if (!p->shared) {
+    const PassArgs a{fp4, p->topk, p->topk, -1, nullptr, nullptr, nullptr, nullptr, true};
+    if (int rc = moe_pass(p, a, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
+                          y_bf16, st))
+      return rc;
+  } else {
+    CUtensorMap m13, m2;
+    if (int rc = shared_maps(p, shared_slot, &m13, &m2)) return rc;
+    const int k = p->topk - 1, shared_e = p->E - 1;
+    if (!fp4) {
+      // bf16 profile: the shared expert is one more assignment of every token
+      // in the same launches (FP8 weights, FP8 activations)
+      const PassArgs a{false, p->topk, k, shared_e, &m13, &m2, shared_slot, nullptr, true};
+      if (int rc = moe_pass(p, a, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
+                            y_bf16, st))
+        return rc;
+    } else {
+      // a4w4: the routed GEMMs read packed E2M1 activations, the shared
+      // expert FP8 ones, so it runs first as its own pass into ys, which the
+      // routed pass's combine adds after the routed rows
+      DSV4_CHECK_ARG(y_bf16, "the a4w4 profile with a shared expert needs y");
+      uint16_t* ys = wsp<uint16_t>(p, p->wl.ys);
+      const PassArgs s1{false, 1, 0, shared_e, &m13, &m2, shared_slot, nullptr, false};
+      if (int rc = moe_pass(p, s1, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert, ys,
+                            st))
+        return rc;
+      const PassArgs s2{true, k, k, -1, nullptr, nullptr, nullptr, ys, true};
+      if (int rc = moe_pass(p, s2, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
+                            y_bf16, st))
+        return rc;
+    }
+  }
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
@@ -844,7 +977,16 @@ extern "C" int dsv4_moe_forward(dsv4_moe_plan* p, int32_t profile, const void* x
                                 const int32_t* slot_of_expert, void* y_bf16, void* stream) {
   if (!y_bf16) return fail(DSV4_EINVAL, "dsv4_moe_forward: null pointer");
   return moe_forward_impl(p, profile, x_bf16, n_tokens, nullptr, route_weights, route_indices, slot_of_expert,
-                          y_bf16, stream);
+                          nullptr, y_bf16, stream);
+}
+
+extern "C" int dsv4_moe_forward_shared(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                                       const float* route_weights, const int32_t* route_indices,
+                                       const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16,
+                                       void* stream) {
+  if (!y_bf16 || !shared_slot) return fail(DSV4_EINVAL, "dsv4_moe_forward_shared: null pointer");
+  return moe_forward_impl(p, profile, x_bf16, n_tokens, nullptr, route_weights, route_indices, slot_of_expert,
+                          shared_slot, y_bf16, stream);
 }
 
 extern "C" int dsv4_moe_forward_rows(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t max_tokens,
@@ -852,7 +994,7 @@ extern "C" int dsv4_moe_forward_rows(dsv4_moe_plan* p, int32_t profile, const vo
                                      const int32_t* route_indices, const int32_t* slot_of_expert, void* y_bf16,
                                      void* stream) {
   return moe_forward_impl(p, profile, x_bf16, max_tokens, n_tokens_dev, route_weights, route_indices,
-                          slot_of_expert, y_bf16, stream);
+                          slot_of_expert, nullptr, y_bf16, stream);
 }
 
 extern "C" int dsv4_moe_output_rows(dsv4_moe_plan* p, void** rows_bf16, int32_t** inv) {
@@ -935,7 +1077,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
       indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-      nullptr, nullptr, nullptr, 1, status, nullptr);
+      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

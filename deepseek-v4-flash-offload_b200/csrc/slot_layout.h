@@ -37,4 +37,11 @@ DSV4_HD int64_t sf_pair_offset(int64_t R, int64_t kb, int64_t K) {
   return ((R / 256) * (K / 128) + kb / 4) * 1024 + ((R % 256) / 128) * 512 + (r % 32) * 16 + (r / 32) * 4 + kb % 4;
 }
 
+// FP8 (E4M3) slot of the shared expert: the same pairs, blocks and scale
+// atoms, one byte per element, so a block is 256 rows x 128 B = 32 KiB and
+// lands in shared memory exactly like an expanded E2M1 block.
+DSV4_HD int64_t w8_pair_offset(int64_t R, int64_t k, int64_t K) {
+  return ((R / 256) * (K / 128) + k / 128) * 32768 + (R % 256) * 128 + k % 128;
+}
+
 }  // namespace dsv4

@@ -51,6 +51,12 @@ SIGNATURES = {
     "dsv4_moe_forward": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p]),
     "dsv4_moe_forward_rows": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_output_rows": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p)]),
+    "dsv4_shared_slot_bytes": (_i64, [_i32, _i32]),
+    "dsv4_pack_shared_host": (C.c_int, [_p, _p, _p, _p, _p, _p, _i32, _i32, _p]),
+    "dsv4_moe_workspace_bytes_ex": (_i64, [_i32, _i32, _i32, _i32, _i64, _i32]),
+    "dsv4_moe_plan_create_ex": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i32, _i64, _f32, _p, _i64, _p, _i64,
+                                          _i32]),
+    "dsv4_moe_forward_shared": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_status": (C.c_int, [_p, _p]),
     "dsv4_moe_enable_timing": (C.c_int, [_p, _i32]),
     "dsv4_moe_set_gemm_tile": (C.c_int, [_p, _i32]),

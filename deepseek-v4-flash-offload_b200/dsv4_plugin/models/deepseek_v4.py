@@ -9,7 +9,10 @@ Same surface as the reference plugin (dsv4_plugin/models/deepseek_v4.py):
   * ``install_patches()``: idempotent swap of ``DeepseekV4MoE`` and
     ``load_weights`` in the target vLLM module;
   * module flag ``_MXFP4_GMM`` (env ``DSV4_MXFP4_GMM=1``) selects the a4w4
-    profile, else bf16.
+    profile, else bf16;
+  * the shared expert: its FP8 weights are teed into the engine at load and
+    ``forward`` runs it inside the routed launches (``DSV4_FUSED_SHARED=0``
+    keeps the vLLM dense MLP added afterwards, as the reference does).
 The patch target is the first importable module of ``DSV4_PATCH_MODULE``
 (comma separated; default: vLLM's CUDA DeepSeek-V4 model module, then the
 vllm-ascend one the reference patches).
@@ -27,10 +30,14 @@ import torch
 from torch import nn
 
 from dsv4_plugin import ops
-from dsv4_plugin.core.engine import get_engine, is_expert_weight
+from dsv4_plugin.core.engine import get_engine, is_expert_weight, is_shared_expert_weight
 
 _PATCHED = False
 _MXFP4_GMM = os.environ.get("DSV4_MXFP4_GMM", "0") == "1"
+# DSV4_FUSED_SHARED=0: the shared expert stays the vLLM dense MLP added after
+# the routed output (the reference's structure); by default its FP8 weights
+# are captured at load and it runs inside the routed launches
+_FUSED_SHARED = os.environ.get("DSV4_FUSED_SHARED", "1") != "0"
 DEFAULT_TARGETS = ("vllm.model_executor.models.deepseek_v4", "vllm_ascend.models.deepseek_v4")
 
 
@@ -181,12 +188,13 @@ class OffloadDeepseekV4MoE(nn.Module):
             x.record_stream(side)
         bank.prefetch(self.layer_idx + 1, lambda: nxt._route(hs, input_ids, out=(pw, pi), workspace=ws)[1])
 
-    def _routed_experts(self, hs, weights, indices, profile, input_ids=None):
+    def _routed_experts(self, hs, weights, indices, profile, input_ids=None, shared_slot=None):
         slot_of, slots = self._slot_table(indices)
         if slots is None and self.engine.bank._dir is not None:
             self._prefetch_next(hs, input_ids)
-        plan = self.engine.plan_for(self.n_routed_experts, self.topk, hs.shape[0], self.swiglu_limit or 0.0)
-        y = plan.forward(hs, weights, indices, slot_of, profile)
+        plan = self.engine.plan_for(self.n_routed_experts, self.topk, hs.shape[0], self.swiglu_limit or 0.0,
+                                    with_shared=shared_slot is not None)
+        y = plan.forward(hs, weights, indices, slot_of, profile, shared_slot=shared_slot)
         if slots is not None and not torch.cuda.is_current_stream_capturing():
             self.engine.bank.mark_used(slots)
         return y
@@ -200,6 +208,13 @@ class OffloadDeepseekV4MoE(nn.Module):
         weights, indices = self._route(hs, input_ids)
         return self._routed_experts(hs, weights, indices, "a4w4", input_ids)
 
+    def _shared_slot(self):
+        """The layer's shared expert as an FP8 slot for the fused launches, or
+        None (no shared expert, not captured, or DSV4_FUSED_SHARED=0)."""
+        if not _FUSED_SHARED or self.n_shared_experts in (None, 0):
+            return None
+        return self.engine.shared_slot(self.layer_idx)
+
     def forward(self, hidden_states: torch.Tensor, input_ids=None) -> torch.Tensor:
         num_tokens, hidden_dim = hidden_states.shape
         hs = hidden_states.view(-1, hidden_dim)
@@ -211,9 +226,18 @@ class OffloadDeepseekV4MoE(nn.Module):
             hs = v4.sequence_parallel_chunk(hs)
             if input_ids is not None:
                 input_ids = v4.sequence_parallel_chunk(input_ids)
-        out = self._routed(hs, input_ids)
-        if self.shared_experts is not None:
-            out = out + self.shared_experts(hs)
+        sh = self._shared_slot()
+        if sh is not None:
+            # routed experts + shared expert in one pass: the shared expert is
+            # every token's last assignment, added in fp32 before the one bf16
+            # rounding (model_npu.py:531-533)
+            weights, indices = self._route(hs, input_ids)
+            out = self._routed_experts(hs, weights, indices, "a4w4" if _MXFP4_GMM else "bf16", input_ids,
+                                       shared_slot=sh)
+        else:
+            out = self._routed(hs, input_ids)
+            if self.shared_experts is not None:
+                out = out + self.shared_experts(hs)
         if self.is_sequence_parallel:
             out = v4.tensor_model_parallel_all_gather(out, 0)[:num_tokens]
         return out.view(num_tokens, hidden_dim)
@@ -222,7 +246,8 @@ class OffloadDeepseekV4MoE(nn.Module):
 def _offload_load_weights(self, weights):
     """Weight-stream tee (deepseek_v4.py:272-288): main-layer routed experts
     go to the engine's host pool, everything else (MTP experts included) to
-    the original ``load_weights``."""
+    the original ``load_weights``.  Shared-expert tensors are also copied into
+    the engine (for the fused launches) and still passed on."""
     engine = get_engine()
     it = iter(weights)
 
@@ -231,6 +256,8 @@ def _offload_load_weights(self, weights):
             if is_expert_weight(name):
                 engine.capture(name, w)
             else:
+                if _FUSED_SHARED and is_shared_expert_weight(name):
+                    engine.capture_shared(name, w)
                 yield name, w
 
     return _ORIG_LOAD_WEIGHTS(self, filtered())

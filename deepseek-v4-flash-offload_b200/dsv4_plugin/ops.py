@@ -189,6 +189,31 @@ def pack_expert(w1p, w1s, w2p, w2s, w3p, w3s, hidden: int, inter: int, out=None)
     return out
 
 
+def shared_slot_bytes(hidden: int, inter: int) -> int:
+    n = lib().dsv4_shared_slot_bytes(hidden, inter)
+    if n < 0:
+        check(int(n))
+    return int(n)
+
+
+def pack_shared_expert(w1, s1, w2, s2, w3, s3, hidden: int, inter: int, out=None) -> torch.Tensor:
+    """Pack the shared expert's FP8 checkpoint tensors (w1 / w3 [I, H], w2
+    [H, I] E4M3 bytes; s* [ceil(N/128), ceil(K/128)] E8M0 bytes; host) into
+    its FP8 slot (host uint8 tensor)."""
+    ts = [t.detach().contiguous().view(torch.uint8) if t.dtype != torch.uint8 else t.detach().contiguous()
+          for t in (w1, s1, w2, s2, w3, s3)]
+    for t in ts:
+        if t.is_cuda:
+            raise ValueError("pack_shared_expert packs host tensors")
+    nb = shared_slot_bytes(hidden, inter)
+    if out is None:
+        out = torch.empty(nb, dtype=torch.uint8)
+    if out.is_cuda or out.numel() < nb or not out.is_contiguous():
+        raise ValueError("out must be a contiguous host uint8 buffer of at least the slot size")
+    check(lib().dsv4_pack_shared_host(*[t.data_ptr() for t in ts], hidden, inter, out.data_ptr()))
+    return out
+
+
 def unpack_expert(slot: torch.Tensor, hidden: int, inter: int) -> dict:
     """Inverse of ``pack_expert`` (host tensors) -> six checkpoint tensors."""
     s = slot.detach().cpu().contiguous()
@@ -219,28 +244,33 @@ class MoEPlan:
     layer on the current stream."""
 
     def __init__(self, hidden: int, inter: int, n_experts: int, topk: int, max_tokens: int,
-                 swiglu_limit: float, arena: torch.Tensor):
+                 swiglu_limit: float, arena: torch.Tensor, with_shared: bool = False):
         _need_cuda(arena)
         if arena.dtype != torch.uint8 or not arena.is_contiguous() or arena.dim() != 2:
             raise TypeError("arena must be a contiguous uint8 CUDA tensor [n_slots, slot_bytes]")
         if arena.shape[1] != expert_slot_bytes(hidden, inter):
             raise ValueError("arena row size must equal the expert slot size")
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
+        self.with_shared = bool(with_shared)
         self.max_tokens = int(max_tokens)
         self.arena = arena
         self.device = arena.device
-        nb = lib().dsv4_moe_workspace_bytes(hidden, inter, n_experts, topk, self.max_tokens)
+        sh = int(self.with_shared)
+        nb = lib().dsv4_moe_workspace_bytes_ex(hidden, inter, n_experts, topk, self.max_tokens, sh)
         if nb < 0:
             check(int(nb))
         self.workspace = torch.empty(int(nb), dtype=torch.uint8, device=self.device)
         h = C.c_void_p()
-        check(lib().dsv4_moe_plan_create(C.byref(h), hidden, inter, n_experts, topk, self.max_tokens,
-                                         float(swiglu_limit), arena.data_ptr(), arena.shape[0],
-                                         self.workspace.data_ptr(), int(nb)))
+        check(lib().dsv4_moe_plan_create_ex(C.byref(h), hidden, inter, n_experts, topk, self.max_tokens,
+                                            float(swiglu_limit), arena.data_ptr(), arena.shape[0],
+                                            self.workspace.data_ptr(), int(nb), sh))
         self._h = h
 
     def forward(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, slot_of: torch.Tensor,
-                profile: str = "bf16", out: torch.Tensor | None = None) -> torch.Tensor:
+                profile: str = "bf16", out: torch.Tensor | None = None,
+                shared_slot: torch.Tensor | None = None) -> torch.Tensor:
+        """Routed experts (plus the shared expert, whose FP8 slot a plan made
+        ``with_shared`` takes) of the [T, H] bf16 tokens -> [T, H] bf16."""
         _need_cuda(x, weights, indices, slot_of)
         x = x.contiguous()
         if x.dtype != torch.bfloat16:
@@ -255,6 +285,13 @@ class MoEPlan:
             raise ValueError("slot_of needs one entry per expert")
         if out is None:
             out = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=x.device)
+        if self.with_shared:
+            if shared_slot is None or not shared_slot.is_cuda or shared_slot.dtype != torch.uint8:
+                raise ValueError("this plan runs the shared expert: pass its FP8 slot (uint8 CUDA tensor)")
+            check(lib().dsv4_moe_forward_shared(self._h, PROFILES[profile], x.data_ptr(), t, w.data_ptr(),
+                                                idx.data_ptr(), so.data_ptr(), shared_slot.data_ptr(), out.data_ptr(),
+                                                _stream(x.device)))
+            return out
         check(lib().dsv4_moe_forward(self._h, PROFILES[profile], x.data_ptr(), t, w.data_ptr(), idx.data_ptr(),
                                      so.data_ptr(), out.data_ptr(), _stream(x.device)))
         return out

@@ -63,6 +63,25 @@ def make_expert(cfg: MoEConfig, seed: int, eid: int, layer: int = 0) -> dict:
     return out
 
 
+def make_shared_expert(cfg: MoEConfig, seed: int, layer: int = 0) -> dict:
+    """The shared expert of a layer in the checkpoint's FP8 form: w1 / w3
+    [I, H] and w2 [H, I] E4M3 bytes (sign random, exponent field 0..8 and
+    any mantissa: |v| <= 3.75, no NaN codes) with one E8M0 scale byte per
+    128 x 128 block, uniform in [118, 126] (``w1s`` [ceil(I/128),
+    ceil(H/128)] ...).  The shared intermediate size is ``inter`` (one
+    shared expert)."""
+    h, i = cfg.hidden, cfg.inter
+    g = _rng(seed, 4000 + layer)
+    out = {}
+    for w, (n, k) in (("w1", (i, h)), ("w2", (h, i)), ("w3", (i, h))):
+        sign = g.integers(0, 2, size=(n, k), dtype=np.uint8) << 7
+        expo = g.integers(0, 9, size=(n, k), dtype=np.uint8) << 3
+        mant = g.integers(0, 8, size=(n, k), dtype=np.uint8)
+        out[w] = (sign | expo | mant).astype(np.uint8)
+        out[w + "s"] = g.integers(118, 127, size=((n + 127) // 128, (k + 127) // 128), dtype=np.uint8)
+    return out
+
+
 def bf16_exact(a: np.ndarray) -> np.ndarray:
     """Round float32 to bf16 (RNE) and return float32 holding the bf16 value."""
     a = np.ascontiguousarray(a, dtype=np.float32)

@@ -186,6 +186,32 @@ int dsv4_moe_forward_rows(dsv4_moe_plan* plan, int32_t profile, const void* x_bf
 /* Device pointers of the last forward's per-assignment output rows (bf16
  * [rows, hidden], sorted by expert) and of inv (int32 [n_tokens * topk]). */
 int dsv4_moe_output_rows(dsv4_moe_plan* plan, void** rows_bf16, int32_t** inv);
+/* ------------------------------------------------------------------------ *
+ * Shared expert fused into the routed launches (the reference runs it as a
+ * separate dense MLP, deepseek_v4.py:87-100 and 264-265; its math is
+ * model_npu.py Expert in "fp8" mode and MoE.forward's
+ * `y = y + self.shared_experts(x)`, model_npu.py:532).  Weights: w1 / w3
+ * [I, H] and w2 [H, I] E4M3 with one E8M0 scale per 128 x 128 block
+ * (dequant_fp8_weight, npu_ops.py:161-167), packed once into an FP8 slot of
+ * dsv4_shared_slot_bytes (same pairs, blocks and scale atoms as the routed
+ * slot, one byte per element).  A plan made with with_shared = 1 treats the
+ * shared expert as one more assignment of every token (expert id n_experts,
+ * weight 1, last in the combine, so the fp32 sum adds it after the routed
+ * rows before the one bf16 rounding, as model_npu does): in the bf16 profile
+ * inside the same launches; in the a4w4 profile (packed E2M1 activations for
+ * the routed GEMMs) as a first pass of its own whose output the routed
+ * combine adds last.  route_weights / route_indices stay [T, k]. */
+int64_t dsv4_shared_slot_bytes(int32_t hidden, int32_t inter);
+int dsv4_pack_shared_host(const uint8_t* w1, const uint8_t* s1, const uint8_t* w2, const uint8_t* s2,
+                          const uint8_t* w3, const uint8_t* s3, int32_t hidden, int32_t inter, uint8_t* slot_out);
+int64_t dsv4_moe_workspace_bytes_ex(int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                                    int64_t max_tokens, int32_t with_shared);
+int dsv4_moe_plan_create_ex(dsv4_moe_plan** out, int32_t hidden, int32_t inter, int32_t n_experts, int32_t topk,
+                            int64_t max_tokens, float swiglu_limit, uint8_t* slot_arena, int64_t n_slots,
+                            void* workspace, int64_t workspace_bytes, int32_t with_shared);
+int dsv4_moe_forward_shared(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t n_tokens,
+                            const float* route_weights, const int32_t* route_indices,
+                            const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16, void* stream);
 /* Synchronises `stream`, returns the plan's device status word (0 or a
  * DSV4_E* code recorded by a kernel) and clears it. */
 int dsv4_moe_status(dsv4_moe_plan* plan, void* stream);

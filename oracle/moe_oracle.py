@@ -298,6 +298,45 @@ def _swiglu(gate, up, w, limit):
     return (silu(gate) * up * w).astype(np.float32)
 
 
+def e4m3_value(b: np.ndarray) -> np.ndarray:
+    """E4M3 (fn) byte -> float32, exact: sign, 4-bit exponent (bias 7), 3-bit
+    mantissa, subnormals at exponent 0; 0x7F / 0xFF are NaN."""
+    b = b.astype(np.uint32)
+    e = ((b >> 3) & 15).astype(np.int32)
+    m = (b & 7).astype(np.float32)
+    v = np.where(e == 0, np.ldexp(m / np.float32(8.0), -6),
+                 np.ldexp(np.float32(1.0) + m / np.float32(8.0), e - 7)).astype(np.float32)
+    v = np.where((b & 0x7F) == 0x7F, np.float32(np.nan), v)
+    return np.where(b & 0x80, -v, v).astype(np.float32)
+
+
+def dequant_fp8_weight(w: np.ndarray, scale: np.ndarray, block: int = 128) -> np.ndarray:
+    """[N, K] E4M3 bytes * E8M0 scale per 128 x 128 block -> float32
+    (npu_ops.py:161-167); exact in bf16 for the scales used here."""
+    n, k = w.shape
+    s = e8m0_to_f32(scale.view(np.uint8))
+    s = np.repeat(np.repeat(s, block, axis=0)[:n], block, axis=1)[:, :k]
+    return (e4m3_value(w) * s).astype(np.float32)
+
+
+def shared_weights_f32(sh: dict) -> dict:
+    """Dequantised shared expert {"w1", "w2", "w3"} (model_npu.Linear in "fp8"
+    mode holds dequant_fp8_weight(...) as bf16, model_npu.py:94-117)."""
+    return {w: dequant_fp8_weight(sh[w], sh[w + "s"]) for w in ("w1", "w2", "w3")}
+
+
+def shared_expert(x: np.ndarray, wd: dict, swiglu_limit: float = 10.0) -> np.ndarray:
+    """model_npu.Expert.forward in "fp8" mode (model_npu.py:469-491): every
+    Linear FP8-round-trips its input (act_quant per 128), the bf16 GEMM
+    outputs are rounded to bf16, SwiGLU with the clamp and no route weight,
+    bf16(h) round-tripped again, bf16 output [T, H]."""
+    xq = act_quant_rt(x)
+    gate = bf16_round(xq @ wd["w1"].T)
+    up = bf16_round(xq @ wd["w3"].T)
+    h = bf16_round(_swiglu(gate, up, np.float32(1.0), swiglu_limit))
+    return bf16_round(act_quant_rt(h) @ wd["w2"].T)
+
+
 def expert_weights_f32(expert: dict) -> dict:
     """Dequantise one expert's six packed tensors (offload.py:77-84)."""
     return {w: dequant_fp4_weight(expert[w + "p"], expert[w + "s"]) for w in ("w1", "w2", "w3")}
@@ -305,7 +344,8 @@ def expert_weights_f32(expert: dict) -> dict:
 
 def moe_routed(x: np.ndarray, weights: np.ndarray, indices: np.ndarray,
                experts, n_experts: int, swiglu_limit: float = 10.0,
-               profile: str = "bf16", deq_cache: dict | None = None) -> np.ndarray:
+               profile: str = "bf16", deq_cache: dict | None = None,
+               shared: dict | None = None) -> np.ndarray:
     """Routed-expert output [T, H] (bf16-exact float32) for one layer.
 
     ``experts[e]`` is a dict of the six packed tensors
@@ -315,7 +355,9 @@ def moe_routed(x: np.ndarray, weights: np.ndarray, indices: np.ndarray,
     times the route weight, FP8 round trip of bf16(h), down GEMM rounded to
     bf16, float32 ``index_add_`` in ascending expert order, cast to bf16.
     Profile ``a4w4`` follows deepseek_v4.py:199-245 with the MXFP4
-    activation quantisation of ``mx_quant_fp4``.
+    activation quantisation of ``mx_quant_fp4``.  With ``shared`` (the
+    dequantised shared expert) its output is added in fp32 after the routed
+    rows, as model_npu.MoE.forward does.
     """
     t, h = x.shape
     al = moe_align(indices, n_experts)
@@ -345,6 +387,11 @@ def moe_routed(x: np.ndarray, weights: np.ndarray, indices: np.ndarray,
         out = bf16_round(hq @ wd["w2"].T)
         # index_add_ in sorted order: per token, experts ascend
         np.add.at(y, rows, out)
+    if shared is not None:
+        # MoE.forward: y = y + self.shared_experts(x) in fp32, then one
+        # rounding to bf16 (model_npu.py:532-533); ``shared`` holds the
+        # dequantised weights (shared_weights_f32)
+        y = y + shared_expert(x, shared, swiglu_limit)
     return bf16_round(y)
 
 

@@ -17,7 +17,8 @@ shims, and writes small ``.npz`` fixtures beside this script:
     plugin's data flow, not the closed NPU op's rounding).
 
 ``--only route_cfg1`` writes just the config-1 routing fixture
-(``route_cfg1.npz``) and leaves the others as they are.
+(``route_cfg1.npz``), ``--only shared_cfg0`` just the shared-expert fixture
+(``shared_cfg0.npz``), and leave the others as they are.
 
 Large inputs (expert weights) are not stored: they come from the seeded
 generator in ``dsv4_plugin/synthetic.py`` and the fixture stores their
@@ -177,10 +178,34 @@ def make_route_cfg1(DV4, S):
     np.savez_compressed(os.path.join(HERE, "route_cfg1.npz"), **out)
 
 
+def make_shared_cfg0(O, MN, S):
+    """shared_cfg0.npz: the reference's shared expert (model_npu.Expert in
+    "fp8" mode: weights from npu_ops.dequant_fp8_weight, as its loader sets
+    them) on config-0 dims, and the dequant of the FP8 weights themselves.
+    The FP8 bytes come from synthetic.make_shared_expert (SHA-256 stored)."""
+    cfg = S.CFG0
+    sh = S.make_shared_expert(cfg, 0, 3)
+    x = S.make_tokens(cfg, 5, 16)
+    ex = MN.Expert(cfg.hidden, cfg.inter, mode="fp8", swiglu_limit=cfg.swiglu_limit)
+    for w in ("w1", "w2", "w3"):
+        deq = O.dequant_fp8_weight(torch.from_numpy(sh[w]).view(torch.float8_e4m3fn),
+                                   torch.from_numpy(sh[w + "s"]).view(torch.float8_e8m0fnu), 128, torch.bfloat16)
+        getattr(ex, w).weight.data.copy_(deq)
+    with torch.no_grad():
+        y = ex(from_f32_bf16(x))
+    out = {"x": bf16_bits(from_f32_bf16(x)), "y": bf16_bits(y),
+           "sha": np.frombuffer(bytes.fromhex(_sha(*[sh[k] for k in sorted(sh)])), dtype=np.uint8)}
+    for w in ("w1", "w2"):
+        deq = O.dequant_fp8_weight(torch.from_numpy(sh[w]).view(torch.float8_e4m3fn),
+                                   torch.from_numpy(sh[w + "s"]).view(torch.float8_e8m0fnu), 128, torch.bfloat16)
+        out[f"deq_{w}"] = bf16_bits(deq)
+    np.savez_compressed(os.path.join(HERE, "shared_cfg0.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["route_cfg1"], default=None,
+    ap.add_argument("--only", choices=["route_cfg1", "shared_cfg0"], default=None,
                     help="write only this fixture (the others stay as they are)")
     args = ap.parse_args()
     os.environ["DSV4_PIN_HOST"] = "0"
@@ -198,6 +223,10 @@ def main():
     if args.only == "route_cfg1":
         make_route_cfg1(DV4, S)
         print("wrote route_cfg1.npz to", HERE)
+        return
+    if args.only == "shared_cfg0":
+        make_shared_cfg0(O, MN, S)
+        print("wrote shared_cfg0.npz to", HERE)
         return
 
     # ---------------------------------------------------------------- ops

@@ -50,10 +50,11 @@ class SyntheticLayer:
 
 
 def make_plugin_layer(cfg: S.MoEConfig, experts: dict, device, layer_idx: int = 3, seed: int = 0,
-                      slots: int | None = None):
+                      slots: int | None = None, shared: dict | None = None):
     """OffloadDeepseekV4MoE for a synthetic layer built through the plugin's
     public API, with ``experts`` {eid: six tensors} registered in a fresh
-    engine (which becomes the process-wide one)."""
+    engine (which becomes the process-wide one), and with ``shared`` (the
+    FP8 shared expert of synthetic.make_shared_expert) fused in."""
     import types
 
     from dsv4_plugin.core import engine as ENG
@@ -64,9 +65,12 @@ def make_plugin_layer(cfg: S.MoEConfig, experts: dict, device, layer_idx: int = 
     for e, ex in experts.items():
         eng.bank.register(layer_idx, e, *[torch.from_numpy(ex[k]) for k in
                                           ("w1p", "w1s", "w2p", "w2s", "w3p", "w3s")])
+    if shared is not None:
+        eng.register_shared(layer_idx, *[torch.from_numpy(shared[k]) for k in ("w1", "w1s", "w2", "w2s", "w3", "w3s")])
     ENG.reset_engine(eng)
     hf = types.SimpleNamespace(
-        n_routed_experts=cfg.n_experts, n_shared_experts=None, num_experts_per_tok=cfg.topk,
+        n_routed_experts=cfg.n_experts, n_shared_experts=1 if shared is not None else None,
+        num_experts_per_tok=cfg.topk,
         norm_topk_prob=cfg.renormalize, scoring_func=cfg.score_func, routed_scaling_factor=cfg.route_scale,
         swiglu_limit=cfg.swiglu_limit, num_hash_layers=0, vocab_size=1000, hidden_size=cfg.hidden,
         moe_intermediate_size=cfg.inter, hidden_act="silu")

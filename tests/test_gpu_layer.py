@@ -217,3 +217,67 @@ def test_device_lru_prefetch_spares_the_batch_in_flight(dev):
     host = arena.cpu()
     for s, key in enumerate(skeys.tolist()):
         assert key >= 0 and torch.equal(host[s], pool[key])
+
+
+@pytest.mark.parametrize("T,tile", [(1, 0), (16, 0), (200, 64), (200, 112)])
+def test_shared_expert_fused_matches_oracle(dev, T, tile):
+    """The shared expert inside the routed launches (config-0 dims, FP8
+    weights with 128 x 128 block scales): bf16 profile in the same GEMMs,
+    a4w4 as a pass of its own added by the combine.  Against the oracle's
+    model_npu.MoE.forward (routed rows in fp32, then + shared, one bf16
+    rounding).  T=200 gives the shared expert several row chunks."""
+    from dsv4_plugin import ops
+    from helpers import SyntheticLayer
+    L = SyntheticLayer(S.CFG0, seed=0)
+    c = L.cfg
+    sh = S.make_shared_expert(c, 0, 3)
+    slot = ops.pack_shared_expert(*[torch.from_numpy(sh[k]) for k in ("w1", "w1s", "w2", "w2s", "w3", "w3s")],
+                                  c.hidden, c.inter).to(dev)
+    shw = O.shared_weights_f32(sh)
+    x = S.make_tokens(c, 60 + T, T)
+    w, idx = O.route(x, L.gate_w, np.zeros(L.n, np.float32), c.topk, "softmax", False)
+    plan = ops.MoEPlan(c.hidden, c.inter, L.n, c.topk, T, c.swiglu_limit, L.arena, with_shared=True)
+    plan.set_gemm_tile(tile)
+    for profile in ("bf16", "a4w4"):
+        y = plan.forward(bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(),
+                         L.slot_of, profile, shared_slot=slot)
+        plan.status()
+        ref = O.moe_routed(x, w, idx, L.experts, L.n, c.swiglu_limit, profile, deq_cache=L.deq_cache, shared=shw)
+        assert rel_err(bf16_to_np(y), ref) <= TOL, profile
+    # the routed part alone is unchanged by the fusion
+    y0 = ops.MoEPlan(c.hidden, c.inter, L.n, c.topk, T, c.swiglu_limit, L.arena).forward(
+        bf16_tensor(x), torch.from_numpy(w).cuda(), torch.from_numpy(idx.astype(np.int32)).cuda(), L.slot_of)
+    ref0 = O.moe_routed(x, w, idx, L.experts, L.n, c.swiglu_limit, "bf16", deq_cache=L.deq_cache)
+    assert rel_err(bf16_to_np(y0), ref0) <= TOL
+
+
+def test_plugin_forward_with_shared_expert_cfg1(dev):
+    """OffloadDeepseekV4MoE.forward at config 1 (T=64) with the shared expert
+    registered in the engine: routed + shared in one pass, both profiles,
+    against the oracle; ``_routed`` stays the routed part alone."""
+    cfg = S.CFG1
+    T = 64
+    x = S.make_tokens(cfg, 23, T)
+    w, idx = _route_oracle(cfg, x)
+    need = sorted(set(idx.reshape(-1).tolist()))
+    experts = {e: S.make_expert(cfg, 0, e, LAYER) for e in need}
+    sh = S.make_shared_expert(cfg, 0, LAYER)
+    moe, eng = make_plugin_layer(cfg, experts, dev, layer_idx=LAYER, shared=sh)
+    shw = O.shared_weights_f32(sh)
+    xt = bf16_tensor(x)
+    deq = {}
+    try:
+        for flag, profile in ((False, "bf16"), (True, "a4w4")):
+            _profile(flag)
+            y = moe.forward(xt)
+            torch.cuda.synchronize()
+            ref = O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, profile, deq_cache=deq,
+                               shared=shw)
+            assert rel_err(bf16_to_np(y), ref) <= TOL, profile
+        _profile(False)
+        yr = moe._routed(xt)
+        torch.cuda.synchronize()
+        ref = O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, "bf16", deq_cache=deq)
+        assert rel_err(bf16_to_np(yr), ref) <= TOL
+    finally:
+        _profile(False)

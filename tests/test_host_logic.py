@@ -167,9 +167,18 @@ def test_install_patches_and_load_weights_tee(monkeypatch):
     for n in ("mtp.0.ffn.experts.3.w1.weight", "model.layers.0.ffn.gate.weight", "model.embed.weight"):
         stream.append((n, torch.zeros(1)))
         expect_pass.append(n)
+    # the shared expert of layer 4 (FP8): teed into the engine and passed on
+    from dsv4_plugin import synthetic as S
+    sh = S.make_shared_expert(S.MoEConfig("t", 256, 128, 8, 2, "softmax", False), 2, 4)
+    for w in ("w1", "w2", "w3"):
+        for kind, key in (("weight", w), ("scale", w + "s")):
+            n = f"model.layers.4.ffn.shared_experts.{w}.{kind}"
+            stream.append((n, torch.from_numpy(sh[key])))
+            expect_pass.append(n)
     got = mod.DeepseekV4ForCausalLM().load_weights(iter(stream))
     assert got == set(expect_pass)
     assert eng.captured == 6 and eng.stats()["parked"] == 0
+    assert eng.shared_slot(4) is not None and eng.shared_slot(0) is None
     ENG.reset_engine(None)
 
 
@@ -223,3 +232,26 @@ def test_gate_split_terms_sum_to_the_gate_exactly():
     assert np.array_equal(lo, r2)
     assert np.array_equal(hi.astype(np.float64) + mid.astype(np.float64) + lo.astype(np.float64),
                           w.astype(np.float64))
+
+
+def test_engine_captures_the_shared_expert_from_the_weight_stream():
+    """Shared-expert tensors in the checkpoint's names are parsed, parked and
+    packed into the FP8 slot once all six arrived (on the CPU here)."""
+    from dsv4_plugin import ops
+    from dsv4_plugin.core.engine import ExpertOffloadEngine, is_shared_expert_weight, parse_shared_name
+    from dsv4_plugin import synthetic as S
+    assert parse_shared_name("model.layers.7.ffn.shared_experts.w2.scale") == (7, "w2", "scale")
+    assert not is_shared_expert_weight("layers.7.ffn.experts.3.w2.scale")
+    assert not is_shared_expert_weight("layers.7.ffn.shared_experts.w2.bias")
+    cfg = S.CFG0
+    sh = S.make_shared_expert(cfg, 1, 7)
+    eng = ExpertOffloadEngine(slot_capacity=1, device="cpu")
+    names = [(f"layers.7.ffn.shared_experts.{w}.{kind}", sh[w + ("" if kind == "weight" else "s")])
+             for w in ("w1", "w2", "w3") for kind in ("weight", "scale")]
+    for j, (n, t) in enumerate(names):
+        assert eng.capture_shared(n, torch.from_numpy(t))
+        assert (eng.shared_slot(7) is None) == (j < 5)
+    ref = ops.pack_shared_expert(*[torch.from_numpy(sh[k]) for k in ("w1", "w1s", "w2", "w2s", "w3", "w3s")],
+                                 cfg.hidden, cfg.inter)
+    assert torch.equal(eng.shared_slot(7), ref)
+    assert ref.numel() == ops.shared_slot_bytes(cfg.hidden, cfg.inter) == 3 * cfg.hidden * cfg.inter * 33 // 32

@@ -201,3 +201,25 @@ def test_lru_model_matches_reference_bank():
     assert [len(m0.keys()), m0.misses] == g["s0_stats"].tolist()
     # ExpertBank.get returns the dequantised bf16 expert
     assert np.array_equal(O.bf16_bits(O.dequant_fp4_weight(g["get_w1_src"], g["get_w1s_src"])), g["get_w1"])
+
+
+def test_shared_expert_matches_reference():
+    """The shared expert (model_npu.Expert in "fp8" mode, weights from
+    npu_ops.dequant_fp8_weight) run by the reference on the CPU
+    (shared_cfg0.npz): the oracle's FP8 dequant is bit-exact and its output
+    equals the reference's to bf16 rounding of a float32 BLAS sum."""
+    import hashlib
+    g = _load("shared_cfg0.npz")
+    cfg = S.CFG0
+    sh = S.make_shared_expert(cfg, 0, 3)
+    h = hashlib.sha256()
+    for k in sorted(sh):
+        h.update(np.ascontiguousarray(sh[k]).tobytes())
+    assert h.digest() == g["sha"].tobytes(), "synthetic generator drifted from the fixture"
+    for w in ("w1", "w2"):
+        assert np.array_equal(O.bf16_bits(O.dequant_fp8_weight(sh[w], sh[w + "s"])), g[f"deq_{w}"])
+    x = _bf16(g["x"])
+    y = O.shared_expert(x, O.shared_weights_f32(sh), cfg.swiglu_limit)
+    ref = _bf16(g["y"])
+    assert _rel(y, ref) <= 1e-2
+    assert np.mean(y == ref) > 0.9
