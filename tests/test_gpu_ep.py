@@ -168,3 +168,63 @@ def test_ep_world4_equals_single_gpu(scattered):
     out = mgr.dict()
     mp.spawn(_run, args=(4, _port(), 40, out, scattered), nprocs=4, join=True)
     assert all(out.values()) and len(out) == 24
+
+
+def _run_timeout(rank, world, port, out):
+    """Rank 1 leaves between steps (it makes no further exchange calls); rank
+    0's next dispatch waits for flags that nothing sets, runs out after the
+    bounded wait and reports DSV4_ETIMEOUT; its stream finishes and the
+    context stays usable.  Both ranks then destroy their handles."""
+    import sys
+    import time
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, root, os.path.join(root, "deepseek-v4-flash-offload_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from datetime import timedelta
+
+    from dsv4_plugin._lib import DSV4_ETIMEOUT, Dsv4Error
+    from dsv4_plugin.parallel_ep import P2PExchange
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+    try:
+        n_experts, tokens, topk, hidden = 16, 8, 4, 256
+        g = torch.Generator().manual_seed(rank)
+        x = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16).to(dev)
+        idx = torch.stack([torch.randperm(n_experts, generator=g)[:topk] for _ in range(tokens)]).to(torch.int32)
+        w = torch.rand(tokens, topk, generator=g).to(dev)
+        ex = P2PExchange(n_experts, rank, world, tokens, topk, hidden, dev)
+        ex.dispatch(x, w, idx.to(dev))
+        ex.give_back(ex.recv_x)          # identity expert: every received row goes back as is
+        ex.check_status()
+        out[(rank, "step1")] = True
+        dist.barrier()
+        if rank == 0:
+            t0 = time.time()
+            ex.dispatch(x, w, idx.to(dev))
+            ex.give_back(ex.recv_x)
+            try:
+                ex.check_status()
+                out[(rank, "timeout")] = False
+            except Dsv4Error as err:
+                out[(rank, "timeout")] = err.code == DSV4_ETIMEOUT
+            out[(rank, "seconds")] = time.time() - t0
+            torch.zeros(1, device=dev).add_(1).item()   # the context still runs work
+        dist.barrier()
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_peer_wait_times_out_when_a_rank_leaves():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_run_timeout, args=(2, _port(), out), nprocs=2, join=True)
+    assert out[(0, "step1")] and out[(1, "step1")]
+    assert out[(0, "timeout")]
+    assert out[(0, "seconds")] < 30.0
