@@ -1114,7 +1114,11 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
         plan = epm.plan if epm is not None else eng.plan_for(_cfg().n_experts, _cfg().topk, T, _cfg().swiglu_limit)
         load = [float(plan.n_active())]
         if epm is not None:
-            load.append(float(int(epm._p2p[T].n_recv.item())) if exchange == "p2p" else 0.0)
+            ex = epm._p2p.get(T) if exchange == "p2p" else None
+            # tokens and assignments this rank received
+            load.append(float(int(ex.n_recv.item())) if ex is not None else 0.0)
+            n_tok = int(ex.n_recv.item()) if ex is not None else 0
+            load.append(float(int((ex.recv_idx[:n_tok] >= 0).sum().item())) if ex is not None else 0.0)
         loads = [load]
         if world > 1:
             buf = torch.tensor(load, dtype=torch.float64, device=device)
@@ -1127,7 +1131,8 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
                         "step_ms_median": round(statistics.median(ms), 5),
                         "segments_ms_max_over_ranks": seg,
                         "active_experts_per_rank": [int(l[0]) for l in loads],
-                        "rows_received_per_rank": [int(l[1]) for l in loads] if world > 1 else None}
+                        "tokens_received_per_rank": [int(l[1]) for l in loads] if world > 1 else None,
+                        "assignments_received_per_rank": [int(l[2]) for l in loads] if world > 1 else None}
         del g
         torch.cuda.synchronize(device)
     if epm is not None:

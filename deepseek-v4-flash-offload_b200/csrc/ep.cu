@@ -171,45 +171,52 @@ extern "C" int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weig
 namespace dsv4 {
 
 // ---------------------------------------------------------------------------
-// Exchange over NVLink peer memory (CUDA IPC), with exact per-peer counts.
-// Each rank owns one device block that its peers write into:
-//   recv_x [world*cap, H] bf16, recv_e [world*cap] int32, recv_w [world*cap]
-//     fp32, recv_src [world*cap] int2 (source rank, source slot): the rows
-//     dispatched to this rank, COMPACT: source s fills rows
-//     off[s] .. off[s] + n[s->me), off[s] = sum over s' < s of n[s'->me];
-//   back [world*cap, H] bf16: expert outputs of this rank's assignments,
-//     owner d fills rows d*cap + r (r = rank of the assignment among this
-//     rank's assignments to d);
-//   cnt [world][world] int32: row s = the per-destination counts of source s;
+// Exchange over NVLink peer memory (CUDA IPC): exact per-peer counts, and
+// each token crosses once per destination rank, however many of its k
+// experts live there.  Each rank owns one device block that its peers write
+// into (T = the token capacity per source, k = top-k):
+//   recv_x [world*T, H] bf16: the tokens dispatched to this rank, COMPACT:
+//     source s fills rows off[s] .. off[s] + n[s->me), off[s] = the sum over
+//     s' < s of n[s'->me];
+//   recv_idx / recv_w [world*T, k]: each received token's k picks with the
+//     experts of other ranks set to -1 (weight 0), recv_src [world*T] int2
+//     (source rank, token index at the source);
+//   back [T*k, H] bf16: expert outputs of this rank's own assignments; the
+//     owner of assignment a = t*k + j writes row a;
+//   cnt [world][world] int32: row s = the per-destination token counts of s;
 //   flags [3][world]: per source, the epoch of its published counts, rows
-//     and returned rows; ctrl: epoch, arrival counters, rows received.
-// A step: (1) one CTA ranks the assignments per destination (stable), writes
-// its count row into every peer's cnt and publishes; (2) a wait for every
-// source's counts; (3) the rows, straight into the owners' blocks at their
-// compact offsets, then "rows published"; (4) a wait for every source's rows,
-// which also sums the received count (the layer's device-side token count);
-// after the layer (5) each received row goes back to its source's `back`,
-// read from the layer's sorted output rows through inv, and (6) a wait.
-// Publishing is a system-scope release of the epoch after the writes are
-// fenced; waiting is an acquire, bounded (DSV4_ETIMEOUT in *status).  A peer
-// writes into this rank's block for step e+1 only after it received this
-// rank's step-e return, which this rank sends after consuming step e, so one
-// buffer set suffices.  After a timeout the step's data are undefined and a
-// late peer may still write: the handle must be destroyed and recreated.
+//     and returned rows; ctrl: epoch, arrival counters, tokens received;
+//   pos [T][world] int32 (local): the compact index of (token, destination).
+// A step: (1) one CTA finds, per destination, the tokens with at least one
+// expert there and their stable rank, writes its count row into every
+// peer's cnt and publishes; (2) a wait for every source's counts; (3) each
+// (token, destination) row, its masked picks and its source into the owner's
+// block, then "rows published"; (4) a wait for every source's rows, which
+// also sums the received count (the layer's device-side token count); after
+// the layer (top-k over the received tokens, foreign experts -1) (5) every
+// assignment's output goes back to its source's `back`, read from the
+// layer's sorted output rows through inv, and (6) a wait.  Publishing is a
+// system-scope release of the epoch after the writes are fenced; waiting is
+// an acquire, bounded (DSV4_ETIMEOUT in *status).  A peer writes into this
+// rank's block for step e+1 only after it received this rank's step-e
+// return, which this rank sends after consuming step e, so one buffer set
+// suffices.  After a timeout the step's data are undefined and a late peer
+// may still write: the handle must be destroyed and created again.
 // ---------------------------------------------------------------------------
 struct EpBlock {
-  int64_t off_back, off_e, off_w, off_src, off_cnt, off_flags, off_ctrl, bytes;
+  int64_t off_back, off_idx, off_w, off_src, off_cnt, off_pos, off_flags, off_ctrl, bytes;
 };
-static EpBlock ep_block(int world, int64_t cap, int hidden) {
+static EpBlock ep_block(int world, int64_t tokens, int topk, int hidden) {
   auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
   EpBlock b;
-  const int64_t rows = (int64_t)world * cap;
+  const int64_t rows = (int64_t)world * tokens;
   b.off_back = al(rows * hidden * 2);
-  b.off_e = b.off_back + al(rows * hidden * 2);
-  b.off_w = b.off_e + al(rows * 4);
-  b.off_src = b.off_w + al(rows * 4);
+  b.off_idx = b.off_back + al(tokens * topk * hidden * 2);
+  b.off_w = b.off_idx + al(rows * topk * 4);
+  b.off_src = b.off_w + al(rows * topk * 4);
   b.off_cnt = b.off_src + al(rows * 8);
-  b.off_flags = b.off_cnt + al((int64_t)world * world * 4);
+  b.off_pos = b.off_cnt + al((int64_t)world * world * 4);
+  b.off_flags = b.off_pos + al(tokens * world * 4);
   b.off_ctrl = b.off_flags + al(3 * (int64_t)world * 4);
   b.bytes = b.off_ctrl + 256;
   return b;
@@ -230,79 +237,83 @@ __device__ __forceinline__ int ep_dest(int e, int e_loc, const int32_t* __restri
   return owner ? owner[e] : e / e_loc;
 }
 
-// One CTA: epoch += 1, each assignment's destination slot d*cap + r (stable
-// rank among this rank's assignments to d), the combine order, then this
-// rank's count row into every peer's cnt, fenced and published.
+// One CTA: epoch += 1; per destination, the tokens with an expert there and
+// their stable rank among them (pos[t][d], or -1); the combine order of each
+// token's assignments (ascending expert id); this rank's count row into
+// every peer's cnt, fenced and published.
 __global__ void __launch_bounds__(EP_THREADS, 1)
-    ep_p2p_index_kernel(const int32_t* __restrict__ idx, int64_t P, int topk, int E, int e_loc,
-                        const int32_t* __restrict__ owner, int world, int my_rank, int64_t cap,
-                        uint8_t* const* __restrict__ peers, int64_t off_cnt, int64_t off_flags,
-                        uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos, int32_t* __restrict__ ordered,
-                        int* __restrict__ status) {
+    ep_p2p_index_kernel(const int32_t* __restrict__ idx, int64_t T, int topk, int E, int e_loc,
+                        const int32_t* __restrict__ owner, int world, int my_rank, uint8_t* const* __restrict__ peers,
+                        int64_t off_cnt, int64_t off_flags, uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos,
+                        int32_t* __restrict__ ordered, int* __restrict__ status) {
   __shared__ int wc[32][EP_MAX_WORLD];
   __shared__ int base[EP_MAX_WORLD];
   __shared__ int round_tot[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned lt = (1u << lane) - 1u;
   if (tid == 0) ctrl[EPC_EPOCH] = ctrl[EPC_EPOCH] + 1u;   // this step's epoch
   if (tid < world) base[tid] = 0;
-  for (int64_t r0 = 0; r0 < P; r0 += EP_THREADS) {
-    for (int i = tid; i < 32 * EP_MAX_WORLD; i += EP_THREADS) (&wc[0][0])[i] = 0;
-    __syncthreads();
-    const int64_t a = r0 + tid;
-    int d = -1;
-    if (a < P) {
-      const int e = idx[a];
-      if (e >= 0 && e < E) {
-        d = ep_dest(e, e_loc, owner);
-        if (d < 0 || d >= world) {
+  for (int64_t t0 = 0; t0 < T; t0 += EP_THREADS) {
+    const int64_t t = t0 + tid;
+    unsigned long long mask = 0ull;   // destinations of this token
+    if (t < T) {
+      for (int j = 0; j < topk; ++j) {
+        const int e = idx[t * topk + j];
+        if (e >= 0 && e < E) {
+          const int d = ep_dest(e, e_loc, owner);
+          if (d >= 0 && d < world)
+            mask |= 1ull << d;
+          else
+            set_status(status, DSV4_EINVAL);
+        } else if (e != -1) {
           set_status(status, DSV4_EINVAL);
-          d = -1;
         }
-      } else if (e != -1) {
-        set_status(status, DSV4_EINVAL);
       }
     }
-    const unsigned same = __match_any_sync(0xffffffffu, d);
-    const int rank = __popc(same & ((1u << lane) - 1u));
-    if (d >= 0 && rank == 0) wc[warp][d] = __popc(same);
+    for (int d = 0; d < world; ++d) {
+      const unsigned bal = __ballot_sync(0xffffffffu, (mask >> d) & 1ull);
+      if (lane == 0) wc[warp][d] = __popc(bal);
+    }
     __syncthreads();
-    if (tid < world) {
-      int s = 0;
+    if (tid < world) {   // exclusive prefix over the warps, per destination
+      int sum = 0;
       for (int v = 0; v < 32; ++v) {
         const int c = wc[v][tid];
-        wc[v][tid] = s;
-        s += c;
+        wc[v][tid] = sum;
+        sum += c;
       }
-      round_tot[tid] = s;
+      round_tot[tid] = sum;
     }
     __syncthreads();
-    if (d >= 0)
-      pos[a] = (int32_t)((int64_t)d * cap + base[d] + wc[warp][d] + rank);
-    else if (a < P)
-      pos[a] = -1;
+    for (int d = 0; d < world; ++d) {
+      const bool on = (mask >> d) & 1ull;
+      const unsigned bal = __ballot_sync(0xffffffffu, on);
+      if (t < T) pos[t * world + d] = on ? base[d] + wc[warp][d] + __popc(bal & lt) : -1;
+    }
     __syncthreads();
     if (tid < world) base[tid] += round_tot[tid];
     __syncthreads();
   }
-  for (int64_t t = tid; t < P / topk; t += EP_THREADS) {
-    int ke[16], kp[16];
+  for (int64_t t = tid; t < T; t += EP_THREADS) {
+    int ke[16], ka[16];
     int n = 0;
     for (int j = 0; j < topk; ++j) {
       const int e = idx[t * topk + j];
-      const int p = pos[t * topk + j];
-      if (p < 0) continue;
+      if (e < 0 || e >= E) continue;
+      const int d = ep_dest(e, e_loc, owner);
+      if (d < 0 || d >= world) continue;
       int i = n++;
       while (i > 0 && ke[i - 1] > e) {
         ke[i] = ke[i - 1];
-        kp[i] = kp[i - 1];
+        ka[i] = ka[i - 1];
         --i;
       }
       ke[i] = e;
-      kp[i] = p;
+      ka[i] = (int)(t * topk + j);
     }
-    for (int j = 0; j < topk; ++j) ordered[t * topk + j] = j < n ? kp[j] : -1;
+    for (int j = 0; j < topk; ++j) ordered[t * topk + j] = j < n ? ka[j] : -1;
   }
   // this rank's counts into row my_rank of every peer's count matrix
   for (int i = tid; i < world * world; i += EP_THREADS) {
@@ -336,14 +347,16 @@ __device__ __forceinline__ void ep_publish(uint32_t* __restrict__ ctrl, int coun
   }
 }
 
-// One warp per assignment: the token's row, expert, weight and return slot
-// into the owner's block at the compact row off[my_rank -> d] + r.  The
+// One warp per (token, destination) with an expert there: the token's row,
+// its picks with the other ranks' experts set to -1 (weight 0) and its
+// source into the owner's block at the compact row off[d] + pos[t][d].  The
 // offsets come from this rank's copy of the count matrix (every source wrote
 // its row before the wait that precedes this kernel).
 __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
-                                   const float* __restrict__ w, const int32_t* __restrict__ pos, int64_t P, int topk,
-                                   int H, int world, int my_rank, int64_t cap, uint8_t* const* __restrict__ peers,
-                                   EpBlock blk, const int32_t* __restrict__ cnt, uint32_t* __restrict__ ctrl) {
+                                   const float* __restrict__ w, const int32_t* __restrict__ pos, int64_t T, int topk,
+                                   int H, int E, int e_loc, const int32_t* __restrict__ owner, int world, int my_rank,
+                                   uint8_t* const* __restrict__ peers, EpBlock blk, const int32_t* __restrict__ cnt,
+                                   uint32_t* __restrict__ ctrl) {
   __shared__ int64_t off[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
@@ -356,43 +369,49 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t a = warp0; a < P; a += nwarps) {
-    const int p = pos[a];
+  for (int64_t pr = warp0; pr < T * world; pr += nwarps) {
+    const int p = pos[pr];
     if (p < 0) continue;
-    const int d = (int)(p / cap);
-    const int64_t r = p - (int64_t)d * cap;
-    const int64_t row = off[d] + r;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (a / topk) * H);
+    const int64_t t = pr / world;
+    const int d = (int)(pr - t * world);
+    const int64_t row = off[d] + p;
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
     uint4* dst = reinterpret_cast<uint4*>(peers[d]) + row * (H / 8);
     for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
-    if (lane == 0) {
-      reinterpret_cast<int32_t*>(peers[d] + blk.off_e)[row] = idx[a];
-      reinterpret_cast<float*>(peers[d] + blk.off_w)[row] = w[a];
-      reinterpret_cast<int2*>(peers[d] + blk.off_src)[row] = make_int2(my_rank, (int)r);
+    if (lane < topk) {
+      const int e = idx[t * topk + lane];
+      const bool mine = e >= 0 && e < E && ep_dest(e, e_loc, owner) == d;
+      reinterpret_cast<int32_t*>(peers[d] + blk.off_idx)[row * topk + lane] = mine ? e : -1;
+      reinterpret_cast<float*>(peers[d] + blk.off_w)[row * topk + lane] = mine ? w[t * topk + lane] : 0.f;
     }
+    if (lane == 0) reinterpret_cast<int2*>(peers[d] + blk.off_src)[row] = make_int2(my_rank, (int)t);
   }
   ep_publish(ctrl, EPC_ROWS, peers, world, blk.off_flags, 1 * world + my_rank);
 }
 
-// One warp per received row j < n_recv: its expert output (row inv[j] of the
-// layer's sorted output, or row j of y when inv is null) back into the
-// source's `back` at my_rank*cap + r.
+// One warp per (received token j < n_recv, pick s) with an expert of this
+// rank: its output (row inv[j*k + s] of the layer's sorted output, or row
+// j*k + s of y when inv is null) into the source's `back` row t*k + s.
 __global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ inv,
-                                     const int2* __restrict__ src_of, const uint32_t* __restrict__ n_recv, int world,
-                                     int my_rank, int64_t cap, int H, uint8_t* const* __restrict__ peers,
-                                     int64_t off_back, int64_t off_flags, uint32_t* __restrict__ ctrl) {
+                                     const int32_t* __restrict__ recv_idx, const int2* __restrict__ src_of,
+                                     const uint32_t* __restrict__ n_recv, int world, int my_rank, int64_t T, int topk,
+                                     int H, uint8_t* const* __restrict__ peers, int64_t off_back, int64_t off_flags,
+                                     uint32_t* __restrict__ ctrl) {
   griddep_wait();
   griddep_launch();
   const int lane = threadIdx.x & 31;
-  const int64_t n = (int64_t)*reinterpret_cast<const volatile uint32_t*>(n_recv);
+  const int64_t n = (int64_t)*reinterpret_cast<const volatile uint32_t*>(n_recv) * topk;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t j = warp0; j < n; j += nwarps) {
-    const int2 sr = src_of[j];
-    if (sr.x < 0 || sr.x >= world || sr.y < 0 || sr.y >= cap) continue;   // not written this step (after a timeout)
-    const int64_t from_row = inv ? (int64_t)inv[j] : j;
+  for (int64_t a = warp0; a < n; a += nwarps) {
+    if (recv_idx[a] < 0) continue;
+    const int64_t j = a / topk;
+    const int s = (int)(a - j * topk);
+    const int2 st = src_of[j];
+    if (st.x < 0 || st.x >= world || st.y < 0 || st.y >= T) continue;   // not written this step (after a timeout)
+    const int64_t from_row = inv ? (int64_t)inv[a] : a;
     const uint4* from = reinterpret_cast<const uint4*>(y + from_row * H);
-    uint4* dst = reinterpret_cast<uint4*>(peers[sr.x] + off_back) + ((int64_t)my_rank * cap + sr.y) * (H / 8);
+    uint4* dst = reinterpret_cast<uint4*>(peers[st.x] + off_back) + ((int64_t)st.y * topk + s) * (H / 8);
     for (int c = lane; c < H / 8; c += 32) dst[c] = from[c];
   }
   ep_publish(ctrl, EPC_BACK, peers, world, off_flags, 2 * world + my_rank);
@@ -400,7 +419,7 @@ __global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y, const int32
 
 // One thread: wait (bounded) until every source has published this step's
 // epoch in flags[first .. first+world).  With `cnt`, also writes the number
-// of rows this rank receives (column my_rank of the count matrix) to *n_recv.
+// of tokens this rank receives (column my_rank of the count matrix) to *n_recv.
 __global__ void ep_p2p_wait_kernel(const uint32_t* __restrict__ flags, const uint32_t* __restrict__ ctrl, int world,
                                    int* __restrict__ status, const int32_t* __restrict__ cnt, int my_rank,
                                    uint32_t* __restrict__ n_recv) {
@@ -428,8 +447,8 @@ __global__ void ep_p2p_wait_kernel(const uint32_t* __restrict__ flags, const uin
 }  // namespace dsv4
 
 struct dsv4_ep {
-  int rank = 0, world = 1, device = 0, hidden = 0;
-  int64_t cap = 0;
+  int rank = 0, world = 1, device = 0, hidden = 0, topk = 0;
+  int64_t tokens = 0;   // token capacity per source
   dsv4::EpBlock blk{};
   uint8_t* base = nullptr;
   uint8_t** peers_dev = nullptr;
@@ -453,22 +472,25 @@ int ep_check(dsv4_ep* ep) {
 }  // namespace
 }  // namespace dsv4
 
-extern "C" int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t cap_rows,
-                              int32_t hidden, void* ipc_handle_out) {
+extern "C" int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t max_tokens,
+                              int32_t topk, int32_t hidden, void* ipc_handle_out) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(out && ipc_handle_out, "null pointer");
   DSV4_CHECK_ARG(world > 0 && world <= EP_MAX_WORLD && rank >= 0 && rank < world, "rank/world out of range");
-  DSV4_CHECK_ARG(cap_rows > 0 && hidden > 0 && hidden % 8 == 0, "bad capacity / hidden");
+  DSV4_CHECK_ARG(max_tokens > 0 && max_tokens < (1LL << 30) && topk > 0 && topk <= 16 && hidden > 0 &&
+                     hidden % 8 == 0,
+                 "bad capacity / topk / hidden");
   std::unique_ptr<dsv4_ep> ep(new dsv4_ep);
   ep->device = device;
   DSV4_CUDA_CHECK(cudaSetDevice(device));
   ep->rank = rank;
   ep->world = world;
-  ep->cap = cap_rows;
+  ep->tokens = max_tokens;
+  ep->topk = topk;
   ep->hidden = hidden;
-  ep->blk = ep_block(world, cap_rows, hidden);
+  ep->blk = ep_block(world, max_tokens, topk, hidden);
   DSV4_CUDA_CHECK(cudaMalloc(&ep->base, (size_t)ep->blk.bytes));
-  DSV4_CUDA_CHECK(cudaMemset(ep->base + ep->blk.off_e, 0, (size_t)(ep->blk.bytes - ep->blk.off_e)));
+  DSV4_CUDA_CHECK(cudaMemset(ep->base + ep->blk.off_idx, 0, (size_t)(ep->blk.bytes - ep->blk.off_idx)));
   cudaIpcMemHandle_t h;
   DSV4_CUDA_CHECK(cudaIpcGetMemHandle(&h, ep->base));
   memcpy(ipc_handle_out, &h, sizeof(h));
@@ -501,57 +523,58 @@ extern "C" int dsv4_ep_connect(dsv4_ep* ep, const void* handles) {
   DSV4_API_END
 }
 
-extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_expert, float** recv_weight,
+extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_indices, float** recv_weights,
                                int32_t** n_recv, void** back) {
   DSV4_API_BEGIN
-  DSV4_CHECK_ARG(ep && recv_x && recv_expert && recv_weight && n_recv && back, "null pointer");
+  DSV4_CHECK_ARG(ep && recv_x && recv_indices && recv_weights && n_recv && back, "null pointer");
   *recv_x = ep->base;
   *back = ep->base + ep->blk.off_back;
-  *recv_expert = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_e);
-  *recv_weight = reinterpret_cast<float*>(ep->base + ep->blk.off_w);
+  *recv_indices = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_idx);
+  *recv_weights = reinterpret_cast<float*>(ep->base + ep->blk.off_w);
   *n_recv = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_ctrl) + EPC_NRECV;
   DSV4_API_END
 }
 
 extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights,
-                                const int32_t* route_indices, int64_t n_tokens, int32_t topk, int32_t n_experts,
-                                const int32_t* expert_owner, int32_t* slot_of_assignment, int32_t* ordered_slots,
-                                int* status, void* stream) {
+                                const int32_t* route_indices, int64_t n_tokens, int32_t n_experts,
+                                const int32_t* expert_owner, int32_t* ordered_assignments, int* status,
+                                void* stream) {
   DSV4_API_BEGIN
   if (int rc = ep_check(ep)) return rc;
-  DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && slot_of_assignment && ordered_slots && status,
-                 "null pointer");
-  DSV4_CHECK_ARG(topk > 0 && topk <= 16 && n_tokens >= 0 && n_tokens * topk <= ep->cap,
-                 "n_tokens * topk must be in [0, capacity] and topk in [1, 16]");
+  DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && ordered_assignments && status, "null pointer");
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= ep->tokens, "n_tokens must be in [0, the handle's max_tokens]");
   DSV4_CHECK_ARG(n_experts > 0 && (expert_owner || n_experts % ep->world == 0),
                  "n_experts must divide over the ranks (or pass expert_owner)");
   DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0, "rows must be 16-byte aligned");
   DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
-  const int64_t P = n_tokens * topk;
+  const int64_t T = n_tokens;
+  const int k = ep->topk;
   uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(ep->base + ep->blk.off_flags);
   const int32_t* cnt = reinterpret_cast<const int32_t*>(ep->base + ep->blk.off_cnt);
+  int32_t* pos = reinterpret_cast<int32_t*>(ep->base + ep->blk.off_pos);
   uint8_t* const* peers = (uint8_t* const*)ep->peers_dev;
-  DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, P, (int)topk,
-                           (int)n_experts, (int)(n_experts / ep->world), expert_owner, ep->world, ep->rank, ep->cap,
-                           peers, ep->blk.off_cnt, ep->blk.off_flags, ctrl, slot_of_assignment, ordered_slots,
-                           status));
+  const int e_loc = (int)(n_experts / ep->world);
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, T, k,
+                           (int)n_experts, e_loc, expert_owner, ep->world, ep->rank, peers, ep->blk.off_cnt,
+                           ep->blk.off_flags, ctrl, pos, ordered_assignments, status));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags, (const uint32_t*)ctrl,
                            ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((P * 32 + 255) / 256, 148 * 8));
+  const int64_t pairs = T * ep->world;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((pairs * 32 + 255) / 256, 148 * 8));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
-                           (const uint16_t*)x_bf16, route_indices, route_weights,
-                           (const int32_t*)slot_of_assignment, P, (int)topk, ep->hidden, ep->world, ep->rank, ep->cap,
-                           peers, ep->blk, cnt, ctrl));
+                           (const uint16_t*)x_bf16, route_indices, route_weights, (const int32_t*)pos, T, k,
+                           ep->hidden, (int)n_experts, e_loc, expert_owner, ep->world, ep->rank, peers, ep->blk, cnt,
+                           ctrl));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags + ep->world,
                            (const uint32_t*)ctrl, ep->world, status, cnt, ep->rank, ctrl + EPC_NRECV));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
 
-extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_recv, int* status,
+extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_assignment, int* status,
                               void* stream) {
   DSV4_API_BEGIN
   if (int rc = ep_check(ep)) return rc;
@@ -561,11 +584,12 @@ extern "C" int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t*
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
   uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
-  const int64_t rows = (int64_t)ep->world * ep->cap;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows * 32 + 255) / 256, 148 * 8));
+  const int64_t assigns = (int64_t)ep->world * ep->tokens * ep->topk;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((assigns * 32 + 255) / 256, 148 * 8));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_return_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
-                           (const uint16_t*)rows_bf16, row_of_recv, (const int2*)(ep->base + ep->blk.off_src),
-                           (const uint32_t*)(ctrl + EPC_NRECV), ep->world, ep->rank, ep->cap, ep->hidden,
+                           (const uint16_t*)rows_bf16, row_of_assignment,
+                           (const int32_t*)(ep->base + ep->blk.off_idx), (const int2*)(ep->base + ep->blk.off_src),
+                           (const uint32_t*)(ctrl + EPC_NRECV), ep->world, ep->rank, ep->tokens, ep->topk, ep->hidden,
                            (uint8_t* const*)ep->peers_dev, ep->blk.off_back, ep->blk.off_flags, ctrl));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
                            (const uint32_t*)(ep->base + ep->blk.off_flags) + 2 * ep->world, (const uint32_t*)ctrl,

@@ -79,10 +79,10 @@ SIGNATURES = {
     "dsv4_slotdir_clear": (C.c_int, [_p, _p]),
     "dsv4_ep_dispatch_pack": (C.c_int, [_p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p]),
     "dsv4_ep_ipc_handle_bytes": (C.c_int, []),
-    "dsv4_ep_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i64, _i32, _p]),
+    "dsv4_ep_create": (C.c_int, [C.POINTER(_p), _i32, _i32, _i32, _i64, _i32, _i32, _p]),
     "dsv4_ep_connect": (C.c_int, [_p, _p]),
     "dsv4_ep_buffers": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p)]),
-    "dsv4_ep_dispatch": (C.c_int, [_p, _p, _p, _p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
+    "dsv4_ep_dispatch": (C.c_int, [_p, _p, _p, _p, _i64, _i32, _p, _p, _p, _p]),
     "dsv4_ep_return": (C.c_int, [_p, _p, _p, _p, _p]),
     "dsv4_ep_destroy": (C.c_int, [_p]),
     "dsv4_moe_combine_ordered": (C.c_int, [_p, _p, _i64, _i32, _i32, _p, _p]),

@@ -199,14 +199,15 @@ class _DevPtr:
 
 class P2PExchange:
     """Exchange over NVLink peer memory (``dsv4_ep_*``) with exact per-peer
-    counts: each source first publishes how many rows it sends to every
-    owner, then writes only its real rows, compactly, straight into the
-    owners' receive blocks (mapped through CUDA IPC); the owners run the
-    layer on exactly the rows they received (a device-side count, no host
-    synchronisation) and write the expert outputs straight back.  Device
-    flags with a per-step epoch replace the collectives; the step can be
-    captured in a CUDA graph.  Creating it is collective (the IPC handles are
-    gathered)."""
+    counts, one row per (token, destination rank): each source first
+    publishes how many of its tokens go to every owner, then writes each such
+    token once, compactly, straight into the owner's receive block (mapped
+    through CUDA IPC) with its k picks, the other ranks' experts set to -1.
+    The owner runs the layer (top-k over its received tokens) on exactly the
+    tokens it received (a device-side count, no host synchronisation) and
+    writes every assignment's output straight back.  Device flags with a
+    per-step epoch replace the collectives; the step can be captured in a
+    CUDA graph.  Creating it is collective (the IPC handles are gathered)."""
 
     def __init__(self, n_experts: int, rank: int, world: int, tokens: int, topk: int, hidden: int, device,
                  group=None, owner=None):
@@ -215,50 +216,51 @@ class P2PExchange:
         from dsv4_plugin._lib import check, lib
         self.n_experts, self.rank, self.world, self.group = n_experts, rank, world, group
         self.t, self.k, self.h = tokens, topk, hidden
-        self.cap = tokens * topk
         self.device = torch.device(device)
         self.owner = torch.tensor(owner if owner is not None else contiguous_placement(n_experts, world),
                                   dtype=torch.int32, device=self.device)
         nb = lib().dsv4_ep_ipc_handle_bytes()
         handle = C.create_string_buffer(nb)
         self._h = C.c_void_p()
-        check(lib().dsv4_ep_create(C.byref(self._h), self.device.index, rank, world, self.cap, hidden, handle))
+        check(lib().dsv4_ep_create(C.byref(self._h), self.device.index, rank, world, tokens, topk, hidden, handle))
         mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(self.device)
         every = torch.empty(world * nb, dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(every, mine, group=group)
         allh = every.cpu().numpy().tobytes()
         check(lib().dsv4_ep_connect(self._h, C.create_string_buffer(allh, len(allh))))
-        rx, re_, rw, rn, bk = (C.c_void_p() for _ in range(5))
-        check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(re_), C.byref(rw), C.byref(rn), C.byref(bk)))
-        rows = world * self.cap
+        rx, ri, rw, rn, bk = (C.c_void_p() for _ in range(5))
+        check(lib().dsv4_ep_buffers(self._h, C.byref(rx), C.byref(ri), C.byref(rw), C.byref(rn), C.byref(bk)))
+        rows = world * tokens
         dev = self.device
         self.recv_x = torch.as_tensor(_DevPtr(rx.value, (rows, hidden), "<i2"), device=dev).view(torch.bfloat16)
-        self.recv_e = torch.as_tensor(_DevPtr(re_.value, (rows,), "<i4"), device=dev)
-        self.recv_w = torch.as_tensor(_DevPtr(rw.value, (rows,), "<f4"), device=dev)
+        self.recv_idx = torch.as_tensor(_DevPtr(ri.value, (rows, topk), "<i4"), device=dev)
+        self.recv_w = torch.as_tensor(_DevPtr(rw.value, (rows, topk), "<f4"), device=dev)
         self.n_recv = torch.as_tensor(_DevPtr(rn.value, (1,), "<i4"), device=dev)
-        self.back = torch.as_tensor(_DevPtr(bk.value, (rows, hidden), "<i2"), device=dev).view(torch.bfloat16)
-        self.pos = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        self.back = torch.as_tensor(_DevPtr(bk.value, (tokens * topk, hidden), "<i2"),
+                                    device=dev).view(torch.bfloat16)
         self.ordered = torch.empty((tokens, topk), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
-        """-> (recv_x, recv_expert, recv_weight, n_recv): the received rows
-        (the first *n_recv of the buffers) and their device-side count."""
+        """-> (recv_x, recv_indices, recv_weights, n_recv): the received tokens
+        (the first *n_recv rows of the buffers) and their device-side count."""
         from dsv4_plugin._lib import check, lib
         x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
-        check(lib().dsv4_ep_dispatch(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.k,
-                                     self.n_experts, self.owner.data_ptr(), self.pos.data_ptr(),
-                                     self.ordered.data_ptr(), self.status.data_ptr(),
+        if x.shape[0] != self.t:
+            raise ValueError(f"the exchange was made for {self.t} tokens, got {x.shape[0]}")
+        check(lib().dsv4_ep_dispatch(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.n_experts,
+                                     self.owner.data_ptr(), self.ordered.data_ptr(), self.status.data_ptr(),
                                      torch.cuda.current_stream(self.device).cuda_stream))
-        return self.recv_x, self.recv_e, self.recv_w, self.n_recv
+        return self.recv_x, self.recv_idx, self.recv_w, self.n_recv
 
-    def give_back(self, rows: torch.Tensor, row_of_recv: torch.Tensor | None = None):
-        """Send the expert output of received row j (``rows[row_of_recv[j]]``,
-        or ``rows[j]``) back to its source; -> this rank's ``back`` rows."""
+    def give_back(self, rows: torch.Tensor, row_of_assignment: torch.Tensor | None = None):
+        """Send the output of every received assignment (token j, pick s) --
+        ``rows[row_of_assignment[j*k + s]]``, or ``rows[j*k + s]`` -- back to
+        its source; -> this rank's ``back`` rows [T*k, H] (assignment order)."""
         from dsv4_plugin._lib import check, lib
         check(lib().dsv4_ep_return(self._h, rows.data_ptr(),
-                                   None if row_of_recv is None else row_of_recv.data_ptr(), self.status.data_ptr(),
-                                   torch.cuda.current_stream(self.device).cuda_stream))
+                                   None if row_of_assignment is None else row_of_assignment.data_ptr(),
+                                   self.status.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
         return self.back
 
     def check_status(self):
@@ -341,9 +343,10 @@ class ExpertParallelMoE:
 
     def forward_p2p(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         """The same layer through ``P2PExchange`` (NVLink peer memory, exact
-        counts): no collectives, no host synchronisation; capturable in a
-        CUDA graph.  The owner runs the experts on exactly the rows it
-        received and returns each output row straight from the layer's sorted
+        counts, each token once per destination rank): no collectives, no host
+        synchronisation; capturable in a CUDA graph.  The owner runs the
+        experts (top-k, foreign picks -1) on exactly the tokens it received
+        and returns each assignment's output straight from the layer's sorted
         output (no combine pass on the owner).  Equals ``forward`` bit for
         bit.  The first call with a new token count is collective (it maps
         the peers' buffers)."""
@@ -366,12 +369,11 @@ class ExpertParallelMoE:
         mark()
         w, idx = moe._route(hs, None)
         mark()
-        x_recv, e_recv, w_recv, n_recv = ex.dispatch(hs, w, idx)
+        x_recv, i_recv, w_recv, n_recv = ex.dispatch(hs, w, idx)
         mark()
-        plan = moe.engine.plan_for(moe.n_routed_experts, 1, x_recv.shape[0], moe.swiglu_limit or 0.0)
+        plan = moe.engine.plan_for(moe.n_routed_experts, moe.topk, x_recv.shape[0], moe.swiglu_limit or 0.0)
         self.plan = plan
-        rows, inv = plan.forward_rows(x_recv, w_recv.view(-1, 1), e_recv.view(-1, 1), self.slot_of, profile,
-                                      n_tokens_dev=n_recv)
+        rows, inv = plan.forward_rows(x_recv, w_recv, i_recv, self.slot_of, profile, n_tokens_dev=n_recv)
         mark()
         back = ex.give_back(rows, inv)
         mark()

@@ -341,40 +341,46 @@ int dsv4_ep_dispatch_pack(const void* x_bf16, const float* route_weights, const 
 /* ------------------------------------------------------------------------ *
  * Expert-parallel exchange over NVLink peer memory (no counterpart in the
  * reference).  Each rank owns one device block; peers map it through CUDA
- * IPC and write into it directly, only real rows crossing NVLink.  Per step:
- *   dsv4_ep_dispatch: per-destination slots as dsv4_ep_dispatch_pack (with
- *     the same expert_owner map); each source first publishes its per-peer
- *     counts to every peer, then writes its rows, experts and weights into
- *     the owners' blocks, compact: owner d holds the rows of source s at
- *     sum_{s'<s} n[s'->d] + r; waits (bounded, DSV4_ETIMEOUT in *status)
- *     until every source published; the number of rows received is then in
- *     the device word *n_recv (dsv4_ep_buffers);
- *   (the routed-expert layer runs on recv_x / recv_expert / recv_weight,
- *     topk = 1, with the device count: dsv4_moe_forward_rows)
- *   dsv4_ep_return: each received row j < *n_recv back into its source's
- *     `back` (owner d fills rows d*cap + r), read as row row_of_recv[j] of
- *     `rows` (the layer's sorted output rows and its inv; NULL: row j), then
- *     waits for every owner;
- *   dsv4_moe_combine_ordered(back, ordered_slots, ...) gives the output.
+ * IPC and write into it directly.  A token crosses once per destination
+ * rank that holds one of its experts, not once per expert.  Per step:
+ *   dsv4_ep_dispatch: each source first publishes to every peer how many of
+ *     its tokens go there, then writes each such token's row, its k picks
+ *     with the other ranks' experts set to -1 (weight 0), and its source
+ *     into the owner's block, compact: owner d holds the tokens of source s
+ *     at sum_{s'<s} n[s'->d] + r (r = stable rank of the token among those
+ *     of s with an expert on d); waits (bounded, DSV4_ETIMEOUT in *status)
+ *     until every source published; the number of tokens received is then in
+ *     the device word *n_recv (dsv4_ep_buffers).  ordered_assignments[t*k+j]
+ *     lists token t's assignments a = t*k + j' in ascending expert order
+ *     (-1 after the last), the order in which the returned rows are added;
+ *   (the routed-expert layer runs on recv_x / recv_indices / recv_weights,
+ *     [tokens, k], with the device count: dsv4_moe_forward_rows)
+ *   dsv4_ep_return: the output of each received assignment (token j, pick
+ *     s, an expert of this rank) back into its source's `back` row t*k + s,
+ *     read as row row_of_assignment[j*k + s] of `rows` (the layer's sorted
+ *     output rows and its inv; NULL: row j*k + s), then waits for every owner;
+ *   dsv4_moe_combine_ordered(back, ordered_assignments, ...) gives the output.
  * Every call is an asynchronous device operation with a fixed launch shape,
  * so a step can be captured in a CUDA graph.  All ranks must make the same
- * calls in the same order.  cap = capacity rows per source (n_tokens*topk).
- * After a DSV4_ETIMEOUT the step's data are undefined and a late peer may
- * still write into this rank's block: destroy the handle and create a new
- * one.  The IPC handle is dsv4_ep_ipc_handle_bytes() bytes; dsv4_ep_connect
- * takes all ranks' handles, rank-major.
+ * calls in the same order.  Buffers: recv_x [world*max_tokens, hidden] bf16,
+ * recv_indices / recv_weights [world*max_tokens, topk], back
+ * [max_tokens*topk, hidden] bf16.  After a DSV4_ETIMEOUT the step's data are
+ * undefined and a late peer may still write into this rank's block: destroy
+ * the handle and create a new one.  The IPC handle is
+ * dsv4_ep_ipc_handle_bytes() bytes; dsv4_ep_connect takes all ranks'
+ * handles, rank-major.
  * ------------------------------------------------------------------------ */
 typedef struct dsv4_ep dsv4_ep;
 int dsv4_ep_ipc_handle_bytes(void);
-int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t cap_rows, int32_t hidden,
-                   void* ipc_handle_out);
+int dsv4_ep_create(dsv4_ep** out, int32_t device, int32_t rank, int32_t world, int64_t max_tokens, int32_t topk,
+                   int32_t hidden, void* ipc_handle_out);
 int dsv4_ep_connect(dsv4_ep* ep, const void* all_handles);
-int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_expert, float** recv_weight, int32_t** n_recv,
+int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_indices, float** recv_weights, int32_t** n_recv,
                     void** back_bf16);
 int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights, const int32_t* route_indices,
-                     int64_t n_tokens, int32_t topk, int32_t n_experts, const int32_t* expert_owner,
-                     int32_t* slot_of_assignment, int32_t* ordered_slots, int* status, void* stream);
-int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_recv, int* status, void* stream);
+                     int64_t n_tokens, int32_t n_experts, const int32_t* expert_owner, int32_t* ordered_assignments,
+                     int* status, void* stream);
+int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_assignment, int* status, void* stream);
 int dsv4_ep_destroy(dsv4_ep* ep);
 
 #ifdef __cplusplus

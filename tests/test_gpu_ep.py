@@ -197,15 +197,16 @@ def _run_timeout(rank, world, port, out):
         idx = torch.stack([torch.randperm(n_experts, generator=g)[:topk] for _ in range(tokens)]).to(torch.int32)
         w = torch.rand(tokens, topk, generator=g).to(dev)
         ex = P2PExchange(n_experts, rank, world, tokens, topk, hidden, dev)
+        rows = torch.zeros((world * tokens * topk, hidden), dtype=torch.bfloat16, device=dev)
         ex.dispatch(x, w, idx.to(dev))
-        ex.give_back(ex.recv_x)          # identity expert: every received row goes back as is
+        ex.give_back(rows)               # a stand-in expert output for every received assignment
         ex.check_status()
         out[(rank, "step1")] = True
         dist.barrier()
         if rank == 0:
             t0 = time.time()
             ex.dispatch(x, w, idx.to(dev))
-            ex.give_back(ex.recv_x)
+            ex.give_back(rows)
             try:
                 ex.check_status()
                 out[(rank, "timeout")] = False
