@@ -204,7 +204,7 @@ namespace dsv4 {
 // may still write: the handle must be destroyed and created again.
 // ---------------------------------------------------------------------------
 struct EpBlock {
-  int64_t off_back, off_idx, off_w, off_src, off_cnt, off_pos, off_flags, off_ctrl, bytes;
+  int64_t off_back, off_idx, off_w, off_src, off_cnt, off_pos, off_dst, off_flags, off_ctrl, bytes;
 };
 static EpBlock ep_block(int world, int64_t tokens, int topk, int hidden) {
   auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
@@ -216,7 +216,8 @@ static EpBlock ep_block(int world, int64_t tokens, int topk, int hidden) {
   b.off_src = b.off_w + al(rows * topk * 4);
   b.off_cnt = b.off_src + al(rows * 8);
   b.off_pos = b.off_cnt + al((int64_t)world * world * 4);
-  b.off_flags = b.off_pos + al(tokens * world * 4);
+  b.off_dst = b.off_pos + al(tokens * world * 4);
+  b.off_flags = b.off_dst + al(rows * topk * 8);
   b.off_ctrl = b.off_flags + al(3 * (int64_t)world * 4);
   b.bytes = b.off_ctrl + 256;
   return b;
@@ -417,6 +418,40 @@ __global__ void ep_p2p_return_kernel(const uint16_t* __restrict__ y, const int32
   ep_publish(ctrl, EPC_BACK, peers, world, off_flags, 2 * world + my_rank);
 }
 
+// The return target of every received assignment a = j*k + s (an expert of
+// this rank): row t*k + s of its source's `back`, as a device address (a
+// peer's memory for the other ranks); null for the other ranks' picks.  The
+// down GEMM in scatter mode stores each output row there directly.
+__global__ void ep_p2p_targets_kernel(const int32_t* __restrict__ recv_idx, const int2* __restrict__ src_of,
+                                      const uint32_t* __restrict__ n_recv, int world, int64_t T, int topk, int H,
+                                      uint8_t* const* __restrict__ peers, int64_t off_back,
+                                      uint16_t** __restrict__ dst) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t n = (int64_t)*reinterpret_cast<const volatile uint32_t*>(n_recv) * topk;
+  for (int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; a < n; a += (int64_t)gridDim.x * blockDim.x) {
+    uint16_t* d = nullptr;
+    if (recv_idx[a] >= 0) {
+      const int64_t j = a / topk;
+      const int s = (int)(a - j * topk);
+      const int2 st = src_of[j];
+      if (st.x >= 0 && st.x < world && st.y >= 0 && st.y < T)
+        d = reinterpret_cast<uint16_t*>(peers[st.x] + off_back) + ((int64_t)st.y * topk + s) * H;
+    }
+    dst[a] = d;
+  }
+}
+
+// One CTA: after the rows this rank wrote into its peers' `back` (the down
+// GEMM in scatter mode, a finished kernel, its stores fenced system-wide),
+// publish "returned" to every peer.
+__global__ void ep_p2p_publish_back_kernel(uint32_t* __restrict__ ctrl, uint8_t* const* __restrict__ peers, int world,
+                                           int64_t off_flags, int my_rank) {
+  griddep_wait();
+  griddep_launch();
+  ep_publish(ctrl, EPC_BACK, peers, world, off_flags, 2 * world + my_rank);
+}
+
 // One thread: wait (bounded) until every source has published this step's
 // epoch in flags[first .. first+world).  With `cnt`, also writes the number
 // of tokens this rank receives (column my_rank of the count matrix) to *n_recv.
@@ -570,6 +605,37 @@ extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* ro
                            ctrl));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags + ep->world,
                            (const uint32_t*)ctrl, ep->world, status, cnt, ep->rank, ctrl + EPC_NRECV));
+  // the return targets of the received assignments (for the scatter-mode down GEMM)
+  const int64_t assigns = (int64_t)ep->world * ep->tokens * ep->topk;
+  const unsigned tblocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((assigns + 255) / 256, 148 * 4));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_targets_kernel, dim3(tblocks), dim3(256), 0, st, pdl,
+                           (const int32_t*)(ep->base + ep->blk.off_idx), (const int2*)(ep->base + ep->blk.off_src),
+                           (const uint32_t*)(ctrl + EPC_NRECV), ep->world, ep->tokens, ep->topk, ep->hidden, peers,
+                           ep->blk.off_back, reinterpret_cast<uint16_t**>(ep->base + ep->blk.off_dst)));
+  DSV4_CUDA_CHECK(cudaGetLastError());
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_return_targets(dsv4_ep* ep, void*** assign_dst) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(ep && assign_dst, "null pointer");
+  *assign_dst = reinterpret_cast<void**>(ep->base + ep->blk.off_dst);
+  DSV4_API_END
+}
+
+extern "C" int dsv4_ep_return_published(dsv4_ep* ep, int* status, void* stream) {
+  DSV4_API_BEGIN
+  if (int rc = ep_check(ep)) return rc;
+  DSV4_CHECK_ARG(status, "null pointer");
+  DSV4_CUDA_CHECK(cudaSetDevice(ep->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool pdl = pdl_enabled();
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ep->base + ep->blk.off_ctrl);
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_publish_back_kernel, dim3(1), dim3(32), 0, st, pdl, ctrl,
+                           (uint8_t* const*)ep->peers_dev, ep->world, ep->blk.off_flags, ep->rank));
+  DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl,
+                           (const uint32_t*)(ep->base + ep->blk.off_flags) + 2 * ep->world, (const uint32_t*)ctrl,
+                           ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

@@ -107,6 +107,12 @@ struct GemmParams {
   int shared_expert;         // -1: none
   const uint8_t* shared_slot;
   int64_t shared_sfa_off;    // byte offset of its A scale atoms
+  // down GEMM, scatter mode (expert parallelism): the output row of sorted
+  // row r goes to assign_dst[sorted_flat[r]] (any memory this GPU can store
+  // to, a peer's buffer over NVLink included; null: dropped) instead of
+  // out_bf16, so the return of the rows overlaps the GEMM tile by tile
+  const int32_t* sorted_flat;
+  uint16_t* const* assign_dst;
 };
 
 __device__ __forceinline__ float warp_max_f(float v) {
@@ -496,15 +502,36 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
         if constexpr (EPI == EPI_STORE_BF16) {
           // rows 0..127 of the pair -> acc0, rows 128..255 -> acc1
-          uint16_t* dst = p.out_bf16 + (int64_t)(row0 + cs) * p.out_ld + mt * p.out_tile_cols + i;
+          if (p.assign_dst) {
+            // scatter: lane L fetches the destination of column cs+L, then
+            // every column's row is stored where it belongs (plain stores,
+            // 64 contiguous bytes per warp and column)
+            uint16_t* mine = nullptr;
+            if (lane < width && cs + lane < nrows) {
+              const int a = p.sorted_flat[row0 + cs + lane];
+              mine = a >= 0 ? p.assign_dst[a] : nullptr;
+            }
+            const unsigned long long mv = reinterpret_cast<unsigned long long>(mine);
 #pragma unroll
-          for (int n = 0; n < SUB; ++n)
-            if (n < width && cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
-          if constexpr (NUM_A == 2) {
-            uint16_t* dst1 = dst + G_BM;
+            for (int n = 0; n < SUB; ++n) {
+              const unsigned long long b = __shfl_sync(0xffffffffu, mv, n);
+              if (b) {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(b) + mt * p.out_tile_cols + i;
+                dst[0] = bf16_bits(acc0[n]);
+                if constexpr (NUM_A == 2) dst[G_BM] = bf16_bits(acc1[n]);
+              }
+            }
+          } else {
+            uint16_t* dst = p.out_bf16 + (int64_t)(row0 + cs) * p.out_ld + mt * p.out_tile_cols + i;
 #pragma unroll
             for (int n = 0; n < SUB; ++n)
-              if (n < width && cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+              if (n < width && cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+            if constexpr (NUM_A == 2) {
+              uint16_t* dst1 = dst + G_BM;
+#pragma unroll
+              for (int n = 0; n < SUB; ++n)
+                if (n < width && cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+            }
           }
         } else {
           // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
@@ -592,6 +619,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
   }
 
+  // scatter mode: the rows stored to other GPUs are visible system-wide
+  // before this grid completes and a later kernel publishes them
+  if (EPI == EPI_STORE_BF16 && p.assign_dst) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -827,6 +827,7 @@ struct PassArgs {
   const uint8_t* shared_slot;
   const uint16_t* extra;
   bool timed;                // records the stage events
+  uint16_t* const* assign_dst = nullptr;   // down GEMM scatter targets (expert parallelism)
 };
 
 static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int64_t n_tokens,
@@ -896,6 +897,8 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   g2.out_sf = nullptr;
   g2.out_bf16 = wsp<uint16_t>(p, w.out);
   g2.out_ld = p->H;
+  g2.sorted_flat = sorted_flat;
+  g2.assign_dst = a.assign_dst;
   // without a shared expert the kernels never read the shared maps; any
   // valid map fills the parameter
   const CUtensorMap& sh13 = a.sh13 ? *a.sh13 : p->tmA13;
@@ -923,7 +926,8 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
 
 static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
                             const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
-                            const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16, void* stream) {
+                            const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16, void* stream,
+                            uint16_t* const* assign_dst = nullptr) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert, "null pointer");
   DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
@@ -936,8 +940,9 @@ static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf1
   DSV4_CUDA_CHECK(cudaSetDevice(p->device));
   cudaStream_t st = (cudaStream_t)stream;
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
+  DSV4_CHECK_ARG(!assign_dst || (!y_bf16 && !p->shared), "scatter mode writes no y and runs no shared expert");
   if (!p->shared) {
-    const PassArgs a{fp4, p->topk, p->topk, -1, nullptr, nullptr, nullptr, nullptr, true};
+    const PassArgs a{fp4, p->topk, p->topk, -1, nullptr, nullptr, nullptr, nullptr, true, assign_dst};
     if (int rc = moe_pass(p, a, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
                           y_bf16, st))
       return rc;
@@ -995,6 +1000,15 @@ extern "C" int dsv4_moe_forward_rows(dsv4_moe_plan* p, int32_t profile, const vo
                                      void* stream) {
   return moe_forward_impl(p, profile, x_bf16, max_tokens, n_tokens_dev, route_weights, route_indices,
                           slot_of_expert, nullptr, y_bf16, stream);
+}
+
+extern "C" int dsv4_moe_forward_scatter(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t max_tokens,
+                                        const int32_t* n_tokens_dev, const float* route_weights,
+                                        const int32_t* route_indices, const int32_t* slot_of_expert,
+                                        void* const* assign_dst, void* stream) {
+  if (!assign_dst) return fail(DSV4_EINVAL, "dsv4_moe_forward_scatter: null assign_dst");
+  return moe_forward_impl(p, profile, x_bf16, max_tokens, n_tokens_dev, route_weights, route_indices,
+                          slot_of_expert, nullptr, nullptr, stream, reinterpret_cast<uint16_t* const*>(assign_dst));
 }
 
 extern "C" int dsv4_moe_output_rows(dsv4_moe_plan* p, void** rows_bf16, int32_t** inv) {

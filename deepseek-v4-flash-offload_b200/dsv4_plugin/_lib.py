@@ -51,6 +51,7 @@ SIGNATURES = {
     "dsv4_moe_forward": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p]),
     "dsv4_moe_forward_rows": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_output_rows": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p)]),
+    "dsv4_moe_forward_scatter": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_shared_slot_bytes": (_i64, [_i32, _i32]),
     "dsv4_pack_shared_host": (C.c_int, [_p, _p, _p, _p, _p, _p, _i32, _i32, _p]),
     "dsv4_moe_workspace_bytes_ex": (_i64, [_i32, _i32, _i32, _i32, _i64, _i32]),
@@ -84,6 +85,8 @@ SIGNATURES = {
     "dsv4_ep_buffers": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p)]),
     "dsv4_ep_dispatch": (C.c_int, [_p, _p, _p, _p, _i64, _i32, _p, _p, _p, _p]),
     "dsv4_ep_return": (C.c_int, [_p, _p, _p, _p, _p]),
+    "dsv4_ep_return_targets": (C.c_int, [_p, C.POINTER(_p)]),
+    "dsv4_ep_return_published": (C.c_int, [_p, _p, _p]),
     "dsv4_ep_destroy": (C.c_int, [_p]),
     "dsv4_moe_combine_ordered": (C.c_int, [_p, _p, _i64, _i32, _i32, _p, _p]),
     "dsv4_moe_stage_times": (C.c_int, [_p, C.POINTER(C.c_float), _i32]),

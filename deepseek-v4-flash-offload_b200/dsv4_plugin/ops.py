@@ -319,6 +319,26 @@ class MoEPlan:
                                           idx.data_ptr(), so.data_ptr(), None, _stream(x.device)))
         return self.output_rows(t * self.topk)
 
+    def forward_scatter(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, slot_of: torch.Tensor,
+                        assign_dst_ptr: int, profile: str = "bf16", n_tokens_dev: torch.Tensor | None = None) -> None:
+        """The layer whose down GEMM stores the output row of assignment a
+        straight to the device address table ``assign_dst_ptr`` [T * k]
+        (another GPU's memory included; null entries are dropped)."""
+        _need_cuda(x, weights, indices, slot_of)
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise TypeError("x must be contiguous bf16")
+        t = x.shape[0]
+        if t > self.max_tokens:
+            raise ValueError(f"{t} tokens exceed the plan's max_tokens={self.max_tokens}")
+        w = weights if weights.dtype == torch.float32 and weights.is_contiguous() else weights.contiguous().float()
+        idx = indices if indices.dtype == torch.int32 and indices.is_contiguous() else \
+            indices.contiguous().to(torch.int32)
+        so = slot_of.contiguous().to(torch.int32)
+        check(lib().dsv4_moe_forward_scatter(self._h, PROFILES[profile], x.data_ptr(), t,
+                                             None if n_tokens_dev is None else n_tokens_dev.data_ptr(),
+                                             w.data_ptr(), idx.data_ptr(), so.data_ptr(), assign_dst_ptr,
+                                             _stream(x.device)))
+
     def output_rows(self, n_assign: int):
         rp, ip = C.c_void_p(), C.c_void_p()
         check(lib().dsv4_moe_output_rows(self._h, C.byref(rp), C.byref(ip)))

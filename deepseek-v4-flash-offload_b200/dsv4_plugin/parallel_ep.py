@@ -253,6 +253,24 @@ class P2PExchange:
                                      torch.cuda.current_stream(self.device).cuda_stream))
         return self.recv_x, self.recv_idx, self.recv_w, self.n_recv
 
+    def return_targets(self) -> int:
+        """Device address of the table of each received assignment's return
+        destination (filled by ``dispatch``), for ``MoEPlan.forward_scatter``."""
+        import ctypes as C
+
+        from dsv4_plugin._lib import check, lib
+        t = C.c_void_p()
+        check(lib().dsv4_ep_return_targets(self._h, C.byref(t)))
+        return t.value
+
+    def returned(self):
+        """After the scatter-mode layer wrote the rows into the sources'
+        ``back``: announce it and wait for every owner; -> ``back``."""
+        from dsv4_plugin._lib import check, lib
+        check(lib().dsv4_ep_return_published(self._h, self.status.data_ptr(),
+                                             torch.cuda.current_stream(self.device).cuda_stream))
+        return self.back
+
     def give_back(self, rows: torch.Tensor, row_of_assignment: torch.Tensor | None = None):
         """Send the output of every received assignment (token j, pick s) --
         ``rows[row_of_assignment[j*k + s]]``, or ``rows[j*k + s]`` -- back to
@@ -299,6 +317,10 @@ class ExpertParallelMoE:
         self._static = {}
         self._p2p = {}
         self.segment_times = None   # set to {} to time the segments of eager forward_static / forward_p2p calls
+        # the peer-memory path returns the rows from the down GEMM's epilogue
+        # (DSV4_EP_FUSED_RETURN=0: a separate return kernel after the layer)
+        import os
+        self.fused_return = os.environ.get("DSV4_EP_FUSED_RETURN", "1") != "0"
 
     def forward_static(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         """The same layer through ``StaticExchange``: no host synchronisation,
@@ -373,9 +395,17 @@ class ExpertParallelMoE:
         mark()
         plan = moe.engine.plan_for(moe.n_routed_experts, moe.topk, x_recv.shape[0], moe.swiglu_limit or 0.0)
         self.plan = plan
-        rows, inv = plan.forward_rows(x_recv, w_recv, i_recv, self.slot_of, profile, n_tokens_dev=n_recv)
-        mark()
-        back = ex.give_back(rows, inv)
+        if self.fused_return:
+            # the down GEMM's epilogue stores every output row straight into
+            # its source's `back` over NVLink, tile by tile
+            plan.forward_scatter(x_recv, w_recv, i_recv, self.slot_of, ex.return_targets(), profile,
+                                 n_tokens_dev=n_recv)
+            mark()
+            back = ex.returned()
+        else:
+            rows, inv = plan.forward_rows(x_recv, w_recv, i_recv, self.slot_of, profile, n_tokens_dev=n_recv)
+            mark()
+            back = ex.give_back(rows, inv)
         mark()
         y = ops.combine_ordered(back, ex.ordered)
         mark()

@@ -183,6 +183,14 @@ int dsv4_moe_forward(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, i
 int dsv4_moe_forward_rows(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t max_tokens,
                           const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
                           const int32_t* slot_of_expert, void* y_bf16, void* stream);
+/* dsv4_moe_forward_rows without y whose down GEMM writes the output row of
+ * assignment a = t * topk + j to assign_dst[a] (any memory this GPU can
+ * store to, another GPU's included; null: dropped) straight from its
+ * epilogue, instead of the plan's output rows.  No counterpart in the
+ * reference (the expert-parallel return fused into the GEMM). */
+int dsv4_moe_forward_scatter(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t max_tokens,
+                             const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
+                             const int32_t* slot_of_expert, void* const* assign_dst, void* stream);
 /* Device pointers of the last forward's per-assignment output rows (bf16
  * [rows, hidden], sorted by expert) and of inv (int32 [n_tokens * topk]). */
 int dsv4_moe_output_rows(dsv4_moe_plan* plan, void** rows_bf16, int32_t** inv);
@@ -381,6 +389,16 @@ int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights
                      int64_t n_tokens, int32_t n_experts, const int32_t* expert_owner, int32_t* ordered_assignments,
                      int* status, void* stream);
 int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_assignment, int* status, void* stream);
+/* The return fused into the down GEMM: dsv4_ep_return_targets gives the
+ * device table [world*max_tokens*topk] of each received assignment's
+ * destination (row t*k + s of its source's `back`, in a peer's memory for
+ * the other ranks; null for the other ranks' picks), filled by each
+ * dsv4_ep_dispatch; dsv4_moe_forward_scatter(..., table) stores every output
+ * row there from the GEMM's epilogue, so the rows cross NVLink while later
+ * tiles compute; dsv4_ep_return_published then announces the returned rows
+ * and waits for every owner's (bounded, DSV4_ETIMEOUT). */
+int dsv4_ep_return_targets(dsv4_ep* ep, void*** assign_dst);
+int dsv4_ep_return_published(dsv4_ep* ep, int* status, void* stream);
 int dsv4_ep_destroy(dsv4_ep* ep);
 
 #ifdef __cplusplus

@@ -90,10 +90,16 @@ def _run(rank, world, port, tokens, out, scattered=False):
         out[(rank, "graph")] = bool(torch.equal(ys.view(torch.int16), ref.view(torch.int16)))
         del g
         torch.cuda.synchronize(dev)
-        # exchange over NVLink peer memory, eager and captured
+        # exchange over NVLink peer memory, eager and captured (the return
+        # fused into the down GEMM), and with a separate return kernel
         got = epm.forward_p2p(xt)
         epm._p2p[xt.shape[0]].check_status()
-        out[(rank, "p2p")] = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        ok = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        epm.fused_return = False
+        got = epm.forward_p2p(xt)
+        epm._p2p[xt.shape[0]].check_status()
+        epm.fused_return = True
+        out[(rank, "p2p")] = ok and bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
         epm.forward_p2p(xs)
         torch.cuda.synchronize(dev)
         g = torch.cuda.CUDAGraph()
