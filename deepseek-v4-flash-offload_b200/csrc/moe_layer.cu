@@ -333,6 +333,155 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// moe_align for large batches on many CTAs (the same stable counting sort):
+//   count  CTA b takes assignments [1024 b, 1024 b + 1024), one per thread,
+//          and writes its per-expert counts cnt_blk[b][E];
+//   scan   one CTA: per expert, the exclusive prefix over the blocks and the
+//          total; the padded group offsets, active list and GEMM chunks as
+//          the one-CTA kernel; cnt_blk becomes each block's start row inside
+//          each group; padding rows;
+//   place  CTA b again: an assignment's row is its block's start in its
+//          expert's group plus its rank among the block's earlier equal
+//          experts (warp ballots + per-warp counts), so the order stays
+//          token-major within an expert.
+// The token count may be known only on the device (n_tokens_dev); CTAs past
+// it do nothing.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int align_count_p(int P, int topk, const int32_t* __restrict__ n_tokens_dev) {
+  return n_tokens_dev ? min(P, max(0, *n_tokens_dev) * topk) : P;
+}
+
+// ranks of this CTA's assignments among equal experts of the CTA: returns
+// the rank, leaves per-expert counts of the CTA in cnt[E] (smem)
+__device__ __forceinline__ int block_rank(int e, int E, int ebits, uint16_t* wc, int* cnt) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t* wc32 = reinterpret_cast<uint32_t*>(wc);
+  for (int j = tid; j < 16 * E; j += AL_THREADS) wc32[j] = 0u;
+  __syncthreads();
+  const unsigned same = match_small(e, ebits);
+  const int rank = __popc(same & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) wc[warp * E + e] = (uint16_t)__popc(same);
+  __syncthreads();
+  for (int x = tid; x < E; x += AL_THREADS) {
+    int c = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int v = wc[w * E + x];
+      wc[w * E + x] = (uint16_t)c;
+      c += v;
+    }
+    cnt[x] = c;
+  }
+  __syncthreads();
+  return e >= 0 ? (int)wc[warp * E + e] + rank : -1;
+}
+
+__device__ __forceinline__ int align_read(const int32_t* __restrict__ idx, int a, int P, int topk, int E, int k_in,
+                                          int shared_e, int* status, int32_t* __restrict__ inv, bool write_inv) {
+  if (a >= P) return -1;
+  int e = assign_expert(idx, a, topk, k_in, shared_e);
+  if (e == -1) {
+    if (write_inv) inv[a] = -1;
+  } else if (e < 0 || e >= E) {
+    if (write_inv) {
+      set_status(status, DSV4_EINVAL);
+      inv[a] = -1;
+    }
+    e = -1;
+  }
+  return e;
+}
+
+__global__ void __launch_bounds__(AL_THREADS, 1)
+    align_count_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, int k_in, int shared_e,
+                       const int32_t* __restrict__ n_tokens_dev, int32_t* __restrict__ cnt_blk, int* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                                              // E
+  uint16_t* wc = reinterpret_cast<uint16_t*>(cnt + E);       // [32][E]
+  griddep_wait();
+  griddep_launch();
+  P = align_count_p(P, topk, n_tokens_dev);
+  if ((int64_t)blockIdx.x * AL_THREADS >= P) return;
+  const int ebits = 32 - __clz(max(E - 1, 1));
+  const int a = blockIdx.x * AL_THREADS + threadIdx.x;
+  const int e = align_read(idx, a, P, topk, E, k_in, shared_e, status, nullptr, false);
+  block_rank(e, E, ebits, wc, cnt);
+  for (int x = threadIdx.x; x < E; x += AL_THREADS) cnt_blk[(int64_t)blockIdx.x * E + x] = cnt[x];
+}
+
+__global__ void __launch_bounds__(AL_THREADS, 1)
+    align_scan_kernel(int P, int topk, int E, const int32_t* __restrict__ n_tokens_dev, int32_t* __restrict__ cnt_blk,
+                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
+                      int32_t* __restrict__ active, int32_t* __restrict__ n_active, float* __restrict__ sorted_w,
+                      int4* __restrict__ chunks, int32_t* __restrict__ n_chunks, int pad) {
+  __shared__ int scratch[96];
+  __shared__ int run_s[1024], cnt_s[1024];
+  griddep_wait();
+  griddep_launch();
+  P = align_count_p(P, topk, n_tokens_dev);
+  const int nblk = (P + AL_THREADS - 1) / AL_THREADS;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int c = 0;
+  if (tid < E) {
+    for (int b = 0; b < nblk; ++b) {
+      const int v = cnt_blk[(int64_t)b * E + tid];
+      cnt_blk[(int64_t)b * E + tid] = c;
+      c += v;
+    }
+  }
+  const int cpad = (c + pad - 1) / pad * pad;
+  const int nch = cpad / pad;
+  int3 tot3;
+  const int3 ex = block_scan3(cpad, c > 0 ? 1 : 0, nch, scratch, &tot3);
+  if (tid < E) {
+    run_s[tid] = ex.x;
+    cnt_s[tid] = c;
+    counts[tid] = c;
+    offsets[tid] = ex.x;
+    if (c > 0) active[ex.y] = tid;
+    if (chunks)
+      for (int j = 0; j < nch; ++j) chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), 0);
+    for (int b = 0; b < nblk; ++b) cnt_blk[(int64_t)b * E + tid] += ex.x;   // absolute start rows
+  }
+  if (tid == 0) {
+    offsets[E] = tot3.x;
+    *n_active = tot3.y;
+    if (chunks) *n_chunks = tot3.z;
+  }
+  __syncthreads();
+  for (int g = warp; g < E; g += AL_THREADS / 32) {
+    const int r0 = run_s[g] + cnt_s[g], r1 = run_s[g] + (cnt_s[g] + pad - 1) / pad * pad;
+    for (int r = r0 + lane; r < r1; r += 32) {
+      sorted_flat[r] = -1;
+      if (sorted_w) sorted_w[r] = 0.f;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(AL_THREADS, 1)
+    align_place_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, int k_in, int shared_e,
+                       const float* __restrict__ w_flat, const int32_t* __restrict__ n_tokens_dev,
+                       const int32_t* __restrict__ start_blk, int32_t* __restrict__ sorted_flat,
+                       int32_t* __restrict__ inv, float* __restrict__ sorted_w, int* status) {
+  extern __shared__ int sm[];
+  int* cnt = sm;
+  uint16_t* wc = reinterpret_cast<uint16_t*>(cnt + E);
+  griddep_wait();
+  griddep_launch();
+  P = align_count_p(P, topk, n_tokens_dev);
+  if ((int64_t)blockIdx.x * AL_THREADS >= P) return;
+  const int ebits = 32 - __clz(max(E - 1, 1));
+  const int a = blockIdx.x * AL_THREADS + threadIdx.x;
+  const int e = align_read(idx, a, P, topk, E, k_in, shared_e, status, inv, true);
+  const int r = block_rank(e, E, ebits, wc, cnt);
+  if (e >= 0) {
+    const int pos = start_blk[(int64_t)blockIdx.x * E + e] + r;
+    sorted_flat[pos] = a;
+    inv[a] = pos;
+    if (sorted_w) sorted_w[pos] = assign_weight(w_flat, a, topk, k_in, shared_e);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // activation quant + gather into the GEMM B operand.  Assignment a = t*topk+j
 // writes token t's row to its sorted row inv[a] (padding rows are never
 // touched; invalid assignments, inv < 0, are skipped).  Scales
@@ -563,7 +712,7 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const
 
 struct WsLayout {
   int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
-  int64_t xq, xsf, hq, hsf, out, ys, bytes;
+  int64_t xq, xsf, hq, hsf, out, ys, blk, bytes;
   int64_t p_max, p_cap, max_chunks;
 };
 
@@ -601,6 +750,7 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   w.hsf = take((I / 128) * (w.p_cap / G_BN) * 512);
   w.out = take(2 * w.p_cap * H);
   w.ys = shared ? take(2 * max_tokens * H) : 0;
+  w.blk = take(4 * E * ((w.p_max + AL_THREADS - 1) / AL_THREADS + 1));   // per-block counts of the large align
   w.bytes = o;
   return w;
 }
@@ -799,6 +949,11 @@ extern "C" int dsv4_moe_plan_create_ex(dsv4_moe_plan** out, int32_t hidden, int3
   const size_t al_smem = (size_t)(2 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
+  const size_t blk_smem = (size_t)n_experts * 4 + (size_t)32 * n_experts * 2;
+  DSV4_CUDA_CHECK(
+      cudaFuncSetAttribute(align_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)blk_smem));
+  DSV4_CUDA_CHECK(
+      cudaFuncSetAttribute(align_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)blk_smem));
   *out = p.release();
   DSV4_API_END
 }
@@ -848,10 +1003,26 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   // events between stages break the programmatic overlap: no PDL while timing
   const bool pdl = pdl_enabled() && !p->timing;
   mark(0);
-  DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P, a.topk,
-                           p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets), sorted_flat,
-                           inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                           wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e));
+  if (P <= AL_THREADS) {
+    DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P,
+                             a.topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
+                             sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
+                             wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e));
+  } else {
+    // large batches: count per block, scan on one CTA, place per block
+    const unsigned nblk = (unsigned)((P + AL_THREADS - 1) / AL_THREADS);
+    const size_t blk_smem = (size_t)p->E * 4 + (size_t)32 * p->E * 2;
+    int32_t* cnt_blk = wsp<int32_t>(p, w.blk);
+    DSV4_CUDA_CHECK(launch_k(align_count_kernel, dim3(nblk), dim3(AL_THREADS), blk_smem, st, pdl, route_indices, P,
+                             a.topk, p->E, a.k_in, a.shared_e, n_tokens_dev, cnt_blk, status));
+    DSV4_CUDA_CHECK(launch_k(align_scan_kernel, dim3(1), dim3(AL_THREADS), 0, st, pdl, P, a.topk, p->E,
+                             n_tokens_dev, cnt_blk, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
+                             sorted_flat, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
+                             wsp<int4>(p, w.chunks), n_chunks, bn));
+    DSV4_CUDA_CHECK(launch_k(align_place_kernel, dim3(nblk), dim3(AL_THREADS), blk_smem, st, pdl, route_indices, P,
+                             a.topk, p->E, a.k_in, a.shared_e, route_weights, n_tokens_dev,
+                             (const int32_t*)cnt_blk, sorted_flat, inv, wsp<float>(p, w.sorted_w), status));
+  }
   mark(1);
   const int64_t rb_cap = (w.p_cap + bn - 1) / bn;   // BN-row scale blocks per k-tile
   {
