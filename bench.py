@@ -75,16 +75,64 @@ def _dist():
 # clocks
 # ---------------------------------------------------------------------------
 class Clocks:
+    """SM clock and clock-event reasons sampled DURING the timed region.
+
+    NVML is polled from a thread every 2 ms (the timed regions here last tens
+    of milliseconds, shorter than nvidia-smi's 200 ms loop); the device is
+    found by the UUID torch reports for this process's GPU.  Without NVML,
+    `nvidia-smi --query-gpu=... -lms 200` runs beside the region instead.
+    The fields are those of the nvidia-smi query: clocks.sm, clocks.max.sm
+    and the hw_slowdown / hw_thermal_slowdown / sw_thermal_slowdown /
+    sw_power_cap reasons."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.002
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.path = None
+        self.thread = None
+        self.samples = []
+        self.max_mhz = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self, h):
+        import pynvml
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), int(get_reasons(h))))
+            except Exception:
+                break
+            time.sleep(self.PERIOD_S)
 
     def start(self):
+        import threading
+        try:
+            import pynvml
+            h = self._nvml_handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, args=(h,), daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 1.0:   # the first sample precedes the region
+                time.sleep(0.001)
+            return
+        except Exception:
+            self.thread = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -94,7 +142,27 @@ class Clocks:
         except (OSError, FileNotFoundError):
             self.proc = None
 
+    def _stop_nvml(self):
+        import pynvml
+        self._stop.set()
+        self.thread.join(timeout=5)
+        rows = self.samples
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"], "source": "nvml"}
+        mx = float(self.max_mhz or max(r[0] for r in rows))
+        sm = [float(r[0]) for r in rows]
+        load = [v for v in sm if v > 0.5 * mx] or sm
+        bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({n for _, r in rows for n, b in bits.items() if r & b})
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows),
+                "source": f"nvml every {self.PERIOD_S * 1e3:.0f} ms"}
+
     def stop(self):
+        if self.thread is not None:
+            return self._stop_nvml()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -117,7 +185,8 @@ class Clocks:
         load = [s for s in sm if s > 0.5 * mx] or sm
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows),
+                "source": "nvidia-smi -lms 200"}
 
 
 # ---------------------------------------------------------------------------
