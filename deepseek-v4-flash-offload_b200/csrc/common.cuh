@@ -197,6 +197,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     }
   }
 }
+// Counters between the CTAs of one grid: a release add after the counted
+// stores, an acquire load before the dependent reads; the wait is bounded
+// like mbar_wait (DSV4_ETIMEOUT, or another wait's timeout, ends it).
+__device__ __forceinline__ void red_release_add(int* addr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool wait_count_geq(const int* addr, int target, int* status) {
+  if (ld_acquire(addr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire(addr) >= target) return true;
+    if (read_status(status) == DSV4_ETIMEOUT) return false;
+    if (globaltimer_ns() - t0 > DSV4_WAIT_NS) {
+      set_status(status, DSV4_ETIMEOUT);
+      return false;
+    }
+  }
+}
+// generic-proxy stores made visible by an acquire, then read by TMA (the
+// async proxy) in this thread
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -113,6 +113,11 @@ struct GemmParams {
   // out_bf16, so the return of the rows overlaps the GEMM tile by tile
   const int32_t* sorted_flat;
   uint16_t* const* assign_dst;
+  // fused gate/up -> down launch: the gate/up epilogue of chunk c counts its
+  // finished tiles in chunk_done[c]; a down tile of chunk c loads its
+  // activations (the h rows) once the count reaches the gate/up tiles per
+  // chunk.  Zeroed by the align of the same pass.
+  int* chunk_done;
 };
 
 __device__ __forceinline__ float warp_max_f(float v) {
@@ -132,12 +137,15 @@ struct TileInfo {
   int nrows;  // valid rows in the chunk
   int mt;     // 128-row tile of the weight matrix
   bool sh;    // the shared expert (FP8 weights)
+  int ph;     // 0: first GEMM of the launch (gate/up, or the only one); 1: down of a fused launch
+  int c;      // chunk
 };
 
 __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_tiles) {
-  TileInfo ti{-1, 0, 0, 0, false};
+  TileInfo ti{-1, 0, 0, 0, false, 0, 0};
   if (t < n_tiles) {
     const int c = t / p.a_row_tiles;
+    ti.c = c;
     const int4 ch = p.chunks[c];
     if (ch.x == p.shared_expert) {
       ti.sh = true;
@@ -150,6 +158,15 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
     ti.nrows = ch.z;
     ti.mt = t - c * p.a_row_tiles;
   }
+  return ti;
+}
+
+// Tile t of a launch: the first GEMM's tiles [0, n0), then (fused launch)
+// the down GEMM's [n0, n_all).
+__device__ __forceinline__ TileInfo load_tile2(const GemmParams& p, const GemmParams& pd, int t, int n0, int n_all) {
+  if (t < n0) return load_tile(p, t, n0);
+  TileInfo ti = load_tile(pd, t - n0, n_all - n0);
+  ti.ph = 1;
   return ti;
 }
 
@@ -183,13 +200,23 @@ __device__ __forceinline__ int b_rows_for(int nrows) {
   return nrows <= 16 ? 16 : (nrows <= 32 ? 32 : (nrows <= 64 ? 64 : BN));
 }
 
-template <int NUM_A, bool B_FP4, int EPI, int BN>
+// The tensor maps of one GEMM: weights (A), activations (B) by rows per
+// tile, and the shared expert's FP8 weights.
+struct GemmMaps {
+  CUtensorMap A, B16, B32, B64, Bwide, Ash;
+};
+
+// FUSED: one launch runs the gate/up GEMM (epilogue EPI, params p, maps m0)
+// and then the down GEMM (bf16 rows, params pd, maps m1) over the same
+// chunks; each CTA takes its gate/up tiles first, so a down tile only ever
+// waits for gate/up tiles, which never wait: no cycle, whatever the CTAs'
+// residency.  Otherwise one GEMM (p, m0; m1 and pd unused).
+template <int NUM_A, bool B_FP4, int EPI, int BN, bool FUSED>
 __global__ void __launch_bounds__(G_THREADS, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB16,
-                    const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmB64,
-                    const __grid_constant__ CUtensorMap tmBwide, const __grid_constant__ CUtensorMap tmAsh,
-                    const GemmParams p) {
+    moe_gemm_kernel(const __grid_constant__ GemmMaps m0, const __grid_constant__ GemmParams p,
+                    const __grid_constant__ GemmMaps m1, const __grid_constant__ GemmParams pd) {
   static_assert(NUM_A == 2, "operand tiles come in 256-row pairs");
+  static_assert(!FUSED || EPI != EPI_STORE_BF16, "a fused launch starts with the gate/up GEMM");
   using C = GemmCfg<NUM_A, BN, B_FP4>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -220,12 +247,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&tmA);
-    prefetch_tensormap(&tmB16);
-    prefetch_tensormap(&tmB32);
-    prefetch_tensormap(&tmB64);
-    if (BN > 64) prefetch_tensormap(&tmBwide);
-    if (!B_FP4 && p.shared_expert >= 0) prefetch_tensormap(&tmAsh);
+#pragma unroll
+    for (int g = 0; g < (FUSED ? 2 : 1); ++g) {
+      const GemmMaps& m = g ? m1 : m0;
+      prefetch_tensormap(&m.A);
+      prefetch_tensormap(&m.B16);
+      prefetch_tensormap(&m.B32);
+      prefetch_tensormap(&m.B64);
+      if (BN > 64) prefetch_tensormap(&m.Bwide);
+      if (!B_FP4 && p.shared_expert >= 0) prefetch_tensormap(&m.Ash);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, G_TMEM_COLS);
@@ -239,27 +270,34 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   // The align outputs (chunks, counts) are two kernels back and complete;
   // the activations come from the immediate predecessor: wait for it, then
   // let the next kernel start its prologue.
-  const int n_tiles = (*p.n_chunks) * p.a_row_tiles;
-  const int k_tiles = p.k_tiles;
+  const int n_chunks_all = *p.n_chunks;
+  const int n0 = n_chunks_all * p.a_row_tiles;                            // first GEMM's tiles
+  const int n_tiles = FUSED ? n0 + n_chunks_all * pd.a_row_tiles : n0;   // all tiles of the launch
   const int step = gridDim.x;
   constexpr uint32_t a_tx = 2 * G_BM * G_BK / 2;      // packed bytes of the 256-row A box
   constexpr uint32_t a_tx_sh = 2 * G_BM * G_BK;       // the shared expert's E4M3 box
+  // parameters and maps of a tile's GEMM
+  auto P = [&](const TileInfo& ti) -> const GemmParams& { return (FUSED && ti.ph) ? pd : p; };
+  auto M = [&](const TileInfo& ti) -> const GemmMaps& { return (FUSED && ti.ph) ? m1 : m0; };
+  auto tile = [&](int t) -> TileInfo { return FUSED ? load_tile2(p, pd, t, n0, n_tiles) : load_tile(p, t, n_tiles); };
   // the shared expert exists only with FP8 activations (the bf16 profile)
-  auto a_map = [&](const TileInfo& ti) -> const CUtensorMap* { return (!B_FP4 && ti.sh) ? &tmAsh : &tmA; };
+  auto a_map = [&](const TileInfo& ti) -> const CUtensorMap* { return (!B_FP4 && ti.sh) ? &M(ti).Ash : &M(ti).A; };
   auto a_bytes = [&](const TileInfo& ti) -> uint32_t { return (!B_FP4 && ti.sh) ? a_tx_sh : a_tx; };
   auto a_sf = [&](const TileInfo& ti) -> const uint8_t* {
-    return (!B_FP4 && ti.sh) ? p.shared_slot + p.shared_sfa_off
-                             : p.arena + (int64_t)ti.slot * p.slot_bytes + p.sfa_off;
+    const GemmParams& q = P(ti);
+    return (!B_FP4 && ti.sh) ? q.shared_slot + q.shared_sfa_off
+                             : q.arena + (int64_t)ti.slot * q.slot_bytes + q.sfa_off;
   };
   // The weights do not depend on the predecessor kernel: the producer puts
   // the first tile's first ring stages of weights and weight scales in
   // flight before it waits; that tile's activations follow after the wait.
   int pre = 0;
   if (warp == 0 && lane == 0) {
-    const TileInfo first = load_tile(p, blockIdx.x, n_tiles);
+    const TileInfo first = tile(blockIdx.x);
     if (first.slot >= 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint8_t* sf_base = a_sf(first);
+      const int k_tiles = P(first).k_tiles;
       const uint32_t b_tx = (uint32_t)b_rows_for<BN>(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
       pre = k_tiles < C::STAGES ? k_tiles : C::STAGES;
       for (int kt = 0; kt < pre; ++kt) {   // stage kt, first phase: the ring is empty
@@ -283,21 +321,33 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+      TileInfo cur = tile(blockIdx.x);
       for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
-        const TileInfo nxt = load_tile(p, t + step, n_tiles);
+        const TileInfo nxt = tile(t + step);
         if (cur.slot < 0) {
           set_status(p.status, DSV4_ENOTFOUND);
           cur = nxt;
           continue;
         }
+        const GemmParams& q = P(cur);
+        const GemmMaps& m = M(cur);
+        const int k_tiles = q.k_tiles;
         const uint8_t* sf_base = a_sf(cur);
         const CUtensorMap* mA = a_map(cur);
         const uint32_t atx = a_bytes(cur);
-        const uint8_t* sfb_base = p.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
+        const uint8_t* sfb_base = q.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
         const int nb = b_rows_for<BN>(cur.nrows);
-        const CUtensorMap* mB = nb == 16 ? &tmB16 : (nb == 32 ? &tmB32 : (nb == 64 ? &tmB64 : &tmBwide));
+        const CUtensorMap* mB = nb == 16 ? &m.B16 : (nb == 32 ? &m.B32 : (nb == 64 ? &m.B64 : &m.Bwide));
         const int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
+        if (FUSED && cur.ph) {
+          // the h rows of this chunk come from the gate/up tiles of other
+          // CTAs: wait until all of them have stored theirs
+          if (!wait_count_geq(p.chunk_done + cur.c, p.a_row_tiles, p.status)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();   // the TMA reads below see those stores
+        }
         for (int kt = 0; kt < k_tiles; ++kt) {
           uint8_t* st = smem + stage * C::STAGE_BYTES;
           uint8_t* sA = st;                        // 256 rows: A0 then A1
@@ -317,7 +367,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           tma_load_2d(sB, mB, &full[stage], kt * C::ROW_BYTES, cur.row0, pol_x);
           // B scales: the atom of (k-tile kt, this 64-row chunk), already in tensor-core order
-          bulk_load(sSFB, sfb_base + (int64_t)kt * p.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
+          bulk_load(sSFB, sfb_base + (int64_t)kt * q.rb_cap * C::SF_BYTES, C::SF_BYTES, &full[stage], pol_x);
           mbar_arrive(&full[stage]);
           ++issued;
           if (++stage == C::STAGES) {
@@ -355,15 +405,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       // each issuer copies the scales it reads into its own TMEM columns:
       // tcgen05 operations of different threads are not ordered
       const uint32_t sfa = tmem + C::SF_COL + 8 * half, sfb = tmem + C::SF_COL + 8 * half + 4;
-      TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+      TileInfo cur = tile(blockIdx.x);
       for (int t = blockIdx.x; t < n_tiles && ok; t += step) {
-        const TileInfo nxt = load_tile(p, t + step, n_tiles);
+        const TileInfo nxt = tile(t + step);
         if (cur.slot < 0) {
           cur = nxt;
           continue;
         }
         const int nb = b_rows_for<BN>(cur.nrows);
         const bool a_e4m3 = !B_FP4 && cur.sh;
+        const int k_tiles = P(cur).k_tiles;
         cur = nxt;
         if (!mbar_wait(&accempty[abuf], aphase ^ 1u, p.status)) break;
         tc_fence_after();
@@ -450,16 +501,19 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
       }
     };
-    TileInfo cur = load_tile(p, blockIdx.x, n_tiles);
+    TileInfo cur = tile(blockIdx.x);
     for (int t = blockIdx.x; t < n_tiles; t += step) {
-      const TileInfo nxt = load_tile(p, t + step, n_tiles);
+      const TileInfo nxt = tile(t + step);
       if (cur.slot < 0) {
         cur = nxt;
         continue;
       }
-      const int row0 = cur.row0, nrows = cur.nrows, mt = cur.mt;
+      const int row0 = cur.row0, nrows = cur.nrows, mt = cur.mt, chunk = cur.c;
+      // bf16 rows out: the down GEMM (alone, or the second half of a fused launch)
+      const bool store_tile = EPI == EPI_STORE_BF16 || (FUSED && cur.ph);
+      const GemmParams& gq = P(cur);
       cur = nxt;
-      load_w(row0, c0);
+      if (!store_tile) load_w(row0, c0);
       // all epilogue warps take the same decision: a failed wait in any of
       // them ends the loop for all (the named barriers below need all 8)
       if (!mbar_wait(&accfull[abuf], aphase, p.status) && lane == 0) atomicOr(epi_fail, 1);
@@ -472,7 +526,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       for (int sub = 0; sub < NPASS; ++sub) {
         const int cs = c0 + sub * SUB;   // first column of this pass
         const int width = HALF - sub * SUB < SUB ? HALF - sub * SUB : SUB;   // 32, or 24 (BN = 112)
-        if (sub > 0) load_w(row0, cs);
+        if (sub > 0 && !store_tile) load_w(row0, cs);
         float acc0[SUB];
         float acc1[NUM_A == 2 ? SUB : 1];
         (void)acc1;
@@ -500,40 +554,40 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if (lane == 0) mbar_arrive(&accempty[abuf]);
         }
 
-        if constexpr (EPI == EPI_STORE_BF16) {
+        if (store_tile) {
           // rows 0..127 of the pair -> acc0, rows 128..255 -> acc1
-          if (p.assign_dst) {
+          if (gq.assign_dst) {
             // scatter: lane L fetches the destination of column cs+L, then
             // every column's row is stored where it belongs (plain stores,
             // 64 contiguous bytes per warp and column)
             uint16_t* mine = nullptr;
             if (lane < width && cs + lane < nrows) {
-              const int a = p.sorted_flat[row0 + cs + lane];
-              mine = a >= 0 ? p.assign_dst[a] : nullptr;
+              const int a = gq.sorted_flat[row0 + cs + lane];
+              mine = a >= 0 ? gq.assign_dst[a] : nullptr;
             }
             const unsigned long long mv = reinterpret_cast<unsigned long long>(mine);
 #pragma unroll
             for (int n = 0; n < SUB; ++n) {
               const unsigned long long b = __shfl_sync(0xffffffffu, mv, n);
               if (b) {
-                uint16_t* dst = reinterpret_cast<uint16_t*>(b) + mt * p.out_tile_cols + i;
+                uint16_t* dst = reinterpret_cast<uint16_t*>(b) + mt * gq.out_tile_cols + i;
                 dst[0] = bf16_bits(acc0[n]);
                 if constexpr (NUM_A == 2) dst[G_BM] = bf16_bits(acc1[n]);
               }
             }
           } else {
-            uint16_t* dst = p.out_bf16 + (int64_t)(row0 + cs) * p.out_ld + mt * p.out_tile_cols + i;
+            uint16_t* dst = gq.out_bf16 + (int64_t)(row0 + cs) * gq.out_ld + mt * gq.out_tile_cols + i;
 #pragma unroll
             for (int n = 0; n < SUB; ++n)
-              if (n < width && cs + n < nrows) dst[(int64_t)n * p.out_ld] = bf16_bits(acc0[n]);
+              if (n < width && cs + n < nrows) dst[(int64_t)n * gq.out_ld] = bf16_bits(acc0[n]);
             if constexpr (NUM_A == 2) {
               uint16_t* dst1 = dst + G_BM;
 #pragma unroll
               for (int n = 0; n < SUB; ++n)
-                if (n < width && cs + n < nrows) dst1[(int64_t)n * p.out_ld] = bf16_bits(acc1[n]);
+                if (n < width && cs + n < nrows) dst1[(int64_t)n * gq.out_ld] = bf16_bits(acc1[n]);
             }
           }
-        } else {
+        } else if constexpr (EPI != EPI_STORE_BF16) {
           // gate = bf16(w1 x), up = bf16(w3 x); clamp; h = silu(gate)*up*w_route;
           // bf16(h) is the input of the activation re-quantisation.
           const float lim = p.swiglu_limit;
@@ -612,6 +666,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
         }
       }
+      if (FUSED && !store_tile) {
+        // this gate/up tile's h columns and scales are stored: count it for
+        // the down tiles of its chunk (stores, fence, barrier, then one add)
+        __threadfence();
+        named_bar_sync(1, 32 * G_EPI_WARPS);
+        if (warp == 2 && lane == 0) red_release_add(p.chunk_done + chunk, 1);
+      }
       if (++abuf == C::ACC_BUFS) {
         abuf = 0;
         aphase ^= 1u;
@@ -621,7 +682,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
   // scatter mode: the rows stored to other GPUs are visible system-wide
   // before this grid completes and a later kernel publishes them
-  if (EPI == EPI_STORE_BF16 && p.assign_dst) __threadfence_system();
+  if ((EPI == EPI_STORE_BF16 && p.assign_dst) || (FUSED && pd.assign_dst)) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

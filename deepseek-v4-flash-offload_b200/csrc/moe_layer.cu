@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                      int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
                      float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
-                     int pad, int* status, const int32_t* __restrict__ n_tokens_dev, int k_in, int shared_e) {
+                     int pad, int* status, const int32_t* __restrict__ n_tokens_dev, int k_in, int shared_e,
+                     int* __restrict__ chunk_done, int max_chunks) {
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   const int ebits = 32 - __clz(max(E - 1, 1));   // bits of the largest expert id
   griddep_wait();
   griddep_launch();
+  for (int j = tid; j < max_chunks; j += AL_THREADS) chunk_done[j] = 0;
   // a token count known only on the device (rows received by expert
   // parallelism): the first n tokens of the buffers
   if (n_tokens_dev) P = min(P, max(0, *n_tokens_dev) * topk);
@@ -412,7 +414,8 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     align_scan_kernel(int P, int topk, int E, const int32_t* __restrict__ n_tokens_dev, int32_t* __restrict__ cnt_blk,
                       int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                       int32_t* __restrict__ active, int32_t* __restrict__ n_active, float* __restrict__ sorted_w,
-                      int4* __restrict__ chunks, int32_t* __restrict__ n_chunks, int pad) {
+                      int4* __restrict__ chunks, int32_t* __restrict__ n_chunks, int pad,
+                      int* __restrict__ chunk_done, int max_chunks) {
   __shared__ int scratch[96];
   __shared__ int run_s[1024], cnt_s[1024];
   griddep_wait();
@@ -420,6 +423,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   P = align_count_p(P, topk, n_tokens_dev);
   const int nblk = (P + AL_THREADS - 1) / AL_THREADS;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int j = tid; j < max_chunks; j += AL_THREADS) chunk_done[j] = 0;
   int c = 0;
   if (tid < E) {
     for (int b = 0; b < nblk; ++b) {
@@ -710,9 +714,15 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const
   return DSV4_OK;
 }
 
+// DSV4_FUSED_FFN=1 runs the gate/up and down GEMMs as one launch.
+static bool fused_ffn_default() {
+  const char* e = getenv("DSV4_FUSED_FFN");
+  return e && e[0] == '1';
+}
+
 struct WsLayout {
   int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
-  int64_t xq, xsf, hq, hsf, out, ys, blk, bytes;
+  int64_t xq, xsf, hq, hsf, out, ys, blk, done, bytes;
   int64_t p_max, p_cap, max_chunks;
 };
 
@@ -751,6 +761,7 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   w.out = take(2 * w.p_cap * H);
   w.ys = shared ? take(2 * max_tokens * H) : 0;
   w.blk = take(4 * E * ((w.p_max + AL_THREADS - 1) / AL_THREADS + 1));   // per-block counts of the large align
+  w.done = take(4 * w.max_chunks);   // finished gate/up tiles per chunk (fused launch)
   w.bytes = o;
   return w;
 }
@@ -774,6 +785,7 @@ struct dsv4_moe_plan {
   CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 112 activation rows per box
   bool timing = false;
   int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
+  bool fused_ffn = false;  // gate/up and down GEMMs in one launch
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -804,12 +816,20 @@ extern "C" int64_t dsv4_moe_workspace_bytes(int32_t hidden, int32_t inter, int32
 // the current device every time a plan is created.
 template <int NUM_A, bool B_FP4, int EPI>
 static int prepare_gemm() {
-  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64>,
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GemmCfg<NUM_A, 64, B_FP4>::SMEM_BYTES));
-  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 112>,
+  DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 112, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GemmCfg<NUM_A, 112, B_FP4>::SMEM_BYTES));
+  if constexpr (EPI != EPI_STORE_BF16) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 64, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmCfg<NUM_A, 64, B_FP4>::SMEM_BYTES));
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NUM_A, B_FP4, EPI, 112, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmCfg<NUM_A, 112, B_FP4>::SMEM_BYTES));
+  }
   return DSV4_OK;
 }
 
@@ -832,15 +852,28 @@ static int gemm_bn(int plan_bn, int64_t assignments, int n_experts, bool packed)
   return assignments >= (packed ? 16 : 32) * (int64_t)n_experts ? 112 : 64;
 }
 
-template <bool B_FP4, int EPI>
-static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, const CUtensorMap& tmA,
-                               const CUtensorMap* tmB, const CUtensorMap& tmAsh, const GemmParams& g) {
+static GemmMaps gemm_maps(int bn, const CUtensorMap& tmA, const CUtensorMap* tmB, const CUtensorMap& tmAsh) {
+  GemmMaps m;
+  m.A = tmA;
+  m.B16 = tmB[0];
+  m.B32 = tmB[1];
+  m.B64 = tmB[2];
+  m.Bwide = bn == 112 ? tmB[3] : tmB[2];
+  m.Ash = tmAsh;
+  return m;
+}
+
+// One GEMM (m0, g0; m1 and g1 unused copies), or with FUSED the gate/up
+// GEMM (m0, g0) and the down GEMM (m1, g1) in one launch.
+template <bool B_FP4, int EPI, bool FUSED>
+static cudaError_t launch_gemm(int bn, cudaStream_t st, bool pdl, int num_sms, const GemmMaps& m0,
+                               const GemmParams& g0, const GemmMaps& m1, const GemmParams& g1) {
   const dim3 grid(num_sms), block(G_THREADS);
   if (bn == 112)
-    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112>, grid, block, GemmCfg<2, 112, B_FP4>::SMEM_BYTES, st, pdl, tmA,
-                    tmB[0], tmB[1], tmB[2], tmB[3], tmAsh, g);
-  return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64>, grid, block, GemmCfg<2, 64, B_FP4>::SMEM_BYTES, st, pdl, tmA,
-                  tmB[0], tmB[1], tmB[2], tmB[2], tmAsh, g);
+    return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 112, FUSED>, grid, block, GemmCfg<2, 112, B_FP4>::SMEM_BYTES, st,
+                    pdl, m0, g0, m1, g1);
+  return launch_k(moe_gemm_kernel<2, B_FP4, EPI, 64, FUSED>, grid, block, GemmCfg<2, 64, B_FP4>::SMEM_BYTES, st, pdl,
+                  m0, g0, m1, g1);
 }
 
 // Tensor maps of the shared expert's FP8 slot (w13 and w2 blocks, UINT8,
@@ -892,6 +925,7 @@ extern "C" int dsv4_moe_plan_create_ex(dsv4_moe_plan** out, int32_t hidden, int3
   p->shared = sh != 0;
   p->max_tokens = max_tokens;
   p->swiglu_limit = swiglu_limit;
+  p->fused_ffn = fused_ffn_default();
   p->arena = slot_arena;
   p->n_slots = n_slots;
   p->slot = slot_layout(hidden, inter);
@@ -1007,7 +1041,8 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
     DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P,
                              a.topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
                              sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                             wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e));
+                             wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e,
+                             wsp<int>(p, w.done), (int)w.max_chunks));
   } else {
     // large batches: count per block, scan on one CTA, place per block
     const unsigned nblk = (unsigned)((P + AL_THREADS - 1) / AL_THREADS);
@@ -1018,7 +1053,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
     DSV4_CUDA_CHECK(launch_k(align_scan_kernel, dim3(1), dim3(AL_THREADS), 0, st, pdl, P, a.topk, p->E,
                              n_tokens_dev, cnt_blk, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
                              sorted_flat, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                             wsp<int4>(p, w.chunks), n_chunks, bn));
+                             wsp<int4>(p, w.chunks), n_chunks, bn, wsp<int>(p, w.done), (int)w.max_chunks));
     DSV4_CUDA_CHECK(launch_k(align_place_kernel, dim3(nblk), dim3(AL_THREADS), blk_smem, st, pdl, route_indices, P,
                              a.topk, p->E, a.k_in, a.shared_e, route_weights, n_tokens_dev,
                              (const int32_t*)cnt_blk, sorted_flat, inv, wsp<float>(p, w.sorted_w), status));
@@ -1053,6 +1088,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   g1.out_ld = p->I;
   g1.swiglu_limit = p->swiglu_limit;
   g1.status = status;
+  g1.chunk_done = wsp<int>(p, w.done);
   g1.shared_expert = a.shared_e;
   g1.shared_slot = a.shared_slot;
   const SlotLayout sl = shared_slot_layout(p->H, p->I);
@@ -1074,15 +1110,27 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   // valid map fills the parameter
   const CUtensorMap& sh13 = a.sh13 ? *a.sh13 : p->tmA13;
   const CUtensorMap& sh2 = a.sh2 ? *a.sh2 : p->tmA2;
-  if (a.fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4>(bn, st, pdl, p->num_sms, p->tmA13p, p->tmB1_fp4, sh13, g1)));
-  else
-    DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8>(bn, st, pdl, p->num_sms, p->tmA13, p->tmB1_fp8, sh13, g1)));
-  mark(3);
-  if (a.fp4)
-    DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2p, p->tmB2_fp4, sh2, g2)));
-  else
-    DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16>(bn, st, pdl, p->num_sms, p->tmA2, p->tmB2_fp8, sh2, g2)));
+  const GemmMaps m1 = a.fp4 ? gemm_maps(bn, p->tmA13p, p->tmB1_fp4, sh13) : gemm_maps(bn, p->tmA13, p->tmB1_fp8, sh13);
+  const GemmMaps m2 = a.fp4 ? gemm_maps(bn, p->tmA2p, p->tmB2_fp4, sh2) : gemm_maps(bn, p->tmA2, p->tmB2_fp8, sh2);
+  if (p->fused_ffn) {
+    // gate/up, SwiGLU, requant and down in one persistent launch; the
+    // stage events put its whole time under the gate/up stage
+    if (a.fp4)
+      DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4, true>(bn, st, pdl, p->num_sms, m1, g1, m2, g2)));
+    else
+      DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8, true>(bn, st, pdl, p->num_sms, m1, g1, m2, g2)));
+    mark(3);
+  } else {
+    if (a.fp4)
+      DSV4_CUDA_CHECK((launch_gemm<true, EPI_SWIGLU_MXFP4, false>(bn, st, pdl, p->num_sms, m1, g1, m1, g1)));
+    else
+      DSV4_CUDA_CHECK((launch_gemm<false, EPI_SWIGLU_FP8, false>(bn, st, pdl, p->num_sms, m1, g1, m1, g1)));
+    mark(3);
+    if (a.fp4)
+      DSV4_CUDA_CHECK((launch_gemm<true, EPI_STORE_BF16, false>(bn, st, pdl, p->num_sms, m2, g2, m2, g2)));
+    else
+      DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16, false>(bn, st, pdl, p->num_sms, m2, g2, m2, g2)));
+  }
   mark(4);
   if (y_bf16) {
     const int threads = std::min(128, p->H / 8);
@@ -1209,6 +1257,13 @@ extern "C" int dsv4_moe_set_gemm_tile(dsv4_moe_plan* p, int32_t tokens_per_tile)
   DSV4_API_END
 }
 
+extern "C" int dsv4_moe_set_ffn_fusion(dsv4_moe_plan* p, int32_t enable) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p, "null plan");
+  p->fused_ffn = enable != 0;
+  DSV4_API_END
+}
+
 extern "C" int dsv4_moe_stage_times(dsv4_moe_plan* p, float* ms, int32_t n) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(p && ms, "null pointer");
@@ -1262,7 +1317,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
       indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1);
+      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }

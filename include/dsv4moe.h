@@ -244,6 +244,14 @@ int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
  * DSV4_GEMM_BN overrides it).  The tile is also the padding of each expert's row group.
  * Takes effect from the next dsv4_moe_forward on the plan. */
 int dsv4_moe_set_gemm_tile(dsv4_moe_plan* plan, int32_t tokens_per_tile);
+/* Gate/up and down GEMMs in one launch (1) or as two launches (0, the
+ * default; the environment variable DSV4_FUSED_FFN=1 changes the default).
+ * The fused launch stores the h rows of each expert chunk and starts that
+ * chunk's down tiles as soon as all of its gate/up tiles are stored; results
+ * are identical.  With stage timing on, the fused launch's time is reported
+ * as the gate/up stage and the down stage is empty.
+ * No counterpart in the reference (npu_grouped_matmul runs per projection). */
+int dsv4_moe_set_ffn_fusion(dsv4_moe_plan* plan, int32_t enable);
 /* Device pointers of the plan's align outputs (valid after a forward):
  * counts[E], offsets[E+1], sorted_flat[P], inv[P], active[E], n_active[1]. */
 int dsv4_moe_debug_align(dsv4_moe_plan* plan, int32_t** counts, int32_t** offsets, int32_t** sorted_flat,

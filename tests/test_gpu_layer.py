@@ -78,6 +78,38 @@ def test_plugin_forward_cfg1_matches_oracle(dev, T):
     assert np.array_equal(_sets(gi_.cpu().numpy()), _sets(idx))
 
 
+@pytest.mark.parametrize("T", [1, 64, 512])
+def test_fused_ffn_launch_equals_two_launches(dev, T):
+    """Gate/up, SwiGLU, requant and down in one persistent launch (down
+    tiles start per chunk once its h rows are stored) give the same bits as
+    the two-launch path, in both profiles; T=512 (4096 assignments) also
+    takes the multi-CTA align.  T=1 is checked against the oracle too."""
+    cfg = S.CFG1
+    x = S.make_tokens(cfg, 23, T)
+    w, idx = _route_oracle(cfg, x)
+    need = sorted(set(idx.reshape(-1).tolist()))
+    experts = {e: S.make_expert(cfg, 0, e, LAYER) for e in need}
+    moe, eng = make_plugin_layer(cfg, experts, dev, layer_idx=LAYER)
+    xt = bf16_tensor(x)
+    plan = eng.plan_for(cfg.n_experts, cfg.topk, T, cfg.swiglu_limit)
+    try:
+        for flag, profile in ((False, "bf16"), (True, "a4w4")):
+            _profile(flag)
+            plan.set_ffn_fusion(True)
+            y_fused = moe.forward(xt).clone()
+            plan.set_ffn_fusion(False)
+            y_two = moe.forward(xt).clone()
+            torch.cuda.synchronize()
+            plan.status()
+            assert torch.equal(y_fused, y_two), profile
+            if T == 1:
+                ref = O.moe_routed(x, w, idx, experts, cfg.n_experts, cfg.swiglu_limit, profile)
+                assert rel_err(bf16_to_np(y_fused), ref) <= TOL, profile
+    finally:
+        _profile(False)
+        plan.set_ffn_fusion(True)
+
+
 def test_plugin_forward_cfg2_a4w4_prefill(dev):
     cfg = S.CFG1           # config 2 shares config 1's dims and router
     T = 2048
