@@ -275,12 +275,15 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+TRAFFIC_PROFILE = "moe_ffn_fused_cfg1_t64_bf16.md"
+
+
 def _traffic():
-    """Per-launch DRAM bytes (read + write) of the gate/up GEMM from the
+    """Per-launch DRAM bytes (read + write) of the fused FFN launch from the
     committed ncu summary, with the algorithmic bytes of that same launch."""
     out = {}
     try:
-        with open(os.path.join(ROOT, "profiles", "moe_gemm_cfg1_t64_bf16.md")) as f:
+        with open(os.path.join(ROOT, "profiles", TRAFFIC_PROFILE)) as f:
             for line in f:
                 k, sep, v = line.partition(":")
                 if sep and k.strip() in ("dram_bytes_per_launch", "algorithmic_bytes_per_launch"):
@@ -374,36 +377,52 @@ def run_ours(a):
     value = T * a.steps / (tot_ms / 1e3)
 
     # per-kernel device times of the same steps, run eagerly with CUDA events
-    # between the stages (on the launching stream)
+    # between the stages (on the launching stream): the product's fused
+    # gate/up -> down launch (its time is the gate/up stage), then the two
+    # GEMMs as separate launches for the per-GEMM split
     plan.enable_timing(True)
     device_steps(2, dev, record=False)
     eager_ms, stages, ds = device_steps(a.steps, dev)
+    plan.set_ffn_fusion(False)
+    device_steps(2, dev, record=False)
+    _, stages2, ds2 = device_steps(a.steps, dev)
+    plan.set_ffn_fusion(None)
     plan.enable_timing(False)
 
-    # roofline of the gate/up GEMM and of the whole layer
+    # rooflines: the fused FFN launch (headline), each GEMM alone, the layer
     hbm, peak_kind = _peaks()
     P = T * _cfg().topk
-    g1_ms = sum(s["gate_up_gemm"] for s in stages)
-    g2_ms = sum(s["down_gemm"] for s in stages)
-    g1_bytes = sum(_gemm_bytes(d, P, "gate_up") for d in ds)
-    g2_bytes = sum(_gemm_bytes(d, P, "down") for d in ds)
+    ffn_ms = sum(s["gate_up_gemm"] + s["down_gemm"] for s in stages)
+    ffn_bytes = sum(_gemm_bytes(d, P, "gate_up") + _gemm_bytes(d, P, "down") for d in ds)
+    g1_ms = sum(s["gate_up_gemm"] for s in stages2)
+    g2_ms = sum(s["down_gemm"] for s in stages2)
+    g1_bytes = sum(_gemm_bytes(d, P, "gate_up") for d in ds2)
+    g2_bytes = sum(_gemm_bytes(d, P, "down") for d in ds2)
+    ach = ffn_bytes / (ffn_ms / 1e3) / 1e9
     ach1 = g1_bytes / (g1_ms / 1e3) / 1e9
     ach2 = g2_bytes / (g2_ms / 1e3) / 1e9
     lay = sum(_layer_bytes(d, T) for d in ds) / (tot_ms / 1e3) / 1e9
     traffic = _traffic()
-    roofline = {"bound": "hbm", "kernel": "moe_gemm_kernel<2,false,0> (gate/up, bf16 profile)",
-                "achieved": round(ach1, 1), "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
-                "unit": "GB/s", "frac": round(ach1 / hbm, 4),
+    roofline = {"bound": "hbm",
+                "kernel": "moe_gemm_kernel<2,false,SWIGLU_FP8,64,FUSED> (gate/up + SwiGLU + FP8 requant + down in "
+                          "one launch, bf16 profile)",
+                "achieved": round(ach, 1), "peak": hbm, "peak_kind": f"{peak_kind} HBM copy",
+                "unit": "GB/s", "frac": round(ach / hbm, 4),
                 "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
-                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch "
-                                   "(token batch 0, profiles/moe_gemm_cfg1_t64_bf16.md); algorithmic bytes of "
-                                   f"that launch: {traffic.get('algorithmic_bytes_per_launch')}") if traffic else None,
-                "algorithmic_bytes_per_launch": round(g1_bytes / len(ds)),
-                "launch_ms": round(g1_ms / len(ds), 5)}
+                "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused launch "
+                                   f"(token batch 0, profiles/{TRAFFIC_PROFILE}); algorithmic bytes of that "
+                                   f"launch: {traffic.get('algorithmic_bytes_per_launch')}") if traffic else None,
+                "algorithmic_bytes_per_launch": round(ffn_bytes / len(ds)),
+                "launch_ms": round(ffn_ms / len(ds), 5)}
     detail = {"active_experts_mean": round(statistics.mean(ds), 2),
               "eager_ms_per_step": round(eager_ms / a.steps, 5),
               "stage_ms_mean": {k: round(statistics.mean(s[k] for s in stages), 5) for k in stages[0]},
-              "down_gemm_roofline": {"achieved": round(ach2, 1), "frac": round(ach2 / hbm, 4)},
+              "stage_ms_mean_two_gemm_launches": {k: round(statistics.mean(s[k] for s in stages2), 5)
+                                                  for k in stages2[0]},
+              "gate_up_gemm_roofline": {"achieved": round(ach1, 1), "frac": round(ach1 / hbm, 4),
+                                        "launch_ms": round(g1_ms / len(ds2), 5)},
+              "down_gemm_roofline": {"achieved": round(ach2, 1), "frac": round(ach2 / hbm, 4),
+                                     "launch_ms": round(g2_ms / len(ds2), 5)},
               "layer_roofline": {"achieved": round(lay, 1), "frac": round(lay / hbm, 4),
                                  "bytes": "D*13369344 + gate fp32 + x/y"}}
 
@@ -446,11 +465,21 @@ def run_ours(a):
             tt = graph_steps(gt, xst, dv, n)
             plan.enable_timing(True)
             _, st, dd = device_steps(n, dv)
+            plan.set_ffn_fusion(False)
+            _, st2, dd2 = device_steps(n, dv)
+            plan.set_ffn_fusion(None)
             plan.enable_timing(False)
+            pt = t * _cfg().topk
             per_t[str(t)] = {"tok_s": round(t * n / (tt / 1e3), 1), "ms": round(tt / n, 5),
                              "active_experts": round(statistics.mean(dd), 1),
-                             "gate_up_frac": round(sum(_gemm_bytes(d, t * 8, "gate_up") for d in dd) /
-                                                   (sum(x["gate_up_gemm"] for x in st) / 1e3) / 1e9 / hbm, 4)}
+                             "ffn_frac": round(sum(_gemm_bytes(d, pt, "gate_up") + _gemm_bytes(d, pt, "down")
+                                                   for d in dd) /
+                                               (sum(x["gate_up_gemm"] + x["down_gemm"] for x in st) / 1e3) / 1e9 /
+                                               hbm, 4),
+                             "gate_up_frac": round(sum(_gemm_bytes(d, pt, "gate_up") for d in dd2) /
+                                                   (sum(x["gate_up_gemm"] for x in st2) / 1e3) / 1e9 / hbm, 4),
+                             "down_frac": round(sum(_gemm_bytes(d, pt, "down") for d in dd2) /
+                                                (sum(x["down_gemm"] for x in st2) / 1e3) / 1e9 / hbm, 4)}
             del gt
         detail["decode_T"] = per_t
     plan.status()
@@ -465,7 +494,9 @@ def run_ours(a):
                        "parallelism": "single GPU",
                        "l2": "256 MiB flush before every timed step; 8 rotating token batches"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": 7 * a.steps, "launch_mode": "CUDA graph replay per step (7 kernels)",
+            "gpu_launches": 6 * a.steps,
+            "launch_mode": "CUDA graph replay per step (6 kernels: router logits, top-k, align, quantise-gather, "
+                           "fused gate/up -> down, combine)",
             "detail": detail}
     if not a.no_detail:
         # the other BASELINE configurations on this GPU, after the headline's
@@ -647,7 +678,9 @@ def run_prefill(a):
                          "gate_up_frac": round(g1_bound / sm["gate_up_gemm"], 4)},
             "e2e": {"value": round(T * a.steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
-            "clocks": clocks, "gpu_launches": 7 * a.steps,
+            "clocks": clocks, "gpu_launches": 10 * a.steps,
+            "launch_mode": "CUDA graph replay per step (10 kernels: gate split, tensor-core router logits, top-k, "
+                           "align count / scan / place, quantise-gather, gate/up, down, combine)",
             "detail": {"active_experts_mean": round(d, 1), "stage_ms_mean": sm}}
     print(json.dumps(line), flush=True)
 
@@ -1260,7 +1293,10 @@ def run_ep(a, rank, world, device):
                        "l2": "256 MiB flush before every timed step"},
             "e2e": {"value": bf["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": CFG4_TOKENS * h * 2,
                     "d2h_bytes_per_step": CFG4_TOKENS * h * 2},
-            "clocks": clocks, "gpu_launches": 9 * a.steps,
+            "clocks": clocks, "gpu_launches": 17 * a.steps,
+            "launch_mode": "CUDA graph replay per step (17 kernels: router 3, dispatch 5 (index, count wait, rows, "
+                           "rows wait, return targets), align 3, quantise-gather, gate/up, down with the return "
+                           "in its epilogue, publish + wait, ordered combine)",
             "detail": {"profiles": r, "same_workload_on_1_gpu": one,
                        "strong_scaling_vs_1_gpu": scal,
                        "note": "the N=1 line of bench.py is BASELINE config 1 (decode, T=64); this line's base "

@@ -714,10 +714,16 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, void* base, const
   return DSV4_OK;
 }
 
-// DSV4_FUSED_FFN=1 runs the gate/up and down GEMMs as one launch.
-static bool fused_ffn_default() {
+// Gate/up and down GEMMs in one launch: 1 always, 0 never, -1 (default)
+// with the 64-token decode tile only.  Measured on config 1 / 2 (graph
+// replay): equal to the two PDL-chained launches at T = 1-64, 2.5 % slower
+// at the 112-token prefill tile, whose SwiGLU epilogue is the longest role.
+// DSV4_FUSED_FFN=0|1 overrides the default.
+static int fused_ffn_default() {
   const char* e = getenv("DSV4_FUSED_FFN");
-  return e && e[0] == '1';
+  if (e && e[0] == '0') return 0;
+  if (e && e[0] == '1') return 1;
+  return -1;
 }
 
 struct WsLayout {
@@ -785,7 +791,7 @@ struct dsv4_moe_plan {
   CUtensorMap tmB1_fp8[4], tmB1_fp4[4], tmB2_fp8[4], tmB2_fp4[4];  // 16, 32, 64, 112 activation rows per box
   bool timing = false;
   int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
-  bool fused_ffn = false;  // gate/up and down GEMMs in one launch
+  int fused_ffn = -1;   // gate/up and down GEMMs in one launch: 1, 0, -1 = with the 64-token tile
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -1112,7 +1118,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   const CUtensorMap& sh2 = a.sh2 ? *a.sh2 : p->tmA2;
   const GemmMaps m1 = a.fp4 ? gemm_maps(bn, p->tmA13p, p->tmB1_fp4, sh13) : gemm_maps(bn, p->tmA13, p->tmB1_fp8, sh13);
   const GemmMaps m2 = a.fp4 ? gemm_maps(bn, p->tmA2p, p->tmB2_fp4, sh2) : gemm_maps(bn, p->tmA2, p->tmB2_fp8, sh2);
-  if (p->fused_ffn) {
+  if (p->fused_ffn == 1 || (p->fused_ffn < 0 && bn == 64)) {
     // gate/up, SwiGLU, requant and down in one persistent launch; the
     // stage events put its whole time under the gate/up stage
     if (a.fp4)
@@ -1260,7 +1266,8 @@ extern "C" int dsv4_moe_set_gemm_tile(dsv4_moe_plan* p, int32_t tokens_per_tile)
 extern "C" int dsv4_moe_set_ffn_fusion(dsv4_moe_plan* p, int32_t enable) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(p, "null plan");
-  p->fused_ffn = enable != 0;
+  DSV4_CHECK_ARG(enable >= -1 && enable <= 1, "enable must be -1, 0 or 1");
+  p->fused_ffn = enable;
   DSV4_API_END
 }
 

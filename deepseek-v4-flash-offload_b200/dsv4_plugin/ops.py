@@ -358,9 +358,10 @@ class MoEPlan:
         """Tokens per GEMM tile: 64, 112, or 0 for the library default."""
         check(lib().dsv4_moe_set_gemm_tile(self._h, int(tokens_per_tile)))
 
-    def set_ffn_fusion(self, enable: bool = True) -> None:
-        """Gate/up and down GEMMs in one launch (default) or two."""
-        check(lib().dsv4_moe_set_ffn_fusion(self._h, int(bool(enable))))
+    def set_ffn_fusion(self, enable=None) -> None:
+        """Gate/up and down GEMMs in one launch (True), two (False), or the
+        library's choice (None: one launch with the decode tile)."""
+        check(lib().dsv4_moe_set_ffn_fusion(self._h, -1 if enable is None else int(bool(enable))))
 
     def enable_timing(self, enable: bool = True) -> None:
         check(lib().dsv4_moe_enable_timing(self._h, int(bool(enable))))

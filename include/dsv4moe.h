@@ -244,8 +244,10 @@ int dsv4_moe_stage_times(dsv4_moe_plan* plan, float* ms_out, int32_t n);
  * DSV4_GEMM_BN overrides it).  The tile is also the padding of each expert's row group.
  * Takes effect from the next dsv4_moe_forward on the plan. */
 int dsv4_moe_set_gemm_tile(dsv4_moe_plan* plan, int32_t tokens_per_tile);
-/* Gate/up and down GEMMs in one launch (1) or as two launches (0, the
- * default; the environment variable DSV4_FUSED_FFN=1 changes the default).
+/* Gate/up and down GEMMs in one launch (1), as two launches (0), or the
+ * library's choice (-1, the default: one launch with the 64-token decode
+ * tile, two with the 112-token prefill tile; the environment variable
+ * DSV4_FUSED_FFN=0|1 replaces the default).
  * The fused launch stores the h rows of each expert chunk and starts that
  * chunk's down tiles as soon as all of its gate/up tiles are stored; results
  * are identical.  With stage timing on, the fused launch's time is reported

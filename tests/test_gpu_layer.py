@@ -107,7 +107,7 @@ def test_fused_ffn_launch_equals_two_launches(dev, T):
                 assert rel_err(bf16_to_np(y_fused), ref) <= TOL, profile
     finally:
         _profile(False)
-        plan.set_ffn_fusion(True)
+        plan.set_ffn_fusion(None)
 
 
 def test_plugin_forward_cfg2_a4w4_prefill(dev):
