@@ -114,16 +114,16 @@ __device__ __forceinline__ float pow2_any(int k) {
 }
 
 // E2M1 code of x (round to nearest, ties to even code, saturate at 6);
-// zero results carry no sign bit.
+// zero results carry no sign bit.  One sm_100a conversion instruction
+// (cvt.rn.satfinite.e2m1x2.f32: x into the low nibble, 0 into the high
+// one), then a result of magnitude zero loses its sign bit.
 __device__ __forceinline__ uint32_t e2m1_code(float x) {
-  float a = fminf(fabsf(x), 6.0f);
-  // grid step q = 0.5, 1 or 2: a / q is a * (1 / q), exact for powers of two
-  const float q = a < 2.0f ? 0.5f : (a < 4.0f ? 1.0f : 2.0f);
-  const float inv_q = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
-  float r = fminf(rintf(a * inv_q) * q, 6.0f);
-  int t = (int)(r * 2.0f);  // 0,1,2,3,4,6,8,12
-  uint32_t mag = t <= 4 ? (uint32_t)t : (t == 6 ? 5u : (t == 8 ? 6u : 7u));
-  return (x < 0.0f && mag != 0u) ? (mag | 8u) : mag;
+  uint32_t w;
+  asm("{\n\t.reg .b8 b;\n\tcvt.rn.satfinite.e2m1x2.f32 b, %2, %1;\n\tmov.b32 %0, {b, b, b, b};\n\t}"
+      : "=r"(w)
+      : "f"(x), "f"(0.0f));
+  const uint32_t c = w & 0xfu;
+  return (c & 7u) ? c : 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -271,6 +271,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ uint64_t policy_evict_last() {

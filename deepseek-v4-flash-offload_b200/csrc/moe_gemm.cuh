@@ -91,7 +91,7 @@ struct GemmParams {
   int out_tile_cols;         // output columns per tile (128: gate/up pair, 256: down pair)
   const uint8_t* b_sf;       // activation scale atoms: 512 B per (k-tile, BN-row block)
   int64_t rb_cap;            // BN-row blocks per k-tile in b_sf / out_sf
-  const int4* chunks;        // {expert, row0, nrows, 0}
+  const int4* chunks;        // {expert, row0, nrows, 1 when the expert has several chunks}
   const int* n_chunks;
   const int* slot_of;        // expert -> slot
   int n_slots;               // slots in the arena; other values are rejected
@@ -137,12 +137,13 @@ struct TileInfo {
   int nrows;  // valid rows in the chunk
   int mt;     // 128-row tile of the weight matrix
   bool sh;    // the shared expert (FP8 weights)
+  bool reuse; // the expert's weights feed several chunks
   int ph;     // 0: first GEMM of the launch (gate/up, or the only one); 1: down of a fused launch
   int c;      // chunk
 };
 
 __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_tiles) {
-  TileInfo ti{-1, 0, 0, 0, false, 0, 0};
+  TileInfo ti{-1, 0, 0, 0, false, false, 0, 0};
   if (t < n_tiles) {
     const int c = t / p.a_row_tiles;
     ti.c = c;
@@ -156,6 +157,7 @@ __device__ __forceinline__ TileInfo load_tile(const GemmParams& p, int t, int n_
     }
     ti.row0 = ch.y;
     ti.nrows = ch.z;
+    ti.reuse = ch.w != 0;
     ti.mt = t - c * p.a_row_tiles;
   }
   return ti;
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   if (warp == 0 && lane == 0) {
     const TileInfo first = tile(blockIdx.x);
     if (first.slot >= 0) {
-      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_w = first.reuse ? policy_evict_normal() : policy_evict_first();
       const uint8_t* sf_base = a_sf(first);
       const int k_tiles = P(first).k_tiles;
       const uint32_t b_tx = (uint32_t)b_rows_for<BN>(first.nrows) * (B_FP4 ? G_BK / 2 : G_BK);
@@ -315,7 +317,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      // weights stream through L2 once (evict first), except an expert's
+      // whose weight tiles feed several chunks: the other chunks' tiles run
+      // at about the same time on other CTAs and find them in L2
+      const uint64_t pol_once = policy_evict_first(), pol_reuse = policy_evict_normal();
       const uint64_t pol_x = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
@@ -339,6 +344,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const int nb = b_rows_for<BN>(cur.nrows);
         const CUtensorMap* mB = nb == 16 ? &m.B16 : (nb == 32 ? &m.B32 : (nb == 64 ? &m.B64 : &m.Bwide));
         const int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
+        const uint64_t pol_w = cur.reuse ? pol_reuse : pol_once;
         if (FUSED && cur.ph) {
           // the h rows of this chunk come from the gate/up tiles of other
           // CTAs: wait until all of them have stored theirs

@@ -194,7 +194,8 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
       offsets[tid] = ex.x;
       if (c > 0) active[ex.y] = tid;
       if (chunks)
-        for (int j = 0; j < nch; ++j) chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), 0);
+        for (int j = 0; j < nch; ++j)
+          chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), nch > 1);
     }
     if (tid == 0) {
       offsets[E] = tot3.x;
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     const int cpos = block_exclusive_scan(nch, scratch, &nchunk_total);
     for (int j = 0; j < nch; ++j) {
       const int r0 = off + j * pad;
-      chunks[cpos + j] = make_int4(tid, r0, min(pad, c - j * pad), 0);
+      chunks[cpos + j] = make_int4(tid, r0, min(pad, c - j * pad), nch > 1);
     }
     if (tid == 0) *n_chunks = nchunk_total;
   }
@@ -443,7 +444,8 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     offsets[tid] = ex.x;
     if (c > 0) active[ex.y] = tid;
     if (chunks)
-      for (int j = 0; j < nch; ++j) chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), 0);
+      for (int j = 0; j < nch; ++j)
+        chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), nch > 1);
     for (int b = 0; b < nblk; ++b) cnt_blk[(int64_t)b * E + tid] += ex.x;   // absolute start rows
   }
   if (tid == 0) {

@@ -75,6 +75,12 @@ def test_mx_quant_bit_exact(ops):
     x[3, :32] = 0.0
     x[4, 32:64] = 1e-30
     x[5, 64:96] = 6.0 * 2.0 ** np.arange(32)
+    # a block scaled by 1 (max 6): the E2M1 grid, every tie between grid
+    # points (to the even code), values that round to +-0, and saturation
+    ties = [6.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 0.1, 0.3, 4.9, 5.1, 5.9, 1.0, 1.5, 3.0]
+    x[6, 96:128] = np.array(ties + [-v for v in ties], np.float32)
+    x[7, 128:160] = np.array(ties + [-v for v in ties], np.float32) * np.float32(2.0 ** -20)
+    x = S.bf16_exact(x)
     q, s = ops.dynamic_mx_quant(bf16_tensor(x))
     vals, k, _ = O.mx_quant_fp4(x)
     assert np.array_equal(q.cpu().numpy(), O.pack_fp4(vals))
