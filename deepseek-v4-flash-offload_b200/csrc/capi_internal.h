@@ -47,6 +47,19 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
 // Whether kernels are launched with PDL (env DSV4_PDL, default on).
 bool pdl_enabled();
 
+// The decode router in one launch (route.cu): partial logits into `part`
+// ([H/128][T][E] fp32), a grid barrier on `bar` (two ints, zero before and
+// after the launch), top-k.  Launches only when T < 256, E <= 256 and the
+// whole grid fits on the GPU at once; *launched reports whether it did.
+int route_fused_launch(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
+                       const int64_t* input_ids, int64_t vocab, int64_t n_tokens, int hidden, int n_experts,
+                       int topk, int score_func, int renormalize, float route_scale, float* weights_out,
+                       int32_t* indices_out, float* part, int* bar, int* status, cudaStream_t st, bool* launched);
+// Bytes of `part` for up to n_tokens (< 256) tokens.
+inline int64_t route_fused_part_bytes(int64_t n_tokens, int hidden, int n_experts) {
+  return (int64_t)(hidden / 128) * n_tokens * n_experts * 4;
+}
+
 // Byte layout of one packed expert slot (see include/dsv4moe.h).
 struct SlotLayout {
   int64_t w13p;   // [2I, H/2] packed, w1 rows then w3 rows

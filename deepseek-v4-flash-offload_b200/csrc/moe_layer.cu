@@ -730,7 +730,7 @@ static int fused_ffn_default() {
 
 struct WsLayout {
   int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
-  int64_t xq, xsf, hq, hsf, out, ys, blk, done, bytes;
+  int64_t xq, xsf, hq, hsf, out, ys, blk, done, rbar, rpart, bytes;
   int64_t p_max, p_cap, max_chunks;
 };
 
@@ -770,6 +770,10 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   w.ys = shared ? take(2 * max_tokens * H) : 0;
   w.blk = take(4 * E * ((w.p_max + AL_THREADS - 1) / AL_THREADS + 1));   // per-block counts of the large align
   w.done = take(4 * w.max_chunks);   // finished gate/up tiles per chunk (fused launch)
+  // decode router (dsv4_moe_route): its grid barrier, zero between launches,
+  // and its partial logits for up to 255 tokens
+  w.rbar = take(256);
+  w.rpart = take(route_fused_part_bytes(std::min<int64_t>(max_tokens, 255), (int)H, (int)(E - (shared ? 1 : 0))));
   w.bytes = o;
   return w;
 }
@@ -1262,6 +1266,41 @@ extern "C" int dsv4_moe_set_gemm_tile(dsv4_moe_plan* p, int32_t tokens_per_tile)
   DSV4_CHECK_ARG(tokens_per_tile == 0 || tokens_per_tile == 64 || tokens_per_tile == 112,
                  "tokens per GEMM tile must be 0 (default), 64 or 112");
   p->gemm_tile = tokens_per_tile;
+  DSV4_API_END
+}
+
+// The router of the plan's layer for a decode batch, in the plan's
+// workspace: one launch (partial logits, grid barrier, top-k) when the batch
+// has fewer than 256 tokens and the grid fits on the GPU at once, else the
+// two kernels of dsv4_route_topk's decode path.
+extern "C" int dsv4_moe_route(dsv4_moe_plan* p, const void* x_bf16, const float* gate_w, const float* bias,
+                              const int32_t* tid2eid, const int64_t* input_ids, int64_t vocab_size, int64_t n_tokens,
+                              int32_t topk, int32_t score_func, int32_t renormalize, float route_scale,
+                              float* weights_out, int32_t* indices_out, void* stream) {
+  DSV4_API_BEGIN
+  DSV4_CHECK_ARG(p, "null plan");
+  const int E = p->E - (p->shared ? 1 : 0);
+  DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens < 256 && n_tokens <= p->max_tokens,
+                 "n_tokens must be below 256 and within the plan's max_tokens");
+  DSV4_CHECK_ARG(x_bf16 && gate_w && weights_out && indices_out, "null pointer");
+  DSV4_CHECK_ARG(E <= 256, "n_experts must be in [1, 256]");
+  DSV4_CHECK_ARG(topk > 0 && topk <= 16 && topk <= E, "topk must be in [1, min(16, n_experts)]");
+  DSV4_CHECK_ARG(score_func >= 0 && score_func <= 2, "unknown score function");
+  DSV4_CHECK_ARG(!tid2eid || (input_ids && vocab_size > 0), "hash routing needs input_ids and vocab_size");
+  if (n_tokens == 0) return DSV4_OK;
+  if (int rc = bind_device_of(x_bf16, nullptr)) return rc;
+  DSV4_CHECK_ARG(((uintptr_t)x_bf16 % 16) == 0 && ((uintptr_t)gate_w % 16) == 0, "x and gate_w must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  const WsLayout& w = p->wl;
+  bool launched = false;
+  if (int rc = route_fused_launch(x_bf16, gate_w, bias, tid2eid, input_ids, vocab_size, n_tokens, p->H, E, topk,
+                                  score_func, renormalize, route_scale, weights_out, indices_out,
+                                  wsp<float>(p, w.rpart), wsp<int>(p, w.rbar), wsp<int>(p, w.status), st, &launched))
+    return rc;
+  if (launched) return DSV4_OK;
+  return dsv4_route_topk(x_bf16, gate_w, bias, tid2eid, input_ids, vocab_size, n_tokens, p->H, E, topk, score_func,
+                         renormalize, route_scale, weights_out, indices_out, wsp<uint8_t>(p, w.rpart),
+                         route_fused_part_bytes(n_tokens, p->H, E), stream);
   DSV4_API_END
 }
 

@@ -31,13 +31,9 @@ constexpr int RT_SPLIT_NOALLOC = 4;  // slices of H on the fixed-scratch path
 // 4tq..4tq+3 against experts 4eq..4eq+3, two 16-byte loads per 16 FMAs.  The
 // next chunk's global loads are issued before the current chunk is computed.
 // One writer per partial: deterministic.
-__global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __restrict__ x,
-                                                           const float* __restrict__ w, float* __restrict__ part,
-                                                           int64_t T, int H, int E, int kslice) {
-  __shared__ __align__(16) float xs[RL_KC][RL_TOK];
-  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
-  griddep_wait();
-  griddep_launch();
+__device__ __forceinline__ void logits_tile(const uint16_t* __restrict__ x, const float* __restrict__ w,
+                                            float* __restrict__ part, int64_t T, int H, int E, int kslice,
+                                            float (*xs)[RL_TOK], float (*ws)[RL_EXP]) {
   const int tid = threadIdx.x;
   const int e0 = blockIdx.x * RL_EXP;
   const int slice = blockIdx.y;
@@ -110,6 +106,16 @@ __global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __res
         if (e + b < E) dst[t * E + e + b] = acc[a][b];
     }
   }
+}
+
+__global__ __launch_bounds__(256) void route_logits_kernel(const uint16_t* __restrict__ x,
+                                                           const float* __restrict__ w, float* __restrict__ part,
+                                                           int64_t T, int H, int E, int kslice) {
+  __shared__ __align__(16) float xs[RL_KC][RL_TOK];
+  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
+  griddep_wait();
+  griddep_launch();
+  logits_tile(x, w, part, T, H, E, kslice, xs, ws);
 }
 
 // Prefill-sized batches: one CTA computes 128 tokens x 128 experts over
@@ -377,29 +383,22 @@ __device__ __forceinline__ float softplus_f(float v) { return v > 20.f ? v : log
 // weights, renormalised and scaled.  A hash-table token id outside
 // [0, vocab) reads nothing: its picks are written as expert id E (out of
 // range), which the layer's align rejects with DSV4_EINVAL.
-__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int split, int64_t T,
-                                                         int E, int K, int score_func, int renorm, float scale,
-                                                         const float* __restrict__ bias,
-                                                         const int32_t* __restrict__ tid2eid,
-                                                         const int64_t* __restrict__ ids, int64_t vocab,
-                                                         float* __restrict__ w_out,
-                                                         int32_t* __restrict__ i_out, const int* __restrict__ err) {
+struct TopkSmem {
+  float sc[RT_MAX_E], ch[RT_MAX_E];
+  float red[2][8];
+};
+
+// Token t's picks by one CTA of 256 threads (see route_topk_kernel).
+__device__ __forceinline__ void topk_token(int64_t t, const float* __restrict__ logits, int split, int64_t T, int E,
+                                           int K, int score_func, int renorm, float scale,
+                                           const float* __restrict__ bias, const int32_t* __restrict__ tid2eid,
+                                           const int64_t* __restrict__ ids, int64_t vocab, float* __restrict__ w_out,
+                                           int32_t* __restrict__ i_out, TopkSmem& sm) {
   constexpr int PER = RT_MAX_E / 32;
-  __shared__ float sc_s[RT_MAX_E], ch_s[RT_MAX_E];
-  __shared__ float red[2][8];
-  griddep_wait();
-  griddep_launch();
-  const int64_t t = blockIdx.x;
+  float* sc_s = sm.sc;
+  float* ch_s = sm.ch;
+  float (*red)[8] = sm.red;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (err && *reinterpret_cast<const volatile int*>(err) != 0) {
-    // the logits kernel gave up on a wait: expert id E is out of range, so
-    // the layer's align rejects these picks and its status reports it
-    if (tid < K) {
-      w_out[t * K + tid] = 0.f;
-      i_out[t * K + tid] = E;
-    }
-    return;
-  }
   const int e = tid;
   float l = -INFINITY;
   if (e < E) {
@@ -441,7 +440,7 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
   sc_s[e] = sc;
   ch_s[e] = e < E ? (bias ? sc + bias[e] : sc) : -INFINITY;
   __syncthreads();
-  if (warp != 0) return;
+  if (warp != 0) return;   // the caller synchronises the CTA before reusing sm
   float ch[PER];
 #pragma unroll
   for (int j = 0; j < PER; ++j) ch[j] = ch_s[lane + 32 * j];
@@ -495,6 +494,86 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict
   }
 }
 
+// picks of a token whose logits are not available (a wait gave up):
+// expert id E is out of range, so the layer's align rejects them and its
+// status reports it
+__device__ __forceinline__ void topk_token_failed(int64_t t, int E, int K, float* __restrict__ w_out,
+                                                  int32_t* __restrict__ i_out) {
+  if ((int)threadIdx.x < K) {
+    w_out[t * K + threadIdx.x] = 0.f;
+    i_out[t * K + threadIdx.x] = E;
+  }
+}
+
+__global__ __launch_bounds__(256) void route_topk_kernel(const float* __restrict__ logits, int split, int64_t T,
+                                                         int E, int K, int score_func, int renorm, float scale,
+                                                         const float* __restrict__ bias,
+                                                         const int32_t* __restrict__ tid2eid,
+                                                         const int64_t* __restrict__ ids, int64_t vocab,
+                                                         float* __restrict__ w_out,
+                                                         int32_t* __restrict__ i_out, const int* __restrict__ err) {
+  __shared__ TopkSmem sm;
+  griddep_wait();
+  griddep_launch();
+  const int64_t t = blockIdx.x;
+  if (err && *reinterpret_cast<const volatile int*>(err) != 0) {
+    topk_token_failed(t, E, K, w_out, i_out);   // the logits kernel gave up on a wait
+    return;
+  }
+  topk_token(t, logits, split, T, E, K, score_func, renorm, scale, bias, tid2eid, ids, vocab, w_out, i_out, sm);
+}
+
+// Decode router in one launch (batches of fewer than 256 tokens): every CTA
+// computes its 64 x 64 x 128 tile of partial logits (logits_tile), the grid
+// meets at a barrier, then CTA b takes the top-k of tokens b, b + G, ... .
+// The barrier is a counter in zeroed memory that the last CTA to finish sets
+// back to zero (bar[0]: arrivals, bar[1]: CTAs past the top-k), so a launch
+// finds it at zero; the host launches this only when the whole grid fits on
+// the GPU at once, and the wait is bounded (DSV4_ETIMEOUT into `status`,
+// the affected tokens' picks marked invalid).  A CTA that arrives late still
+// completes its share and the count, so the counter is back at zero after
+// every launch.
+__global__ __launch_bounds__(256) void route_fused_kernel(const uint16_t* __restrict__ x,
+                                                          const float* __restrict__ w, float* __restrict__ part,
+                                                          int64_t T, int H, int E, int kslice, int* bar, int K,
+                                                          int score_func, int renorm, float scale,
+                                                          const float* __restrict__ bias,
+                                                          const int32_t* __restrict__ tid2eid,
+                                                          const int64_t* __restrict__ ids, int64_t vocab,
+                                                          float* __restrict__ w_out, int32_t* __restrict__ i_out,
+                                                          int* status) {
+  __shared__ __align__(16) float xs[RL_KC][RL_TOK];
+  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
+  __shared__ TopkSmem sm;
+  __shared__ int ok_s;
+  griddep_wait();
+  griddep_launch();
+  const int G = (int)(gridDim.x * gridDim.y * gridDim.z);
+  const int b = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  logits_tile(x, w, part, T, H, E, kslice, xs, ws);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_add(bar, 1);
+    ok_s = wait_count_geq(bar, G, status) ? 1 : 0;
+  }
+  __syncthreads();
+  const int split = H / kslice;
+  for (int64_t t = b; t < T; t += G) {
+    if (ok_s)
+      topk_token(t, part, split, T, E, K, score_func, renorm, scale, bias, tid2eid, ids, vocab, w_out, i_out, sm);
+    else
+      topk_token_failed(t, E, K, w_out, i_out);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (atomicAdd(bar + 1, 1) == G - 1) {   // every CTA is past the barrier
+      atomicExch(bar, 0);
+      atomicExch(bar + 1, 0);
+    }
+  }
+}
+
 }  // namespace dsv4
 
 using namespace dsv4;
@@ -526,7 +605,43 @@ int prepare_route_tc() {
   if (dev >= 0 && dev < 64) g_tc_ready[dev] = true;
   return DSV4_OK;
 }
+std::mutex g_fused_mu;
+int g_fused_cap[64] = {};   // CTAs of route_fused_kernel resident at once, per device (0: not known yet)
 }  // namespace
+
+namespace dsv4 {
+int route_fused_launch(const void* x_bf16, const float* gate_w, const float* bias, const int32_t* tid2eid,
+                       const int64_t* input_ids, int64_t vocab, int64_t n_tokens, int hidden, int n_experts,
+                       int topk, int score_func, int renormalize, float route_scale, float* weights_out,
+                       int32_t* indices_out, float* part, int* bar, int* status, cudaStream_t st, bool* launched) {
+  *launched = false;
+  if (n_tokens <= 0 || n_tokens >= RTC_MIN_TOKENS || n_experts > RT_MAX_E || hidden % RL_SLICE != 0) return DSV4_OK;
+  int dev = 0;
+  DSV4_CUDA_CHECK(cudaGetDevice(&dev));
+  int cap = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_fused_mu);
+    if (dev >= 0 && dev < 64 && g_fused_cap[dev] > 0) {
+      cap = g_fused_cap[dev];
+    } else {
+      int per_sm = 0, sms = 0;
+      DSV4_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, route_fused_kernel, 256, 0));
+      DSV4_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      cap = per_sm * sms;
+      if (dev >= 0 && dev < 64) g_fused_cap[dev] = cap;
+    }
+  }
+  const dim3 grid((n_experts + RL_EXP - 1) / RL_EXP, hidden / RL_SLICE, (unsigned)((n_tokens + RL_TOK - 1) / RL_TOK));
+  // the barrier needs every CTA resident at once; half the capacity leaves
+  // room for the kernels it may still share the GPU with under PDL
+  if ((int64_t)grid.x * grid.y * grid.z > cap / 2) return DSV4_OK;
+  DSV4_CUDA_CHECK(launch_k(route_fused_kernel, grid, dim3(256), 0, st, pdl_enabled(), (const uint16_t*)x_bf16, gate_w,
+                           part, n_tokens, hidden, n_experts, (int)RL_SLICE, bar, topk, score_func, renormalize,
+                           route_scale, bias, tid2eid, input_ids, vocab, weights_out, indices_out, status));
+  *launched = true;
+  return DSV4_OK;
+}
+}  // namespace dsv4
 
 extern "C" int64_t dsv4_route_workspace_bytes(int64_t n_tokens, int32_t hidden, int32_t n_experts) {
   if (n_tokens < 0 || hidden <= 0 || n_experts <= 0) return DSV4_EINVAL;

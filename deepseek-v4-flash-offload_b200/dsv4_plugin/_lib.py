@@ -62,6 +62,7 @@ SIGNATURES = {
     "dsv4_moe_enable_timing": (C.c_int, [_p, _i32]),
     "dsv4_moe_set_gemm_tile": (C.c_int, [_p, _i32]),
     "dsv4_moe_set_ffn_fusion": (C.c_int, [_p, _i32]),
+    "dsv4_moe_route": (C.c_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i32, _i32, _i32, _f32, _p, _p, _p]),
     "dsv4_slotcache_create": (C.c_int, [C.POINTER(_p), _i64]),
     "dsv4_slotcache_destroy": (C.c_int, [_p]),
     "dsv4_slotcache_lookup": (C.c_int, [_p, _p, _p, _i64, _p, _p]),

@@ -38,6 +38,9 @@ _MXFP4_GMM = os.environ.get("DSV4_MXFP4_GMM", "0") == "1"
 # the routed output (the reference's structure); by default its FP8 weights
 # are captured at load and it runs inside the routed launches
 _FUSED_SHARED = os.environ.get("DSV4_FUSED_SHARED", "1") != "0"
+# decode batches route in one launch in the layer plan's workspace
+# (DSV4_PLAN_ROUTE=0: the two-kernel router with its own workspace)
+_PLAN_ROUTE = os.environ.get("DSV4_PLAN_ROUTE", "0") != "0"
 DEFAULT_TARGETS = ("vllm.model_executor.models.deepseek_v4", "vllm_ascend.models.deepseek_v4")
 
 
@@ -136,12 +139,18 @@ class OffloadDeepseekV4MoE(nn.Module):
         self.experts = _ExpertsFacade(self)
 
     # -- routing ------------------------------------------------------------
-    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None, out=None, workspace=None):
-        """(weights fp32 [T, k], indices int32 [T, k]); deepseek_v4.py:118-148."""
+    def _route(self, hs: torch.Tensor, input_ids: torch.Tensor | None, out=None, workspace=None, plan=None):
+        """(weights fp32 [T, k], indices int32 [T, k]); deepseek_v4.py:118-148.
+        A decode batch (< 256 tokens) with the layer's plan routes in one
+        launch in the plan's workspace (``MoEPlan.route``)."""
         tid2eid = getattr(self.gate, "tid2eid", None) if self.hash else None
         if self.hash and input_ids is None:
             raise RuntimeError("hash-layer routing needs input_ids (forward_context.input_ids is missing)")
         bias = None if self.hash else getattr(self.gate, "e_score_correction_bias", None)
+        if plan is not None and out is None and hs.shape[0] < 256 and _PLAN_ROUTE:
+            return plan.route(hs, self.gate.weight, bias, self.topk, self.scoring_func, self.renormalize,
+                              self.routed_scaling_factor, tid2eid=tid2eid,
+                              input_ids=input_ids if self.hash else None)
         return ops.route_topk(hs, self.gate.weight, bias, self.topk, self.scoring_func, self.renormalize,
                               self.routed_scaling_factor, tid2eid=tid2eid,
                               input_ids=input_ids if self.hash else None, out=out, workspace=workspace)
@@ -199,13 +208,17 @@ class OffloadDeepseekV4MoE(nn.Module):
             self.engine.bank.mark_used(slots)
         return y
 
+    def _plan(self, n_tokens: int, with_shared: bool = False):
+        return self.engine.plan_for(self.n_routed_experts, self.topk, n_tokens, self.swiglu_limit or 0.0,
+                                    with_shared=with_shared)
+
     def _routed(self, hs: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
         """Routed-expert output [T, H] bf16; profile from ``_MXFP4_GMM``."""
-        weights, indices = self._route(hs, input_ids)
+        weights, indices = self._route(hs, input_ids, plan=self._plan(hs.shape[0]))
         return self._routed_experts(hs, weights, indices, "a4w4" if _MXFP4_GMM else "bf16", input_ids)
 
     def _routed_mxfp4(self, hs: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
-        weights, indices = self._route(hs, input_ids)
+        weights, indices = self._route(hs, input_ids, plan=self._plan(hs.shape[0]))
         return self._routed_experts(hs, weights, indices, "a4w4", input_ids)
 
     def _shared_slot(self):
@@ -231,7 +244,7 @@ class OffloadDeepseekV4MoE(nn.Module):
             # routed experts + shared expert in one pass: the shared expert is
             # every token's last assignment, added in fp32 before the one bf16
             # rounding (model_npu.py:531-533)
-            weights, indices = self._route(hs, input_ids)
+            weights, indices = self._route(hs, input_ids, plan=self._plan(hs.shape[0], with_shared=True))
             out = self._routed_experts(hs, weights, indices, "a4w4" if _MXFP4_GMM else "bf16", input_ids,
                                        shared_slot=sh)
         else:

@@ -296,6 +296,35 @@ class MoEPlan:
                                      so.data_ptr(), out.data_ptr(), _stream(x.device)))
         return out
 
+    def route(self, x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor | None, topk: int,
+              score_func: str = "sqrtsoftplus", renormalize: bool = True, route_scale: float = 1.5,
+              tid2eid: torch.Tensor | None = None, input_ids: torch.Tensor | None = None):
+        """``route_topk`` for a decode batch (< 256 tokens) in this plan's
+        workspace: one launch (partial logits, grid barrier, top-k) when the
+        grid fits on the GPU.  Returns (weights fp32 [T,k], indices int32 [T,k])."""
+        _need_cuda(x, gate_weight, bias, tid2eid, input_ids)
+        if x.dtype != torch.bfloat16:
+            x = x.to(torch.bfloat16)
+        x = x.contiguous()
+        w = gate_weight.contiguous().float()
+        t = x.shape[0]
+        if tid2eid is not None:
+            if input_ids is None:
+                raise RuntimeError("hash routing needs input_ids (forward_context.input_ids is missing)")
+            tid2eid = tid2eid.to(torch.int32).contiguous()
+            input_ids = input_ids.to(torch.int64).reshape(-1).contiguous()
+            if input_ids.numel() != t:
+                raise ValueError("input_ids must have one id per token")
+        b = None if bias is None else bias.float().contiguous()
+        wo = torch.empty((t, topk), dtype=torch.float32, device=x.device)
+        io = torch.empty((t, topk), dtype=torch.int32, device=x.device)
+        check(lib().dsv4_moe_route(
+            self._h, x.data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(),
+            None if tid2eid is None else tid2eid.data_ptr(), None if input_ids is None else input_ids.data_ptr(),
+            0 if tid2eid is None else tid2eid.shape[0], t, topk, SCORE_FUNCS[score_func], int(bool(renormalize)),
+            float(route_scale), wo.data_ptr(), io.data_ptr(), _stream(x.device)))
+        return wo, io
+
     def forward_rows(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, slot_of: torch.Tensor,
                      profile: str = "bf16", n_tokens_dev: torch.Tensor | None = None):
         """The layer without its combine, for a token count that may be known

@@ -174,6 +174,20 @@ int dsv4_moe_plan_destroy(dsv4_moe_plan* plan);
 int dsv4_moe_forward(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t n_tokens,
                      const float* route_weights, const int32_t* route_indices, const int32_t* slot_of_expert,
                      void* y_bf16, void* stream);
+/* The router of the plan's layer (OffloadDeepseekV4MoE._route,
+ * deepseek_v4.py:118-148; the same arguments and results as
+ * dsv4_route_topk) for a decode batch of fewer than 256 tokens (and at most
+ * the plan's max_tokens), with its scratch in the plan's workspace: partial
+ * logits, a grid-wide barrier and the top-k in one launch when the grid fits
+ * on the GPU at once, else dsv4_route_topk's two kernels.  The plan's status
+ * (dsv4_moe_status) reports a barrier that timed out (DSV4_ETIMEOUT; the
+ * affected picks are expert id n_experts, which the forward rejects).
+ * Calls on one plan must not overlap on the GPU (they share its workspace,
+ * as forwards do). */
+int dsv4_moe_route(dsv4_moe_plan* plan, const void* x_bf16, const float* gate_w, const float* bias,
+                   const int32_t* tid2eid, const int64_t* input_ids, int64_t vocab_size, int64_t n_tokens,
+                   int32_t topk, int32_t score_func, int32_t renormalize, float route_scale, float* weights_out,
+                   int32_t* indices_out, void* stream);
 /* The same layer for a batch whose token count is known only on the device
  * (the rows that expert parallelism received): the first *n_tokens_dev
  * (<= max_tokens) rows of x and of the router outputs are used.  y_bf16 may

@@ -78,6 +78,44 @@ def test_plugin_forward_cfg1_matches_oracle(dev, T):
     assert np.array_equal(_sets(gi_.cpu().numpy()), _sets(idx))
 
 
+def test_plan_route_equals_route_topk(dev):
+    """The decode router in one launch (partial logits, grid barrier,
+    top-k; ``MoEPlan.route``) gives the same bits as the two-kernel
+    ``route_topk``: every score function, the hash table, batches of 1 to
+    200 tokens (200 needs 512 CTAs; when they do not fit at once the plan
+    falls back to the two kernels), two calls in a row on the same barrier;
+    at T=64 also the reference plugin's own routing (route_cfg1.npz)."""
+    import os
+    from dsv4_plugin import ops
+    cfg = S.CFG1
+    arena = torch.empty((1, ops.expert_slot_bytes(cfg.hidden, cfg.inter)), dtype=torch.uint8, device=dev)
+    plan = ops.MoEPlan(cfg.hidden, cfg.inter, cfg.n_experts, cfg.topk, 256, 0.0, arena)
+    gw, bias = S.make_gate(cfg, 0)
+    gwt, bt = torch.from_numpy(gw).to(dev), torch.from_numpy(bias).to(dev)
+    vocab = 1000
+    rng = np.random.default_rng(5)
+    tid2eid = torch.from_numpy(np.stack([rng.choice(cfg.n_experts, cfg.topk, replace=False)
+                                         for _ in range(vocab)]).astype(np.int32)).to(dev)
+    for T in (1, 8, 64, 200):
+        xt = bf16_tensor(S.make_tokens(cfg, 0, T))
+        ids = torch.from_numpy(rng.integers(0, vocab, T)).to(dev)
+        for func in ("sqrtsoftplus", "softmax", "sigmoid", "hash"):
+            kw = dict(tid2eid=tid2eid, input_ids=ids) if func == "hash" else {}
+            b = None if func == "hash" else bt
+            f = "sqrtsoftplus" if func == "hash" else func
+            w0, i0 = ops.route_topk(xt, gwt, b, cfg.topk, f, True, 1.5, **kw)
+            for _ in range(2):
+                w1, i1 = plan.route(xt, gwt, b, cfg.topk, f, True, 1.5, **kw)
+                torch.cuda.synchronize()
+                plan.status()
+                assert torch.equal(i0, i1), (T, func)
+                assert torch.equal(w0, w1), (T, func)
+        if T == 64:
+            g = np.load(os.path.join(os.path.dirname(__file__), "golden", "route_cfg1.npz"))
+            w1, i1 = plan.route(xt, gwt, bt, cfg.topk, cfg.score_func, cfg.renormalize)
+            assert np.array_equal(_sets(i1.cpu().numpy()), _sets(g["t64_idx"]))
+
+
 @pytest.mark.parametrize("T", [1, 64, 512])
 def test_fused_ffn_launch_equals_two_launches(dev, T):
     """Gate/up, SwiGLU, requant and down in one persistent launch (down
