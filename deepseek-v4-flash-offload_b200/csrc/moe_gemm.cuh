@@ -118,17 +118,6 @@ struct GemmParams {
   // activations (the h rows) once the count reaches the gate/up tiles per
   // chunk.  Zeroed by the align of the same pass.
   int* chunk_done;
-  // combine in the down epilogue (fused launch, bf16 rows in out_bf16): a
-  // token's output columns [256 mt, 256 mt + 256) are the fp32 sum of its
-  // valid assignments' rows in ascending sorted position, rounded once to
-  // bf16 into comb_y, done by the tile that stores the last of those rows
-  // (comb_cnt[t * comb_blocks + mt] counts them; zeroed by the align).
-  // Null: a separate combine kernel.
-  int* comb_cnt;
-  uint16_t* comb_y;
-  const int32_t* inv;
-  int topk;
-  int comb_blocks;
 };
 
 __device__ __forceinline__ float warp_max_f(float v) {
@@ -689,55 +678,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         __threadfence();
         named_bar_sync(1, 32 * G_EPI_WARPS);
         if (warp == 2 && lane == 0) red_release_add(p.chunk_done + chunk, 1);
-      }
-      if (FUSED && store_tile && gq.comb_cnt) {
-        // combine: count this tile's rows per token; a token whose last row
-        // this was gets its 256 output columns summed here (the combine
-        // kernel's order and rounding)
-        const int et = threadIdx.x - 64;   // 0..255 over the epilogue warps
-        int* fin = reinterpret_cast<int*>(red);   // [0]: count, [1..]: tokens (up to BN)
-        int* pos = fin + 128;                     // [0]: valid rows, [1..]: their positions, ascending
-        if (et == 0) fin[0] = 0;
-        __threadfence();
-        named_bar_sync(1, 32 * G_EPI_WARPS);
-        if (et < nrows) {
-          const int a = gq.sorted_flat[row0 + et];
-          const int tk = a / gq.topk;
-          int kv = 0;
-          for (int j = 0; j < gq.topk; ++j) kv += gq.inv[tk * gq.topk + j] >= 0 ? 1 : 0;
-          if (atomicAdd(gq.comb_cnt + (int64_t)tk * gq.comb_blocks + mt, 1) == kv - 1) {
-            __threadfence();
-            fin[1 + atomicAdd(fin, 1)] = tk;
-          }
-        }
-        named_bar_sync(1, 32 * G_EPI_WARPS);
-        const int nfin = fin[0];
-        const int col = mt * gq.out_tile_cols + et;   // one output column per thread
-        for (int f = 0; f < nfin; ++f) {
-          const int tk = fin[1 + f];
-          if (et == 0) {
-            int k = 0;
-            for (int j = 0; j < gq.topk; ++j) {
-              const int v = gq.inv[tk * gq.topk + j];
-              if (v < 0) continue;
-              int s = k++;
-              while (s > 0 && pos[s] > v) {   // pos[1..k]: insertion sort
-                pos[s + 1] = pos[s];
-                --s;
-              }
-              pos[s + 1] = v;
-            }
-            pos[0] = k;
-          }
-          named_bar_sync(1, 32 * G_EPI_WARPS);
-          float acc = 0.f;
-          const int k = pos[0];
-          for (int j = 0; j < k; ++j)
-            acc += bf16_from_bits(__ldcg(gq.out_bf16 + (int64_t)pos[1 + j] * gq.out_ld + col));
-          gq.comb_y[(int64_t)tk * gq.out_ld + col] = bf16_bits(acc);
-          named_bar_sync(1, 32 * G_EPI_WARPS);   // pos is rewritten for the next token
-        }
-        named_bar_sync(1, 32 * G_EPI_WARPS);   // fin is reused by the next tile
       }
       if (++abuf == C::ACC_BUFS) {
         abuf = 0;

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
                      int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
                      float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
                      int pad, int* status, const int32_t* __restrict__ n_tokens_dev, int k_in, int shared_e,
-                     int* __restrict__ chunk_done, int max_chunks, int* __restrict__ comb_cnt, int comb_n) {
+                     int* __restrict__ chunk_done, int max_chunks) {
   extern __shared__ int sm[];
   int* cnt = sm;                 // E
   int* run = cnt + E;            // E
@@ -141,7 +141,6 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   griddep_wait();
   griddep_launch();
   for (int j = tid; j < max_chunks; j += AL_THREADS) chunk_done[j] = 0;
-  for (int j = tid; j < comb_n; j += AL_THREADS) comb_cnt[j] = 0;
   // a token count known only on the device (rows received by expert
   // parallelism): the first n tokens of the buffers
   if (n_tokens_dev) P = min(P, max(0, *n_tokens_dev) * topk);
@@ -417,7 +416,7 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
                       int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
                       int32_t* __restrict__ active, int32_t* __restrict__ n_active, float* __restrict__ sorted_w,
                       int4* __restrict__ chunks, int32_t* __restrict__ n_chunks, int pad,
-                      int* __restrict__ chunk_done, int max_chunks, int* __restrict__ comb_cnt, int comb_n) {
+                      int* __restrict__ chunk_done, int max_chunks) {
   __shared__ int scratch[96];
   __shared__ int run_s[1024], cnt_s[1024];
   griddep_wait();
@@ -426,7 +425,6 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
   const int nblk = (P + AL_THREADS - 1) / AL_THREADS;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int j = tid; j < max_chunks; j += AL_THREADS) chunk_done[j] = 0;
-  for (int j = tid; j < comb_n; j += AL_THREADS) comb_cnt[j] = 0;
   int c = 0;
   if (tid < E) {
     for (int b = 0; b < nblk; ++b) {
@@ -732,7 +730,7 @@ static int fused_ffn_default() {
 
 struct WsLayout {
   int64_t status, counts, offsets, active, n_active, n_chunks, sorted_flat, inv, sorted_w, chunks;
-  int64_t xq, xsf, hq, hsf, out, ys, blk, done, rbar, rpart, comb, comb_cap, bytes;
+  int64_t xq, xsf, hq, hsf, out, ys, blk, done, rbar, rpart, bytes;
   int64_t p_max, p_cap, max_chunks;
 };
 
@@ -775,10 +773,6 @@ static WsLayout ws_layout(int64_t H, int64_t I, int64_t E, int64_t topk, int64_t
   // decode router (dsv4_moe_route): its grid barrier, zero between launches,
   // and its partial logits for up to 255 tokens
   w.rbar = take(256);
-  // per (token, 256-column block) row counts of the combine folded into the
-  // fused launch, for batches of up to comb_cap tokens
-  w.comb_cap = std::min<int64_t>(max_tokens, 4096);
-  w.comb = take(4 * w.comb_cap * (H / 256));
   w.rpart = take(route_fused_part_bytes(std::min<int64_t>(max_tokens, 255), (int)H, (int)(E - (shared ? 1 : 0))));
   w.bytes = o;
   return w;
@@ -804,7 +798,6 @@ struct dsv4_moe_plan {
   bool timing = false;
   int gemm_tile = 0;   // tokens per GEMM tile; 0 = default
   int fused_ffn = -1;   // gate/up and down GEMMs in one launch: 1, 0, -1 = with the 64-token tile
-  bool fused_combine = true;   // the combine in the fused launch's down epilogue
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   ~dsv4_moe_plan() {
     for (auto& e : ev)
@@ -945,10 +938,6 @@ extern "C" int dsv4_moe_plan_create_ex(dsv4_moe_plan** out, int32_t hidden, int3
   p->max_tokens = max_tokens;
   p->swiglu_limit = swiglu_limit;
   p->fused_ffn = fused_ffn_default();
-  {
-    const char* e = getenv("DSV4_FUSED_COMBINE");
-    p->fused_combine = !(e && e[0] == '0');
-  }
   p->arena = slot_arena;
   p->n_slots = n_slots;
   p->slot = slot_layout(hidden, inter);
@@ -1059,18 +1048,13 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   };
   // events between stages break the programmatic overlap: no PDL while timing
   const bool pdl = pdl_enabled() && !p->timing;
-  // gate/up and down in one launch, and with it the combine in the down
-  // epilogue (rows to y, no extra row, batch within the counters)
-  const bool fused = p->fused_ffn == 1 || (p->fused_ffn < 0 && bn == 64);
-  const bool comb = fused && y_bf16 && !a.extra && !a.assign_dst && n_tokens <= w.comb_cap && p->fused_combine;
-  const int comb_n = comb ? (int)(n_tokens * (p->H / 256)) : 0;
   mark(0);
   if (P <= AL_THREADS) {
     DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P,
                              a.topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
                              sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
                              wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e,
-                             wsp<int>(p, w.done), (int)w.max_chunks, wsp<int>(p, w.comb), comb_n));
+                             wsp<int>(p, w.done), (int)w.max_chunks));
   } else {
     // large batches: count per block, scan on one CTA, place per block
     const unsigned nblk = (unsigned)((P + AL_THREADS - 1) / AL_THREADS);
@@ -1081,8 +1065,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
     DSV4_CUDA_CHECK(launch_k(align_scan_kernel, dim3(1), dim3(AL_THREADS), 0, st, pdl, P, a.topk, p->E,
                              n_tokens_dev, cnt_blk, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
                              sorted_flat, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
-                             wsp<int4>(p, w.chunks), n_chunks, bn, wsp<int>(p, w.done), (int)w.max_chunks,
-                             wsp<int>(p, w.comb), comb_n));
+                             wsp<int4>(p, w.chunks), n_chunks, bn, wsp<int>(p, w.done), (int)w.max_chunks));
     DSV4_CUDA_CHECK(launch_k(align_place_kernel, dim3(nblk), dim3(AL_THREADS), blk_smem, st, pdl, route_indices, P,
                              a.topk, p->E, a.k_in, a.shared_e, route_weights, n_tokens_dev,
                              (const int32_t*)cnt_blk, sorted_flat, inv, wsp<float>(p, w.sorted_w), status));
@@ -1141,14 +1124,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   const CUtensorMap& sh2 = a.sh2 ? *a.sh2 : p->tmA2;
   const GemmMaps m1 = a.fp4 ? gemm_maps(bn, p->tmA13p, p->tmB1_fp4, sh13) : gemm_maps(bn, p->tmA13, p->tmB1_fp8, sh13);
   const GemmMaps m2 = a.fp4 ? gemm_maps(bn, p->tmA2p, p->tmB2_fp4, sh2) : gemm_maps(bn, p->tmA2, p->tmB2_fp8, sh2);
-  if (comb) {
-    g2.comb_cnt = wsp<int>(p, w.comb);
-    g2.comb_y = (uint16_t*)y_bf16;
-    g2.inv = inv;
-    g2.topk = a.topk;
-    g2.comb_blocks = p->H / 256;
-  }
-  if (fused) {
+  if (p->fused_ffn == 1 || (p->fused_ffn < 0 && bn == 64)) {
     // gate/up, SwiGLU, requant and down in one persistent launch; the
     // stage events put its whole time under the gate/up stage
     if (a.fp4)
@@ -1168,7 +1144,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
       DSV4_CUDA_CHECK((launch_gemm<false, EPI_STORE_BF16, false>(bn, st, pdl, p->num_sms, m2, g2, m2, g2)));
   }
   mark(4);
-  if (y_bf16 && !comb) {
+  if (y_bf16) {
     const int threads = std::min(128, p->H / 8);
     const unsigned gy = (unsigned)std::max(1, p->H / (8 * threads));
     DSV4_CUDA_CHECK(launch_k(combine_kernel, dim3((unsigned)n_tokens, gy), dim3(threads), 0, st, pdl,
@@ -1389,7 +1365,7 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
   moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
       indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0, nullptr, 0);
+      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
