@@ -494,6 +494,146 @@ __device__ __forceinline__ void topk_token(int64_t t, const float* __restrict__ 
   }
 }
 
+// Token t's picks by one warp: lane L holds experts L + 32 j (j < 8).  The
+// same arithmetic in the same order as topk_token (the slices added in
+// order; the softmax sum as the per-32-expert shuffle trees added in expert
+// order), so the results are bit-identical; no block barrier, so a CTA of
+// 8 warps takes 8 tokens (prefill batches: a few slices per logit).
+__device__ __forceinline__ void topk_token_warp(int64_t t, const float* __restrict__ logits, int split, int64_t T,
+                                                int E, int K, int score_func, int renorm, float scale,
+                                                const float* __restrict__ bias, const int32_t* __restrict__ tid2eid,
+                                                const int64_t* __restrict__ ids, int64_t vocab,
+                                                float* __restrict__ w_out, int32_t* __restrict__ i_out) {
+  constexpr int PER = RT_MAX_E / 32;
+  const int lane = threadIdx.x & 31;
+  float l[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) l[j] = lane + 32 * j < E ? 0.f : -INFINITY;
+  {
+    const float* src = logits + t * E + lane;
+    const int64_t stride = T * E;
+    for (int s0 = 0; s0 < split; s0 += 4) {
+      float v[4][PER];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < PER; ++j)
+          v[u][j] = (s0 + u < split && lane + 32 * j < E) ? src[(s0 + u) * stride + 32 * j] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < PER; ++j)
+          if (s0 + u < split && lane + 32 * j < E) l[j] += v[u][j];
+    }
+  }
+  float sc[PER];
+  if (score_func == DSV4_SCORE_SOFTMAX) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) m = fmaxf(m, l[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float ex[PER];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      ex[j] = lane + 32 * j < E ? expf(l[j] - m) : 0.f;
+      float s = ex[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      sum += s;
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = ex[j] / sum;
+  } else if (score_func == DSV4_SCORE_SIGMOID) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = 1.f / (1.f + expf(-l[j]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = sqrtf(softplus_f(l[j]));
+  }
+  float ch[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int ej = lane + 32 * j;
+    ch[j] = ej < E ? (bias ? sc[j] + bias[ej] : sc[j]) : -INFINITY;
+  }
+  float wsel = 0.f;   // lane r keeps pick r
+  int isel = 0;
+  for (int r = 0; r < K; ++r) {
+    int pick;
+    if (tid2eid) {
+      const int64_t id = ids[t];
+      pick = (id >= 0 && id < vocab) ? tid2eid[id * K + r] : E;
+    } else {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int ej = lane + 32 * j;
+        if (ej < E && (ch[j] > bv || (ch[j] == bv && ej < bi))) {
+          bv = ch[j];
+          bi = ej;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      pick = bi;
+      if ((pick & 31) == lane) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j)
+          if (j == (pick >> 5)) ch[j] = -INFINITY;
+      }
+    }
+    // the unbiased score of the pick, from the lane that holds it
+    const bool ok = pick >= 0 && pick < E;
+    float mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (ok && j == (pick >> 5)) mine = sc[j];
+    const float sp = __shfl_sync(0xffffffffu, mine, ok ? (pick & 31) : 0);
+    if (lane == r) {
+      wsel = ok ? sp : 0.f;
+      isel = pick;
+    }
+  }
+  float ssum = 0.f;
+  for (int r = 0; r < K; ++r) ssum += __shfl_sync(0xffffffffu, wsel, r);
+  if (lane < K) {
+    const float v = (isel >= E) ? 0.f : (renorm ? wsel / ssum : wsel);
+    w_out[t * K + lane] = v * scale;
+    i_out[t * K + lane] = isel;
+  }
+}
+
+__global__ __launch_bounds__(256) void route_topk_warp_kernel(const float* __restrict__ logits, int split, int64_t T,
+                                                              int E, int K, int score_func, int renorm, float scale,
+                                                              const float* __restrict__ bias,
+                                                              const int32_t* __restrict__ tid2eid,
+                                                              const int64_t* __restrict__ ids, int64_t vocab,
+                                                              float* __restrict__ w_out, int32_t* __restrict__ i_out,
+                                                              const int* __restrict__ err) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  if (err && *reinterpret_cast<const volatile int*>(err) != 0) {
+    if ((int)(threadIdx.x & 31) < K) {   // the logits kernel gave up on a wait: picks out of range
+      w_out[t * K + (threadIdx.x & 31)] = 0.f;
+      i_out[t * K + (threadIdx.x & 31)] = E;
+    }
+    return;
+  }
+  topk_token_warp(t, logits, split, T, E, K, score_func, renorm, scale, bias, tid2eid, ids, vocab, w_out, i_out);
+}
+
 // picks of a token whose logits are not available (a wait gave up):
 // expert id E is out of range, so the layer's align rejects them and its
 // status reports it
@@ -719,9 +859,14 @@ extern "C" int dsv4_route_topk(const void* x_bf16, const float* gate_w, const fl
     DSV4_CUDA_CHECK(launch_k(route_logits_kernel, grid, dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, gate_w,
                              (float*)workspace, n_tokens, hidden, n_experts, (int)RL_SLICE));
   }
-  DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl, logits, split,
-                           n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid, input_ids,
-                           vocab_size, weights_out, indices_out, err));
+  if (n_tokens >= RTC_MIN_TOKENS)   // a few slices per logit: a warp per token, 8 tokens per CTA
+    DSV4_CUDA_CHECK(launch_k(route_topk_warp_kernel, dim3((unsigned)((n_tokens + 7) / 8)), dim3(256), 0, st, pdl,
+                             logits, split, n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias,
+                             tid2eid, input_ids, vocab_size, weights_out, indices_out, err));
+  else   // 32 slices per logit: a CTA per token, a thread per expert
+    DSV4_CUDA_CHECK(launch_k(route_topk_kernel, dim3((unsigned)n_tokens), dim3(256), 0, st, pdl, logits, split,
+                             n_tokens, n_experts, topk, score_func, renormalize, route_scale, bias, tid2eid,
+                             input_ids, vocab_size, weights_out, indices_out, err));
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
