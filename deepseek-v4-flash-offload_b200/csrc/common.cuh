@@ -126,6 +126,37 @@ __device__ __forceinline__ uint32_t e2m1_code(float x) {
   return (c & 7u) ? c : 0u;
 }
 
+// Activation quantisation of one 128-column block held by a warp, four
+// consecutive columns per lane (lane L: columns 4L..4L+3), as the layer's
+// quantise-gather does it (the reference's act_quant / dynamic MX quant):
+//   FP8: one E4M3 byte per column, the block's scale 2^e with
+//        e = fp8_scale_exp(amax of the 128); returns the lane's 4 bytes;
+//   MXFP4: one E2M1 code per column, a scale 2^e per 32 columns (lanes
+//        8g..8g+7), e = mx_scale_exp(amax of the 32); returns the lane's 4
+//        codes packed low nibble first.
+__device__ __forceinline__ uint32_t fp8_block_quant(const float v[4], int* e_out) {
+  float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  const int e = fp8_scale_exp(a);
+  const float inv_s = pow2i(-e);
+  uint32_t o = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv_s, -448.f), 448.f)) << (8 * i);
+  *e_out = e;
+  return o;
+}
+__device__ __forceinline__ uint32_t mxfp4_block_quant(const float v[4], int* e_out) {
+  float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  const int e = mx_scale_exp(a);
+  const float inv_s = pow2_any(-e);
+  *e_out = e;
+  return e2m1_code(v[0] * inv_s) | (e2m1_code(v[1] * inv_s) << 4) | (e2m1_code(v[2] * inv_s) << 8) |
+         (e2m1_code(v[3] * inv_s) << 12);
+}
+
 // ---------------------------------------------------------------------------
 // status word shared by a kernel and its host wrapper
 // ---------------------------------------------------------------------------

@@ -348,16 +348,21 @@ __device__ __forceinline__ void ep_publish(uint32_t* __restrict__ ctrl, int coun
   }
 }
 
-// One warp per (token, destination) with an expert there: the token's row,
-// its picks with the other ranks' experts set to -1 (weight 0) and its
-// source into the owner's block at the compact row off[d] + pos[t][d].  The
-// offsets come from this rank's copy of the count matrix (every source wrote
-// its row before the wait that precedes this kernel).
+// One warp per token: the row goes to every destination rank with at least
+// one of its experts, at the compact row off[d] + pos[t][d] of the owner's
+// block, with its picks (the other ranks' experts set to -1, weight 0) and
+// its source.  The offsets come from this rank's copy of the count matrix
+// (every source wrote its row before the wait that precedes this kernel).
+// Row format (DSV4_ROWS_*): bf16 as it is, or quantised here once for all
+// destinations exactly as the owner's quantise-gather would (FP8 per 128 /
+// MXFP4 per 32), so that fewer bytes cross NVLink; the block scales follow
+// the codes in the same row.
+template <int FMT>
 __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
                                    const float* __restrict__ w, const int32_t* __restrict__ pos, int64_t T, int topk,
                                    int H, int E, int e_loc, const int32_t* __restrict__ owner, int world, int my_rank,
                                    uint8_t* const* __restrict__ peers, EpBlock blk, const int32_t* __restrict__ cnt,
-                                   uint32_t* __restrict__ ctrl) {
+                                   uint32_t* __restrict__ ctrl, int64_t row_bytes) {
   __shared__ int64_t off[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
@@ -370,22 +375,80 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t pr = warp0; pr < T * world; pr += nwarps) {
-    const int p = pos[pr];
-    if (p < 0) continue;
-    const int64_t t = pr / world;
-    const int d = (int)(pr - t * world);
-    const int64_t row = off[d] + p;
-    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
-    uint4* dst = reinterpret_cast<uint4*>(peers[d]) + row * (H / 8);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
-    if (lane < topk) {
-      const int e = idx[t * topk + lane];
-      const bool mine = e >= 0 && e < E && ep_dest(e, e_loc, owner) == d;
-      reinterpret_cast<int32_t*>(peers[d] + blk.off_idx)[row * topk + lane] = mine ? e : -1;
-      reinterpret_cast<float*>(peers[d] + blk.off_w)[row * topk + lane] = mine ? w[t * topk + lane] : 0.f;
+  const int kblk = H / 128;
+  for (int64_t t = warp0; t < T; t += nwarps) {
+    // destinations of this token: lane d < world holds its row there, or -1
+    const int p = lane < world ? pos[t * world + lane] : -1;
+    const int64_t my_row = p >= 0 ? off[lane] + p : -1;
+    const unsigned dests = __ballot_sync(0xffffffffu, p >= 0);
+    if (dests == 0u) continue;
+    uint32_t scl[2] = {0u, 0u};   // lane L: the scale(s) of block L (and L + 32)
+    for (int kb = 0; kb < kblk; ++kb) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(x + t * H + kb * 128 + lane * 4);
+      if constexpr (FMT == DSV4_ROWS_BF16) {
+        for (unsigned m = dests; m; m &= m - 1u) {
+          const int d = __ffs(m) - 1;
+          const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+          *reinterpret_cast<uint2*>(peers[d] + row * row_bytes + (int64_t)(kb * 128 + lane * 4) * 2) = raw;
+        }
+      } else {
+        const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
+                            bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
+        int e;
+        if constexpr (FMT == DSV4_ROWS_FP8) {
+          const uint32_t o = fp8_block_quant(v, &e);
+          if (lane == (kb & 31)) scl[kb >> 5] = (uint32_t)(e + 127);
+          for (unsigned m = dests; m; m &= m - 1u) {
+            const int d = __ffs(m) - 1;
+            const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+            *reinterpret_cast<uint32_t*>(peers[d] + row * row_bytes + kb * 128 + lane * 4) = o;
+          }
+        } else {
+          const uint32_t packed = mxfp4_block_quant(v, &e);
+          const uint32_t sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
+                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
+                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
+                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
+          if (lane == (kb & 31)) scl[kb >> 5] = sword;
+          for (unsigned m = dests; m; m &= m - 1u) {
+            const int d = __ffs(m) - 1;
+            const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+            *reinterpret_cast<uint16_t*>(peers[d] + row * row_bytes + kb * 64 + lane * 2) = (uint16_t)packed;
+          }
+        }
+      }
     }
-    if (lane == 0) reinterpret_cast<int2*>(peers[d] + blk.off_src)[row] = make_int2(my_rank, (int)t);
+    if constexpr (FMT != DSV4_ROWS_BF16) {
+      // the block scales after the codes: one byte (FP8) or one word of four
+      // (MXFP4) per 128 columns, lane L storing block L's
+      for (unsigned m = dests; m; m &= m - 1u) {
+        const int d = __ffs(m) - 1;
+        const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+        uint8_t* base = peers[d] + row * row_bytes + (FMT == DSV4_ROWS_FP8 ? H : H / 2);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int kb = lane + 32 * h;
+          if (kb < kblk) {
+            if (FMT == DSV4_ROWS_FP8)
+              base[kb] = (uint8_t)scl[h];
+            else
+              reinterpret_cast<uint32_t*>(base)[kb] = scl[h];
+          }
+        }
+      }
+    }
+    // picks and source, per destination
+    for (unsigned m = dests; m; m &= m - 1u) {
+      const int d = __ffs(m) - 1;
+      const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+      if (lane < topk) {
+        const int e = idx[t * topk + lane];
+        const bool mine = e >= 0 && e < E && ep_dest(e, e_loc, owner) == d;
+        reinterpret_cast<int32_t*>(peers[d] + blk.off_idx)[row * topk + lane] = mine ? e : -1;
+        reinterpret_cast<float*>(peers[d] + blk.off_w)[row * topk + lane] = mine ? w[t * topk + lane] : 0.f;
+      }
+      if (lane == 0) reinterpret_cast<int2*>(peers[d] + blk.off_src)[row] = make_int2(my_rank, (int)t);
+    }
   }
   ep_publish(ctrl, EPC_ROWS, peers, world, blk.off_flags, 1 * world + my_rank);
 }
@@ -570,13 +633,40 @@ extern "C" int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x, int32_t** recv_indice
   DSV4_API_END
 }
 
+extern "C" int64_t dsv4_ep_row_bytes(int32_t row_format, int32_t hidden) {
+  if (hidden <= 0 || hidden % 128 != 0) return DSV4_EINVAL;
+  const int64_t H = hidden;
+  int64_t b;
+  if (row_format == DSV4_ROWS_BF16)
+    b = 2 * H;
+  else if (row_format == DSV4_ROWS_FP8)
+    b = H + H / 128;
+  else if (row_format == DSV4_ROWS_MXFP4)
+    b = H / 2 + H / 32;
+  else
+    return DSV4_EINVAL;
+  return (b + 15) / 16 * 16;
+}
+
 extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights,
                                 const int32_t* route_indices, int64_t n_tokens, int32_t n_experts,
                                 const int32_t* expert_owner, int32_t* ordered_assignments, int* status,
                                 void* stream) {
+  return dsv4_ep_dispatch_q(ep, x_bf16, route_weights, route_indices, n_tokens, n_experts, expert_owner,
+                            ordered_assignments, DSV4_ROWS_BF16, status, stream);
+}
+
+extern "C" int dsv4_ep_dispatch_q(dsv4_ep* ep, const void* x_bf16, const float* route_weights,
+                                  const int32_t* route_indices, int64_t n_tokens, int32_t n_experts,
+                                  const int32_t* expert_owner, int32_t* ordered_assignments, int32_t row_format,
+                                  int* status, void* stream) {
   DSV4_API_BEGIN
   if (int rc = ep_check(ep)) return rc;
   DSV4_CHECK_ARG(x_bf16 && route_weights && route_indices && ordered_assignments && status, "null pointer");
+  DSV4_CHECK_ARG(row_format >= DSV4_ROWS_BF16 && row_format <= DSV4_ROWS_MXFP4, "unknown row format");
+  DSV4_CHECK_ARG(ep->world <= 32, "the peer-memory exchange takes at most 32 ranks");
+  DSV4_CHECK_ARG(ep->hidden % 128 == 0 && ep->hidden <= 8192, "hidden must be a multiple of 128, at most 8192");
+  const int64_t row_bytes = dsv4_ep_row_bytes(row_format, ep->hidden);
   DSV4_CHECK_ARG(n_tokens >= 0 && n_tokens <= ep->tokens, "n_tokens must be in [0, the handle's max_tokens]");
   DSV4_CHECK_ARG(n_experts > 0 && (expert_owner || n_experts % ep->world == 0),
                  "n_experts must divide over the ranks (or pass expert_owner)");
@@ -597,12 +687,14 @@ extern "C" int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* ro
                            ep->blk.off_flags, ctrl, pos, ordered_assignments, status));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags, (const uint32_t*)ctrl,
                            ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
-  const int64_t pairs = T * ep->world;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((pairs * 32 + 255) / 256, 148 * 8));
-  DSV4_CUDA_CHECK(launch_k(ep_p2p_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl,
-                           (const uint16_t*)x_bf16, route_indices, route_weights, (const int32_t*)pos, T, k,
-                           ep->hidden, (int)n_experts, e_loc, expert_owner, ep->world, ep->rank, peers, ep->blk, cnt,
-                           ctrl));
+  // a warp per token
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((T * 32 + 255) / 256, 148 * 8));
+  auto rows_kernel = row_format == DSV4_ROWS_FP8     ? ep_p2p_rows_kernel<DSV4_ROWS_FP8>
+                     : row_format == DSV4_ROWS_MXFP4 ? ep_p2p_rows_kernel<DSV4_ROWS_MXFP4>
+                                                     : ep_p2p_rows_kernel<DSV4_ROWS_BF16>;
+  DSV4_CUDA_CHECK(launch_k(rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl, (const uint16_t*)x_bf16,
+                           route_indices, route_weights, (const int32_t*)pos, T, k, ep->hidden, (int)n_experts, e_loc,
+                           expert_owner, ep->world, ep->rank, peers, ep->blk, cnt, ctrl, row_bytes));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags + ep->world,
                            (const uint32_t*)ctrl, ep->world, status, cnt, ep->rank, ctrl + EPC_NRECV));
   // the return targets of the received assignments (for the scatter-mode down GEMM)

@@ -506,10 +506,18 @@ __host__ __device__ __forceinline__ int64_t act_sf_offset(int64_t row, int kt, i
 // quantised once, then written to the sorted rows of its topk assignments
 // (inv[t*topk + j]), 4 bytes per lane per row; lanes 0..topk-1 store the
 // rows' scale words.
-__global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                        int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
-                                        uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-                                        const int32_t* __restrict__ n_tokens_dev) {
+// IN = DSV4_ROWS_BF16: x is [n_tokens][K] bf16, quantised here (FP8 per
+// 128: one E4M3 byte per column and the block exponent fp8_scale_exp(amax);
+// MXFP4 (a4w4) per 32: an E8M0 scale floor(log2(amax/6)) + 127 and E2M1
+// codes, round to nearest even, saturating; lanes 8g..8g+7 own block g).
+// IN = DSV4_ROWS_FP8 / DSV4_ROWS_MXFP4: x holds rows of row_bytes already
+// quantised the same way at the token's source (the expert-parallel
+// dispatch), codes then block scales; they are only gathered.
+template <bool FP4, int IN>
+__global__ void quant_gather_kernel(const uint8_t* __restrict__ x, int64_t row_bytes, const int32_t* __restrict__ inv,
+                                    int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
+                                    uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                    const int32_t* __restrict__ n_tokens_dev) {
   griddep_wait();
   griddep_launch();
   if (n_tokens_dev) n_tokens = min(n_tokens, (int64_t)max(0, *n_tokens_dev));
@@ -523,64 +531,50 @@ __global__ void quant_gather_fp8_kernel(const uint16_t* __restrict__ x, const in
     const int kb = (int)(b - tok * kblk);
     const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
     if (__ballot_sync(0xffffffffu, my_row >= 0) == 0u) continue;   // no assignment to write
-    const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
-    const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
-                        bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
-    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    a = warp_max_f(a);
-    const int e = fp8_scale_exp(a);
-    const float inv_s = pow2i(-e);
-    uint32_t o = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o |= e4m3_byte(fminf(fmaxf(v[i] * inv_s, -448.f), 448.f)) << (8 * i);
-    for (int j = 0; j < topk; ++j) {
-      const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
-      if (row >= 0) *reinterpret_cast<uint32_t*>(q + row * K + kb * 128 + lane * 4) = o;
+    const uint8_t* xr = x + tok * row_bytes;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (IN == DSV4_ROWS_BF16) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(xr + (int64_t)(kb * 128 + lane * 4) * 2);
+      v[0] = bf16_from_bits(raw.x & 0xffffu);
+      v[1] = bf16_from_bits(raw.x >> 16);
+      v[2] = bf16_from_bits(raw.y & 0xffffu);
+      v[3] = bf16_from_bits(raw.y >> 16);
     }
-    if (my_row >= 0)
-      *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = (uint32_t)(e + 127) * 0x01010101u;
-  }
-}
-
-// MXFP4 (a4w4): per 32 columns an E8M0 scale floor(log2(amax/6)) + 127 and
-// E2M1 codes, round to nearest even, saturating; lanes 8g..8g+7 own block g.
-__global__ void quant_gather_mxfp4_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
-                                          int64_t n_tokens, int topk, int K, int64_t rb_cap, int bn,
-                                          uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-                                          const int32_t* __restrict__ n_tokens_dev) {
-  griddep_wait();
-  griddep_launch();
-  if (n_tokens_dev) n_tokens = min(n_tokens, (int64_t)max(0, *n_tokens_dev));
-  const int lane = threadIdx.x & 31;
-  const int kblk = K / 128;
-  const int64_t ntask = n_tokens * kblk;
-  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t b = warp0; b < ntask; b += nwarps) {
-    const int64_t tok = b / kblk;
-    const int kb = (int)(b - tok * kblk);
-    const int my_row = lane < topk ? inv[tok * topk + lane] : -1;
-    if (__ballot_sync(0xffffffffu, my_row >= 0) == 0u) continue;   // no assignment to write
-    const uint2 raw = *reinterpret_cast<const uint2*>(x + tok * K + kb * 128 + lane * 4);
-    const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
-                        bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
-    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const int e = mx_scale_exp(a);
-    const float inv_s = pow2_any(-e);
-    const uint32_t packed = e2m1_code(v[0] * inv_s) | (e2m1_code(v[1] * inv_s) << 4) |
-                            (e2m1_code(v[2] * inv_s) << 8) | (e2m1_code(v[3] * inv_s) << 12);
-    // the four block scales of this 128-column block as one word
-    const uint32_t sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
-                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
-                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
-                           ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
-    for (int j = 0; j < topk; ++j) {
-      const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
-      if (row >= 0) *reinterpret_cast<uint16_t*>(q + row * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
+    if constexpr (!FP4) {
+      uint32_t o;
+      int e;
+      if constexpr (IN == DSV4_ROWS_BF16) {
+        o = fp8_block_quant(v, &e);
+      } else {
+        o = *reinterpret_cast<const uint32_t*>(xr + kb * 128 + lane * 4);
+        e = (int)xr[K + kb] - 127;
+      }
+      for (int j = 0; j < topk; ++j) {
+        const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
+        if (row >= 0) *reinterpret_cast<uint32_t*>(q + row * K + kb * 128 + lane * 4) = o;
+      }
+      if (my_row >= 0)
+        *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = (uint32_t)(e + 127) * 0x01010101u;
+    } else {
+      uint32_t packed, sword;
+      if constexpr (IN == DSV4_ROWS_BF16) {
+        int e;
+        packed = mxfp4_block_quant(v, &e);
+        // the four block scales of this 128-column block as one word
+        sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
+                ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
+                ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
+                ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
+      } else {
+        packed = *reinterpret_cast<const uint16_t*>(xr + kb * 64 + lane * 2);
+        sword = *reinterpret_cast<const uint32_t*>(xr + K / 2 + kb * 4);
+      }
+      for (int j = 0; j < topk; ++j) {
+        const int64_t row = __shfl_sync(0xffffffffu, my_row, j);
+        if (row >= 0) *reinterpret_cast<uint16_t*>(q + row * (K / 2) + kb * 64 + lane * 2) = (uint16_t)packed;
+      }
+      if (my_row >= 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = sword;
     }
-    if (my_row >= 0) *reinterpret_cast<uint32_t*>(sf + act_sf_offset(my_row, kb, rb_cap, bn)) = sword;
   }
 }
 
@@ -1029,6 +1023,8 @@ struct PassArgs {
   const uint16_t* extra;
   bool timed;                // records the stage events
   uint16_t* const* assign_dst = nullptr;   // down GEMM scatter targets (expert parallelism)
+  int x_format = DSV4_ROWS_BF16;           // rows of x: bf16, or quantised at their source
+  int64_t x_row_bytes = 0;                 // bytes per row of a quantised x
 };
 
 static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int64_t n_tokens,
@@ -1076,9 +1072,14 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
     const int64_t warps = n_tokens * (p->H / 128);
     int64_t blocks = (warps * 32 + 255) / 256;
     blocks = std::min<int64_t>(blocks, (int64_t)p->num_sms * 16);
-    DSV4_CUDA_CHECK(launch_k(a.fp4 ? quant_gather_mxfp4_kernel : quant_gather_fp8_kernel, dim3((unsigned)blocks),
-                             dim3(256), 0, st, pdl, (const uint16_t*)x_bf16, (const int32_t*)inv, n_tokens,
-                             a.topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf, n_tokens_dev));
+    auto qk = a.x_format == DSV4_ROWS_FP8     ? quant_gather_kernel<false, DSV4_ROWS_FP8>
+              : a.x_format == DSV4_ROWS_MXFP4 ? quant_gather_kernel<true, DSV4_ROWS_MXFP4>
+              : a.fp4                         ? quant_gather_kernel<true, DSV4_ROWS_BF16>
+                                              : quant_gather_kernel<false, DSV4_ROWS_BF16>;
+    const int64_t row_bytes = a.x_format == DSV4_ROWS_BF16 ? 2 * (int64_t)p->H : a.x_row_bytes;
+    DSV4_CUDA_CHECK(launch_k(qk, dim3((unsigned)blocks), dim3(256), 0, st, pdl, (const uint8_t*)x_bf16, row_bytes,
+                             (const int32_t*)inv, n_tokens, a.topk, p->H, rb_cap, bn, p->ws + w.xq, p->ws + w.xsf,
+                             n_tokens_dev));
   }
   mark(2);
   GemmParams g1{};
@@ -1158,7 +1159,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
 static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf16, int64_t n_tokens,
                             const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
                             const int32_t* slot_of_expert, const uint8_t* shared_slot, void* y_bf16, void* stream,
-                            uint16_t* const* assign_dst = nullptr) {
+                            uint16_t* const* assign_dst = nullptr, int x_format = DSV4_ROWS_BF16) {
   DSV4_API_BEGIN
   DSV4_CHECK_ARG(p && x_bf16 && route_weights && route_indices && slot_of_expert, "null pointer");
   DSV4_CHECK_ARG(profile == DSV4_PROFILE_BF16 || profile == DSV4_PROFILE_A4W4, "unknown profile");
@@ -1172,8 +1173,13 @@ static int moe_forward_impl(dsv4_moe_plan* p, int32_t profile, const void* x_bf1
   cudaStream_t st = (cudaStream_t)stream;
   const bool fp4 = profile == DSV4_PROFILE_A4W4;
   DSV4_CHECK_ARG(!assign_dst || (!y_bf16 && !p->shared), "scatter mode writes no y and runs no shared expert");
+  DSV4_CHECK_ARG(x_format == DSV4_ROWS_BF16 || (!p->shared && x_format == (fp4 ? DSV4_ROWS_MXFP4 : DSV4_ROWS_FP8)),
+                 "quantised rows must be in the profile's format (FP8 for bf16, MXFP4 for a4w4), without a shared "
+                 "expert");
   if (!p->shared) {
-    const PassArgs a{fp4, p->topk, p->topk, -1, nullptr, nullptr, nullptr, nullptr, true, assign_dst};
+    PassArgs a{fp4, p->topk, p->topk, -1, nullptr, nullptr, nullptr, nullptr, true, assign_dst};
+    a.x_format = x_format;
+    a.x_row_bytes = x_format == DSV4_ROWS_BF16 ? 0 : dsv4_ep_row_bytes(x_format, p->H);
     if (int rc = moe_pass(p, a, x_bf16, n_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
                           y_bf16, st))
       return rc;
@@ -1240,6 +1246,15 @@ extern "C" int dsv4_moe_forward_scatter(dsv4_moe_plan* p, int32_t profile, const
   if (!assign_dst) return fail(DSV4_EINVAL, "dsv4_moe_forward_scatter: null assign_dst");
   return moe_forward_impl(p, profile, x_bf16, max_tokens, n_tokens_dev, route_weights, route_indices,
                           slot_of_expert, nullptr, nullptr, stream, reinterpret_cast<uint16_t* const*>(assign_dst));
+}
+
+extern "C" int dsv4_moe_forward_scatter_q(dsv4_moe_plan* p, int32_t profile, const void* x_rows, int32_t x_format,
+                                          int64_t max_tokens, const int32_t* n_tokens_dev,
+                                          const float* route_weights, const int32_t* route_indices,
+                                          const int32_t* slot_of_expert, void* const* assign_dst, void* stream) {
+  if (!assign_dst) return fail(DSV4_EINVAL, "dsv4_moe_forward_scatter_q: null assign_dst");
+  return moe_forward_impl(p, profile, x_rows, max_tokens, n_tokens_dev, route_weights, route_indices, slot_of_expert,
+                          nullptr, nullptr, stream, reinterpret_cast<uint16_t* const*>(assign_dst), x_format);
 }
 
 extern "C" int dsv4_moe_output_rows(dsv4_moe_plan* p, void** rows_bf16, int32_t** inv) {

@@ -24,6 +24,8 @@ DSV4_EUNSUPPORTED = -7
 
 SCORE_FUNCS = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 PROFILES = {"bf16": 0, "a4w4": 1}
+# token row formats of the expert-parallel dispatch (DSV4_ROWS_*)
+ROWS_BF16, ROWS_FP8, ROWS_MXFP4 = 0, 1, 2
 
 _p, _i32, _i64, _f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
 
@@ -52,6 +54,7 @@ SIGNATURES = {
     "dsv4_moe_forward_rows": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_moe_output_rows": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p)]),
     "dsv4_moe_forward_scatter": (C.c_int, [_p, _i32, _p, _i64, _p, _p, _p, _p, _p, _p]),
+    "dsv4_moe_forward_scatter_q": (C.c_int, [_p, _i32, _p, _i32, _i64, _p, _p, _p, _p, _p, _p]),
     "dsv4_shared_slot_bytes": (_i64, [_i32, _i32]),
     "dsv4_pack_shared_host": (C.c_int, [_p, _p, _p, _p, _p, _p, _i32, _i32, _p]),
     "dsv4_moe_workspace_bytes_ex": (_i64, [_i32, _i32, _i32, _i32, _i64, _i32]),
@@ -86,6 +89,8 @@ SIGNATURES = {
     "dsv4_ep_connect": (C.c_int, [_p, _p]),
     "dsv4_ep_buffers": (C.c_int, [_p, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), C.POINTER(_p)]),
     "dsv4_ep_dispatch": (C.c_int, [_p, _p, _p, _p, _i64, _i32, _p, _p, _p, _p]),
+    "dsv4_ep_dispatch_q": (C.c_int, [_p, _p, _p, _p, _i64, _i32, _p, _p, _i32, _p, _p]),
+    "dsv4_ep_row_bytes": (C.c_int64, [_i32, _i32]),
     "dsv4_ep_return": (C.c_int, [_p, _p, _p, _p, _p]),
     "dsv4_ep_return_targets": (C.c_int, [_p, C.POINTER(_p)]),
     "dsv4_ep_return_published": (C.c_int, [_p, _p, _p]),

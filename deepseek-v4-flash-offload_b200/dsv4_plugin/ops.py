@@ -19,7 +19,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import PROFILES, SCORE_FUNCS, check, lib
+from ._lib import PROFILES, ROWS_BF16, ROWS_FP8, ROWS_MXFP4, SCORE_FUNCS, check, lib  # noqa: F401
 
 _E8M0 = getattr(torch, "float8_e8m0fnu", None)
 
@@ -349,13 +349,18 @@ class MoEPlan:
         return self.output_rows(t * self.topk)
 
     def forward_scatter(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, slot_of: torch.Tensor,
-                        assign_dst_ptr: int, profile: str = "bf16", n_tokens_dev: torch.Tensor | None = None) -> None:
+                        assign_dst_ptr: int, profile: str = "bf16", n_tokens_dev: torch.Tensor | None = None,
+                        x_format: int = ROWS_BF16) -> None:
         """The layer whose down GEMM stores the output row of assignment a
         straight to the device address table ``assign_dst_ptr`` [T * k]
-        (another GPU's memory included; null entries are dropped)."""
+        (another GPU's memory included; null entries are dropped).  With
+        ``x_format`` ROWS_FP8 (bf16 profile) or ROWS_MXFP4 (a4w4), x is uint8
+        [T, row_bytes] rows quantised at their source."""
         _need_cuda(x, weights, indices, slot_of)
-        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        if x_format == ROWS_BF16 and (x.dtype != torch.bfloat16 or not x.is_contiguous()):
             raise TypeError("x must be contiguous bf16")
+        if x_format != ROWS_BF16 and (x.dtype != torch.uint8 or not x.is_contiguous()):
+            raise TypeError("quantised rows must be a contiguous uint8 tensor")
         t = x.shape[0]
         if t > self.max_tokens:
             raise ValueError(f"{t} tokens exceed the plan's max_tokens={self.max_tokens}")
@@ -363,10 +368,10 @@ class MoEPlan:
         idx = indices if indices.dtype == torch.int32 and indices.is_contiguous() else \
             indices.contiguous().to(torch.int32)
         so = slot_of.contiguous().to(torch.int32)
-        check(lib().dsv4_moe_forward_scatter(self._h, PROFILES[profile], x.data_ptr(), t,
-                                             None if n_tokens_dev is None else n_tokens_dev.data_ptr(),
-                                             w.data_ptr(), idx.data_ptr(), so.data_ptr(), assign_dst_ptr,
-                                             _stream(x.device)))
+        check(lib().dsv4_moe_forward_scatter_q(self._h, PROFILES[profile], x.data_ptr(), int(x_format), t,
+                                               None if n_tokens_dev is None else n_tokens_dev.data_ptr(),
+                                               w.data_ptr(), idx.data_ptr(), so.data_ptr(), assign_dst_ptr,
+                                               _stream(x.device)))
 
     def output_rows(self, n_assign: int):
         rp, ip = C.c_void_p(), C.c_void_p()

@@ -26,6 +26,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from dsv4_plugin._lib import ROWS_BF16, ROWS_FP8, ROWS_MXFP4
+
 
 def contiguous_placement(n_experts: int, world: int) -> list:
     """owner[e] = e // (E / R)."""
@@ -240,18 +242,26 @@ class P2PExchange:
                                     device=dev).view(torch.bfloat16)
         self.ordered = torch.empty((tokens, topk), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        # the receive rows seen as quantised rows (uint8 [rows, row_bytes]) per format
+        self._recv_q = {}
+        for fmt in (ROWS_FP8, ROWS_MXFP4):
+            rb = int(lib().dsv4_ep_row_bytes(fmt, hidden))
+            self._recv_q[fmt] = torch.as_tensor(_DevPtr(rx.value, (rows, rb), "|u1"), device=dev)
 
-    def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
+    def dispatch(self, x: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor, row_format: int = ROWS_BF16):
         """-> (recv_x, recv_indices, recv_weights, n_recv): the received tokens
-        (the first *n_recv rows of the buffers) and their device-side count."""
+        (the first *n_recv rows of the buffers) and their device-side count.
+        With ``row_format`` ROWS_FP8 / ROWS_MXFP4 the tokens are quantised at
+        the source and recv_x is uint8 [rows, row_bytes] of quantised rows."""
         from dsv4_plugin._lib import check, lib
         x, w, i = x.contiguous(), weights.contiguous().float(), indices.contiguous().to(torch.int32)
         if x.shape[0] != self.t:
             raise ValueError(f"the exchange was made for {self.t} tokens, got {x.shape[0]}")
-        check(lib().dsv4_ep_dispatch(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.n_experts,
-                                     self.owner.data_ptr(), self.ordered.data_ptr(), self.status.data_ptr(),
-                                     torch.cuda.current_stream(self.device).cuda_stream))
-        return self.recv_x, self.recv_idx, self.recv_w, self.n_recv
+        check(lib().dsv4_ep_dispatch_q(self._h, x.data_ptr(), w.data_ptr(), i.data_ptr(), self.t, self.n_experts,
+                                       self.owner.data_ptr(), self.ordered.data_ptr(), int(row_format),
+                                       self.status.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+        rx = self.recv_x if row_format == ROWS_BF16 else self._recv_q[row_format]
+        return rx, self.recv_idx, self.recv_w, self.n_recv
 
     def return_targets(self) -> int:
         """Device address of the table of each received assignment's return
@@ -321,6 +331,9 @@ class ExpertParallelMoE:
         # (DSV4_EP_FUSED_RETURN=0: a separate return kernel after the layer)
         import os
         self.fused_return = os.environ.get("DSV4_EP_FUSED_RETURN", "1") != "0"
+        # the tokens cross NVLink quantised in the profile's format (FP8 rows
+        # for bf16, MXFP4 for a4w4; DSV4_EP_QUANT_DISPATCH=0: bf16 rows)
+        self.quant_dispatch = os.environ.get("DSV4_EP_QUANT_DISPATCH", "1") != "0"
 
     def forward_static(self, hs: torch.Tensor, profile: str = "bf16") -> torch.Tensor:
         """The same layer through ``StaticExchange``: no host synchronisation,
@@ -391,7 +404,10 @@ class ExpertParallelMoE:
         mark()
         w, idx = moe._route(hs, None)
         mark()
-        x_recv, i_recv, w_recv, n_recv = ex.dispatch(hs, w, idx)
+        fmt = ROWS_BF16
+        if self.fused_return and self.quant_dispatch:
+            fmt = ROWS_MXFP4 if profile == "a4w4" else ROWS_FP8
+        x_recv, i_recv, w_recv, n_recv = ex.dispatch(hs, w, idx, fmt)
         mark()
         plan = moe.engine.plan_for(moe.n_routed_experts, moe.topk, x_recv.shape[0], moe.swiglu_limit or 0.0)
         self.plan = plan
@@ -399,7 +415,7 @@ class ExpertParallelMoE:
             # the down GEMM's epilogue stores every output row straight into
             # its source's `back` over NVLink, tile by tile
             plan.forward_scatter(x_recv, w_recv, i_recv, self.slot_of, ex.return_targets(), profile,
-                                 n_tokens_dev=n_recv)
+                                 n_tokens_dev=n_recv, x_format=fmt)
             mark()
             back = ex.returned()
         else:

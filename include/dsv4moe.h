@@ -42,6 +42,18 @@ extern "C" {
 #define DSV4_PROFILE_BF16 0
 #define DSV4_PROFILE_A4W4 1
 
+/* token row formats of the expert-parallel dispatch (no counterpart in the
+ * reference, which sends bf16 through its all-to-all):
+ *   BF16: H bf16 values (2H bytes);
+ *   FP8:  H E4M3 bytes, then H/128 scale exponent bytes (e + 127, scale 2^e),
+ *         the bf16 profile's activation quantisation;
+ *   MXFP4: H/2 bytes of E2M1 codes (low nibble = even column), then H/32
+ *         E8M0 scale bytes, the a4w4 profile's;
+ * each row padded to a multiple of 16 bytes (dsv4_ep_row_bytes). */
+#define DSV4_ROWS_BF16 0
+#define DSV4_ROWS_FP8 1
+#define DSV4_ROWS_MXFP4 2
+
 const char* dsv4_last_error_string(void);
 int dsv4_abi_version(void);
 
@@ -205,6 +217,15 @@ int dsv4_moe_forward_rows(dsv4_moe_plan* plan, int32_t profile, const void* x_bf
 int dsv4_moe_forward_scatter(dsv4_moe_plan* plan, int32_t profile, const void* x_bf16, int64_t max_tokens,
                              const int32_t* n_tokens_dev, const float* route_weights, const int32_t* route_indices,
                              const int32_t* slot_of_expert, void* const* assign_dst, void* stream);
+/* dsv4_moe_forward_scatter on rows quantised at their source
+ * (dsv4_ep_dispatch_q; x_format DSV4_ROWS_FP8 with the bf16 profile,
+ * DSV4_ROWS_MXFP4 with a4w4, rows of dsv4_ep_row_bytes bytes): the layer
+ * only gathers them, with the results of the bf16 rows they came from.
+ * Plans without a shared expert.  No counterpart in the reference. */
+int dsv4_moe_forward_scatter_q(dsv4_moe_plan* plan, int32_t profile, const void* x_rows, int32_t x_format,
+                               int64_t max_tokens, const int32_t* n_tokens_dev, const float* route_weights,
+                               const int32_t* route_indices, const int32_t* slot_of_expert, void* const* assign_dst,
+                               void* stream);
 /* Device pointers of the last forward's per-assignment output rows (bf16
  * [rows, hidden], sorted by expert) and of inv (int32 [n_tokens * topk]). */
 int dsv4_moe_output_rows(dsv4_moe_plan* plan, void** rows_bf16, int32_t** inv);
@@ -412,6 +433,17 @@ int dsv4_ep_buffers(dsv4_ep* ep, void** recv_x_bf16, int32_t** recv_indices, flo
 int dsv4_ep_dispatch(dsv4_ep* ep, const void* x_bf16, const float* route_weights, const int32_t* route_indices,
                      int64_t n_tokens, int32_t n_experts, const int32_t* expert_owner, int32_t* ordered_assignments,
                      int* status, void* stream);
+/* dsv4_ep_dispatch with the rows sent in a quantised format (DSV4_ROWS_FP8
+ * for the bf16 profile, DSV4_ROWS_MXFP4 for a4w4): each token is quantised
+ * once at its source exactly as the owner's layer would quantise it, so the
+ * owner's results are unchanged and a row crosses NVLink in 4128 (FP8) or
+ * 2176 (MXFP4) bytes instead of 8192 at H = 4096.  recv_x then holds rows of
+ * dsv4_ep_row_bytes(row_format, hidden) bytes, which
+ * dsv4_moe_forward_scatter_q takes.  No counterpart in the reference. */
+int64_t dsv4_ep_row_bytes(int32_t row_format, int32_t hidden);
+int dsv4_ep_dispatch_q(dsv4_ep* ep, const void* x_bf16, const float* route_weights, const int32_t* route_indices,
+                       int64_t n_tokens, int32_t n_experts, const int32_t* expert_owner, int32_t* ordered_assignments,
+                       int32_t row_format, int* status, void* stream);
 int dsv4_ep_return(dsv4_ep* ep, const void* rows_bf16, const int32_t* row_of_assignment, int* status, void* stream);
 /* The return fused into the down GEMM: dsv4_ep_return_targets gives the
  * device table [world*max_tokens*topk] of each received assignment's

@@ -91,10 +91,23 @@ def _run(rank, world, port, tokens, out, scattered=False):
         del g
         torch.cuda.synchronize(dev)
         # exchange over NVLink peer memory, eager and captured (the return
-        # fused into the down GEMM), and with a separate return kernel
-        got = epm.forward_p2p(xt)
-        epm._p2p[xt.shape[0]].check_status()
-        ok = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        # fused into the down GEMM), both profiles with the tokens sent
+        # quantised at their source (FP8 / MXFP4 rows) and as bf16 rows, and
+        # with a separate return kernel
+        from dsv4_plugin.models import deepseek_v4 as DV4
+        ok = True
+        for profile in ("bf16", "a4w4"):
+            DV4._MXFP4_GMM = profile == "a4w4"
+            try:
+                refp = full.forward(xt).clone()
+            finally:
+                DV4._MXFP4_GMM = False
+            for quant in (True, False):
+                epm.quant_dispatch = quant
+                got = epm.forward_p2p(xt, profile)
+                epm._p2p[xt.shape[0]].check_status()
+                ok = ok and bool(torch.equal(got.view(torch.int16), refp.view(torch.int16)))
+        epm.quant_dispatch = True
         epm.fused_return = False
         got = epm.forward_p2p(xt)
         epm._p2p[xt.shape[0]].check_status()
