@@ -43,6 +43,19 @@ def test_slot_bytes(lib):
     assert L.dsv4_expert_slot_bytes(1152, 512) == lib.DSV4_EINVAL   # hidden must pair 128-row tiles
 
 
+def test_dispatch_row_bytes(lib):
+    """Bytes of one dispatched token row per format: bf16 2H; FP8 H codes
+    + H/128 exponents; MXFP4 H/2 codes + H/32 scales; padded to 16."""
+    L = lib.lib()
+    assert L.dsv4_ep_row_bytes(lib.ROWS_BF16, 4096) == 8192
+    assert L.dsv4_ep_row_bytes(lib.ROWS_FP8, 4096) == 4128
+    assert L.dsv4_ep_row_bytes(lib.ROWS_MXFP4, 4096) == 2176
+    assert L.dsv4_ep_row_bytes(lib.ROWS_FP8, 1024) == 1040        # 1024 + 8, padded to 16
+    assert L.dsv4_ep_row_bytes(lib.ROWS_MXFP4, 1024) == 544
+    assert L.dsv4_ep_row_bytes(3, 4096) == lib.DSV4_EINVAL
+    assert L.dsv4_ep_row_bytes(lib.ROWS_FP8, 1000) == lib.DSV4_EINVAL
+
+
 def _pack_py(w, sc, k, row_of, wout, sout):
     """Python restatement of the paired slot layout (256-row pairs x 128 K)."""
     rows = w.shape[0]
