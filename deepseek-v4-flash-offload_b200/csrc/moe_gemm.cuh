@@ -343,11 +343,39 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const uint8_t* sfb_base = q.b_sf + (int64_t)(cur.row0 / BN) * C::SF_BYTES;
         const int nb = b_rows_for<BN>(cur.nrows);
         const CUtensorMap* mB = nb == 16 ? &m.B16 : (nb == 32 ? &m.B32 : (nb == 64 ? &m.B64 : &m.Bwide));
-        const int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
+        int early = t == (int)blockIdx.x ? pre : 0;   // stages whose weights are already in flight
         const uint64_t pol_w = cur.reuse ? pol_reuse : pol_once;
         if (FUSED && cur.ph) {
           // the h rows of this chunk come from the gate/up tiles of other
-          // CTAs: wait until all of them have stored theirs
+          // CTAs: until all of them have stored theirs, fill the ring
+          // stages as they free up with this tile's weights (which do not
+          // depend on them), then wait
+          if (ld_acquire(p.chunk_done + cur.c) < p.a_row_tiles) {
+            const int npre = k_tiles < C::STAGES ? k_tiles : C::STAGES;
+            const uint32_t b_tx = (uint32_t)nb * (B_FP4 ? G_BK / 2 : G_BK);
+            int s = stage;
+            uint32_t ph = phase;
+            for (int kt = 0; kt < npre; ++kt) {
+              if (kt >= early) {
+                if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) {
+                  ok = false;
+                  break;
+                }
+                uint8_t* st = smem + s * C::STAGE_BYTES;
+                mbar_expect_tx(&full[s], atx + 2 * C::SF_BYTES + b_tx + C::SF_BYTES);
+                tma_load_5d(st, mA, &full[s], 0, 0, kt, cur.mt, cur.slot, pol_w);
+                bulk_load(st + NUM_A * C::A_BYTES + C::B_BYTES,
+                          sf_base + ((int64_t)cur.mt * k_tiles + kt) * 2 * C::SF_BYTES, 2 * C::SF_BYTES, &full[s],
+                          pol_w);
+              }
+              if (++s == C::STAGES) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+            if (!ok) break;
+            early = early > npre ? early : npre;
+          }
           if (!wait_count_geq(p.chunk_done + cur.c, p.a_row_tiles, p.status)) {
             ok = false;
             break;
