@@ -156,15 +156,15 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
     int e = -1;
     float wv = 0.f;
     if (tid < P) {
+      // both loads issued together (the weight does not depend on the id)
       e = assign_expert(idx, tid, topk, k_in, shared_e);
+      if (sorted_w) wv = assign_weight(w_flat, tid, topk, k_in, shared_e);
       if (e == -1) {   // an empty assignment (padding of the expert-parallel exchange)
         inv[tid] = -1;
       } else if (e < 0 || e >= E) {
         set_status(status, DSV4_EINVAL);
         inv[tid] = -1;
         e = -1;
-      } else if (sorted_w) {
-        wv = assign_weight(w_flat, tid, topk, k_in, shared_e);
       }
     }
     __syncthreads();
