@@ -336,108 +336,6 @@ __global__ void __launch_bounds__(AL_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// moe_align for decode batches (P <= 1024 assignments, E <= 1024): the
-// batch's expert ids are staged in shared memory as 16-bit values, and the
-// thread of expert x counts, then places, its assignments by scanning them
-// eight at a time (broadcast reads, SIMD compares, no atomics and no
-// per-warp tables).  The scan visits assignments in order, so the rows are
-// the stable counting sort's (token-major within an expert), as in
-// moe_align_kernel; the outputs are the same.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t match8(const uint4 v, uint32_t x2) {
-  // bit j set when entry j of the eight 16-bit values equals x
-  const uint32_t m0 = __vcmpeq2(v.x, x2), m1 = __vcmpeq2(v.y, x2), m2 = __vcmpeq2(v.z, x2), m3 = __vcmpeq2(v.w, x2);
-  return (m0 & 1u) | ((m0 >> 15) & 2u) | ((m1 & 1u) << 2) | ((m1 >> 13) & 8u) | ((m2 & 1u) << 4) |
-         ((m2 >> 11) & 32u) | ((m3 & 1u) << 6) | ((m3 >> 9) & 128u);
-}
-
-__global__ void __launch_bounds__(AL_THREADS, 1)
-    align_small_kernel(const int32_t* __restrict__ idx, int P, int topk, int E, const float* __restrict__ w_flat,
-                       int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_flat,
-                       int32_t* __restrict__ inv, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
-                       float* __restrict__ sorted_w, int4* __restrict__ chunks, int32_t* __restrict__ n_chunks,
-                       int pad, int* status, const int32_t* __restrict__ n_tokens_dev, int k_in, int shared_e,
-                       int* __restrict__ chunk_done, int max_chunks) {
-  __shared__ __align__(16) uint16_t es[AL_THREADS];   // expert of assignment a; 0xffff: none
-  __shared__ int run_s[AL_THREADS], cnt_s[AL_THREADS];
-  __shared__ int scratch[96];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  griddep_wait();
-  griddep_launch();
-  for (int j = tid; j < max_chunks; j += AL_THREADS) chunk_done[j] = 0;
-  if (n_tokens_dev) P = min(P, max(0, *n_tokens_dev) * topk);
-  uint16_t ev = 0xffffu;
-  if (tid < P) {
-    const int e = assign_expert(idx, tid, topk, k_in, shared_e);
-    if (e == -1) {   // an empty assignment (padding of the expert-parallel exchange)
-      inv[tid] = -1;
-    } else if (e < 0 || e >= E) {
-      set_status(status, DSV4_EINVAL);
-      inv[tid] = -1;
-    } else {
-      ev = (uint16_t)e;
-    }
-  }
-  es[tid] = ev;
-  __syncthreads();
-  const int n8 = (P + 7) >> 3;
-  const uint4* e8 = reinterpret_cast<const uint4*>(es);
-  const uint32_t x2 = (uint32_t)tid * 0x00010001u;
-  int c = 0;
-  if (tid < E) {
-    for (int i = 0; i < n8; ++i) {
-      const uint4 v = e8[i];
-      c += __popc(__vcmpeq2(v.x, x2)) + __popc(__vcmpeq2(v.y, x2)) + __popc(__vcmpeq2(v.z, x2)) +
-           __popc(__vcmpeq2(v.w, x2));
-    }
-    c >>= 4;   // 16 bits per equal entry
-  }
-  const int cpad = (c + pad - 1) / pad * pad;
-  const int nch = cpad / pad;
-  int3 tot3;
-  const int3 ex = block_scan3(cpad, c > 0 ? 1 : 0, nch, scratch, &tot3);
-  if (tid < E) {
-    run_s[tid] = ex.x;
-    cnt_s[tid] = c;
-    counts[tid] = c;
-    offsets[tid] = ex.x;
-    if (c > 0) active[ex.y] = tid;
-    if (chunks)
-      for (int j = 0; j < nch; ++j)
-        chunks[ex.z + j] = make_int4(tid, ex.x + j * pad, min(pad, c - j * pad), nch > 1);
-  }
-  if (tid == 0) {
-    offsets[E] = tot3.x;
-    *n_active = tot3.y;
-    if (chunks) *n_chunks = tot3.z;
-  }
-  // this expert's rows, in assignment order
-  if (tid < E && c > 0) {
-    int r = ex.x, left = c;
-    for (int i = 0; i < n8 && left > 0; ++i) {
-      for (uint32_t m = match8(e8[i], x2); m; m &= m - 1u) {
-        const int a = i * 8 + __ffs(m) - 1;
-        sorted_flat[r] = a;
-        inv[a] = r;
-        if (sorted_w) sorted_w[r] = assign_weight(w_flat, a, topk, k_in, shared_e);
-        ++r;
-        --left;
-      }
-    }
-  }
-  __syncthreads();
-  // padding rows of each group (fewer than `pad`), one warp per group so the
-  // stores of a warp are contiguous
-  for (int g = warp; g < E; g += AL_THREADS / 32) {
-    const int r0 = run_s[g] + cnt_s[g], r1 = run_s[g] + (cnt_s[g] + pad - 1) / pad * pad;
-    for (int r = r0 + lane; r < r1; r += 32) {
-      sorted_flat[r] = -1;
-      if (sorted_w) sorted_w[r] = 0.f;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // moe_align for large batches on many CTAs (the same stable counting sort):
 //   count  CTA b takes assignments [1024 b, 1024 b + 1024), one per thread,
 //          and writes its per-expert counts cnt_blk[b][E];
@@ -1140,6 +1038,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   int32_t* inv = wsp<int32_t>(p, w.inv);
   int32_t* n_active = wsp<int32_t>(p, w.n_active);
   int* n_chunks = wsp<int>(p, w.n_chunks);
+  const size_t al_smem = (size_t)(2 * p->E + 32 + AL_THREADS) * 4 + (size_t)32 * p->E * 4;
   auto mark = [&](int i) {
     if (p->timing && a.timed) cudaEventRecord(p->ev[i], st);
   };
@@ -1147,7 +1046,7 @@ static int moe_pass(dsv4_moe_plan* p, const PassArgs& a, const void* x_bf16, int
   const bool pdl = pdl_enabled() && !p->timing;
   mark(0);
   if (P <= AL_THREADS) {
-    DSV4_CUDA_CHECK(launch_k(align_small_kernel, dim3(1), dim3(AL_THREADS), 0, st, pdl, route_indices, P,
+    DSV4_CUDA_CHECK(launch_k(moe_align_kernel, dim3(1), dim3(AL_THREADS), al_smem, st, pdl, route_indices, P,
                              a.topk, p->E, route_weights, wsp<int32_t>(p, w.counts), wsp<int32_t>(p, w.offsets),
                              sorted_flat, inv, wsp<int32_t>(p, w.active), n_active, wsp<float>(p, w.sorted_w),
                              wsp<int4>(p, w.chunks), n_chunks, bn, status, n_tokens_dev, a.k_in, a.shared_e,
@@ -1479,14 +1378,9 @@ extern "C" int dsv4_moe_align(const int32_t* indices, int64_t n_tokens, int32_t 
   const size_t al_smem = (size_t)(2 * n_experts + 32 + AL_THREADS) * 4 + (size_t)32 * n_experts * 4;
   DSV4_CUDA_CHECK(
       cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)al_smem));
-  if (n_tokens * topk <= AL_THREADS)
-    align_small_kernel<<<1, AL_THREADS, 0, (cudaStream_t)stream>>>(
-        indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
-        nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0);
-  else
-    moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
-        indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active,
-        n_active, nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0);
+  moe_align_kernel<<<1, AL_THREADS, al_smem, (cudaStream_t)stream>>>(
+      indices, (int)(n_tokens * topk), topk, n_experts, nullptr, counts, offsets, sorted_flat, inv, active, n_active,
+      nullptr, nullptr, nullptr, 1, status, nullptr, topk, -1, nullptr, 0);
   DSV4_CUDA_CHECK(cudaGetLastError());
   DSV4_API_END
 }
