@@ -179,7 +179,8 @@ class OffloadDeepseekV4MoE(nn.Module):
 
     def _prefetch_next(self, hs: torch.Tensor, input_ids):
         """Warm the next layer's predicted experts while this layer computes
-        (the reference's planned prefetch, DESIGN.md:82 there): the next
+        (the prefetch the reference's design notes plan, line 82, but do not
+        implement): the next
         layer's gate applied to this layer's hidden states, or its hash table
         on the same token ids, on the bank's side stream."""
         bank = self.engine.bank
