@@ -180,9 +180,9 @@ class OffloadDeepseekV4MoE(nn.Module):
     def _prefetch_next(self, hs: torch.Tensor, input_ids):
         """Warm the next layer's predicted experts while this layer computes
         (the prefetch the reference's design notes plan, line 82, but do not
-        implement): the next
-        layer's gate applied to this layer's hidden states, or its hash table
-        on the same token ids, on the bank's side stream."""
+        implement): the next layer's gate applied to this layer's hidden
+        states, or its hash table on the same token ids, on the bank's side
+        stream."""
         bank = self.engine.bank
         nxt = self.engine.layer(self.layer_idx + 1) if self.engine.prefetch else None
         if nxt is None or bank._dir is None or (nxt.hash and input_ids is None):
