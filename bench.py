@@ -53,9 +53,11 @@ def _args(argv=None):
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-detail", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill", "offload"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "offload", "ep1"], default="decode",
                     help="decode: BASELINE config 1 (the headline); prefill: config 2 (T=2048, a4w4); "
-                         "offload: config 3 (8 layers, LRU slot cache fed from pinned host memory)")
+                         "offload: config 3 (8 layers, LRU slot cache fed from pinned host memory); "
+                         "ep1: config 4 through the expert-parallel exchange on one rank (a profiling aid: "
+                         "every kernel of the exchange runs, each token going to this rank)")
     ap.add_argument("--prefetch", action="store_true",
                     help="offload: copy the next layer's missing experts while the current layer computes")
     a = ap.parse_args(argv)
@@ -1115,7 +1117,8 @@ def _calibrated_placement(device, world: int):
     return balanced_placement(counts, world)
 
 
-def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), steps=None, warmup=None):
+def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), steps=None, warmup=None,
+               force_ep=False):
     """BASELINE config 4: E=256 experts sharded e // (E/N) over N ranks, a
     fixed step of 8192 tokens split evenly (T/N per rank), Zipf-skewed
     routing, both profiles.  world == 1 runs the plain single-GPU layer (all
@@ -1141,7 +1144,7 @@ def ep_config4(a, rank: int, world: int, device, profiles=("bf16", "a4w4"), step
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     exchange = os.environ.get("DSV4_EP_EXCHANGE", "p2p")
     epm = None
-    if world > 1:
+    if world > 1 or force_ep:
         from dsv4_plugin.parallel_ep import ExpertParallelMoE
         epm = ExpertParallelMoE(moe, rank, world, owner=owner)
 
@@ -1304,6 +1307,37 @@ def run_ep(a, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_ep1(a):
+    """--workload ep1: BASELINE config 4's 8192-token step through the
+    peer-memory exchange on a one-rank group, so that every kernel of the
+    exchange (index, waits, quantised rows, return targets, the scatter-mode
+    layer, publish, ordered combine) can be profiled on one GPU.  Not a
+    scaling number: all tokens go to this rank and nothing crosses NVLink."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    device = torch.device("cuda:0")
+    torch.cuda.set_device(device)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29611")
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=device, timeout=timedelta(seconds=120))
+    try:
+        r = ep_config4(a, 0, 1, device, profiles=("bf16",), force_ep=True)
+    finally:
+        dist.destroy_process_group()
+    bf = r["bf16"]
+    line = {"metric": METRIC, "value": bf["tok_s"], "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": bf["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e2m1 x e4m3 block-scaled (bf16 profile), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded; BASELINE config 4 distributions)",
+            "config": {"workload": "cfg4 through the expert-parallel exchange on one rank (profiling aid)",
+                       "tokens_per_step": CFG4_TOKENS, "global_batch": CFG4_TOKENS, "parallelism": "ep1",
+                       "l2": "256 MiB flush before every timed step"},
+            "detail": {"profiles": r}}
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None):
     a = _args(argv)
     if a.impl == "reference":
@@ -1312,6 +1346,8 @@ def main(argv=None):
         run_prefill(a)
     elif a.workload == "offload":
         run_offload(a)
+    elif a.workload == "ep1":
+        run_ep1(a)
     else:
         run_ours(a)
 
