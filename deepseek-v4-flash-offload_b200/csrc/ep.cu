@@ -260,8 +260,13 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
     const int64_t t = t0 + tid;
     unsigned long long mask = 0ull;   // destinations of this token
     if (t < T) {
-      for (int j = 0; j < topk; ++j) {
-        const int e = idx[t * topk + j];
+      int ev[16];   // the token's picks, loaded together
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ev[j] = j < topk ? idx[t * topk + j] : -1;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= topk) break;
+        const int e = ev[j];
         if (e >= 0 && e < E) {
           const int d = ep_dest(e, e_loc, owner);
           if (d >= 0 && d < world)
@@ -298,10 +303,12 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
     __syncthreads();
   }
   for (int64_t t = tid; t < T; t += EP_THREADS) {
-    int ke[16], ka[16];
+    int ke[16], ka[16], ev[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ev[j] = j < topk ? idx[t * topk + j] : -1;
     int n = 0;
     for (int j = 0; j < topk; ++j) {
-      const int e = idx[t * topk + j];
+      const int e = ev[j];
       if (e < 0 || e >= E) continue;
       const int d = ep_dest(e, e_loc, owner);
       if (d < 0 || d >= world) continue;
@@ -383,37 +390,48 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
     const unsigned dests = __ballot_sync(0xffffffffu, p >= 0);
     if (dests == 0u) continue;
     uint32_t scl[2] = {0u, 0u};   // lane L: the scale(s) of block L (and L + 32)
-    for (int kb = 0; kb < kblk; ++kb) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(x + t * H + kb * 128 + lane * 4);
-      if constexpr (FMT == DSV4_ROWS_BF16) {
-        for (unsigned m = dests; m; m &= m - 1u) {
-          const int d = __ffs(m) - 1;
-          const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
-          *reinterpret_cast<uint2*>(peers[d] + row * row_bytes + (int64_t)(kb * 128 + lane * 4) * 2) = raw;
-        }
-      } else {
-        const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
-                            bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
-        int e;
-        if constexpr (FMT == DSV4_ROWS_FP8) {
-          const uint32_t o = fp8_block_quant(v, &e);
-          if (lane == (kb & 31)) scl[kb >> 5] = (uint32_t)(e + 127);
+    for (int kb0 = 0; kb0 < kblk; kb0 += 8) {
+      // eight 128-column blocks' loads in flight together, then each block
+      uint2 raws[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        raws[u] = kb0 + u < kblk ? *reinterpret_cast<const uint2*>(x + t * H + (kb0 + u) * 128 + lane * 4)
+                                 : make_uint2(0u, 0u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kb = kb0 + u;
+        if (kb >= kblk) break;
+        const uint2 raw = raws[u];
+        if constexpr (FMT == DSV4_ROWS_BF16) {
           for (unsigned m = dests; m; m &= m - 1u) {
             const int d = __ffs(m) - 1;
             const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
-            *reinterpret_cast<uint32_t*>(peers[d] + row * row_bytes + kb * 128 + lane * 4) = o;
+            *reinterpret_cast<uint2*>(peers[d] + row * row_bytes + (int64_t)(kb * 128 + lane * 4) * 2) = raw;
           }
         } else {
-          const uint32_t packed = mxfp4_block_quant(v, &e);
-          const uint32_t sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
-                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
-                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
-                                 ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
-          if (lane == (kb & 31)) scl[kb >> 5] = sword;
-          for (unsigned m = dests; m; m &= m - 1u) {
-            const int d = __ffs(m) - 1;
-            const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
-            *reinterpret_cast<uint16_t*>(peers[d] + row * row_bytes + kb * 64 + lane * 2) = (uint16_t)packed;
+          const float v[4] = {bf16_from_bits(raw.x & 0xffffu), bf16_from_bits(raw.x >> 16),
+                              bf16_from_bits(raw.y & 0xffffu), bf16_from_bits(raw.y >> 16)};
+          int e;
+          if constexpr (FMT == DSV4_ROWS_FP8) {
+            const uint32_t o = fp8_block_quant(v, &e);
+            if (lane == (kb & 31)) scl[kb >> 5] = (uint32_t)(e + 127);
+            for (unsigned m = dests; m; m &= m - 1u) {
+              const int d = __ffs(m) - 1;
+              const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+              *reinterpret_cast<uint32_t*>(peers[d] + row * row_bytes + kb * 128 + lane * 4) = o;
+            }
+          } else {
+            const uint32_t packed = mxfp4_block_quant(v, &e);
+            const uint32_t sword = (uint32_t)(__shfl_sync(0xffffffffu, e, 0) + 127) |
+                                   ((uint32_t)(__shfl_sync(0xffffffffu, e, 8) + 127) << 8) |
+                                   ((uint32_t)(__shfl_sync(0xffffffffu, e, 16) + 127) << 16) |
+                                   ((uint32_t)(__shfl_sync(0xffffffffu, e, 24) + 127) << 24);
+            if (lane == (kb & 31)) scl[kb >> 5] = sword;
+            for (unsigned m = dests; m; m &= m - 1u) {
+              const int d = __ffs(m) - 1;
+              const int64_t row = __shfl_sync(0xffffffffu, my_row, d);
+              *reinterpret_cast<uint16_t*>(peers[d] + row * row_bytes + kb * 64 + lane * 2) = (uint16_t)packed;
+            }
           }
         }
       }
