@@ -239,14 +239,14 @@ __device__ __forceinline__ int ep_dest(int e, int e_loc, const int32_t* __restri
 }
 
 // One CTA: epoch += 1; per destination, the tokens with an expert there and
-// their stable rank among them (pos[t][d], or -1); the combine order of each
-// token's assignments (ascending expert id); this rank's count row into
-// every peer's cnt, fenced and published.
+// their stable rank among them (pos[t][d], or -1); this rank's count row
+// into every peer's cnt, fenced and published.  (The combine order of each
+// token's assignments is left to the rows kernel, a warp per token.)
 __global__ void __launch_bounds__(EP_THREADS, 1)
     ep_p2p_index_kernel(const int32_t* __restrict__ idx, int64_t T, int topk, int E, int e_loc,
                         const int32_t* __restrict__ owner, int world, int my_rank, uint8_t* const* __restrict__ peers,
                         int64_t off_cnt, int64_t off_flags, uint32_t* __restrict__ ctrl, int32_t* __restrict__ pos,
-                        int32_t* __restrict__ ordered, int* __restrict__ status) {
+                        int* __restrict__ status) {
   __shared__ int wc[32][EP_MAX_WORLD];
   __shared__ int base[EP_MAX_WORLD];
   __shared__ int round_tot[EP_MAX_WORLD];
@@ -302,27 +302,6 @@ __global__ void __launch_bounds__(EP_THREADS, 1)
     if (tid < world) base[tid] += round_tot[tid];
     __syncthreads();
   }
-  for (int64_t t = tid; t < T; t += EP_THREADS) {
-    int ke[16], ka[16], ev[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) ev[j] = j < topk ? idx[t * topk + j] : -1;
-    int n = 0;
-    for (int j = 0; j < topk; ++j) {
-      const int e = ev[j];
-      if (e < 0 || e >= E) continue;
-      const int d = ep_dest(e, e_loc, owner);
-      if (d < 0 || d >= world) continue;
-      int i = n++;
-      while (i > 0 && ke[i - 1] > e) {
-        ke[i] = ke[i - 1];
-        ka[i] = ka[i - 1];
-        --i;
-      }
-      ke[i] = e;
-      ka[i] = (int)(t * topk + j);
-    }
-    for (int j = 0; j < topk; ++j) ordered[t * topk + j] = j < n ? ka[j] : -1;
-  }
   // this rank's counts into row my_rank of every peer's count matrix
   for (int i = tid; i < world * world; i += EP_THREADS) {
     const int d = i / world, c = i - d * world;
@@ -369,7 +348,7 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
                                    const float* __restrict__ w, const int32_t* __restrict__ pos, int64_t T, int topk,
                                    int H, int E, int e_loc, const int32_t* __restrict__ owner, int world, int my_rank,
                                    uint8_t* const* __restrict__ peers, EpBlock blk, const int32_t* __restrict__ cnt,
-                                   uint32_t* __restrict__ ctrl, int64_t row_bytes) {
+                                   uint32_t* __restrict__ ctrl, int64_t row_bytes, int32_t* __restrict__ ordered) {
   __shared__ int64_t off[EP_MAX_WORLD];
   griddep_wait();
   griddep_launch();
@@ -387,6 +366,24 @@ __global__ void ep_p2p_rows_kernel(const uint16_t* __restrict__ x, const int32_t
     // destinations of this token: lane d < world holds its row there, or -1
     const int p = lane < world ? pos[t * world + lane] : -1;
     const int64_t my_row = p >= 0 ? off[lane] + p : -1;
+    {
+      // the token's combine order: its valid assignments t*k + j in ascending
+      // expert id (equal ids by j), then -1; lane j ranks pick j
+      const int e = lane < topk ? idx[t * topk + lane] : -1;
+      const bool valid = e >= 0 && e < E && [&] {
+        const int d = ep_dest(e, e_loc, owner);
+        return d >= 0 && d < world;
+      }();
+      int rank = 0;
+      for (int i = 0; i < topk; ++i) {
+        const int ei = __shfl_sync(0xffffffffu, e, i);
+        const int vi = __shfl_sync(0xffffffffu, valid ? 1 : 0, i);
+        rank += (vi && (ei < e || (ei == e && i < lane))) ? 1 : 0;
+      }
+      const int nv = __popc(__ballot_sync(0xffffffffu, valid));
+      if (valid) ordered[t * topk + rank] = (int)(t * topk + lane);
+      if (lane >= nv && lane < topk) ordered[t * topk + lane] = -1;
+    }
     const unsigned dests = __ballot_sync(0xffffffffu, p >= 0);
     if (dests == 0u) continue;
     uint32_t scl[2] = {0u, 0u};   // lane L: the scale(s) of block L (and L + 32)
@@ -702,7 +699,7 @@ extern "C" int dsv4_ep_dispatch_q(dsv4_ep* ep, const void* x_bf16, const float* 
   const int e_loc = (int)(n_experts / ep->world);
   DSV4_CUDA_CHECK(launch_k(ep_p2p_index_kernel, dim3(1), dim3(EP_THREADS), 0, st, pdl, route_indices, T, k,
                            (int)n_experts, e_loc, expert_owner, ep->world, ep->rank, peers, ep->blk.off_cnt,
-                           ep->blk.off_flags, ctrl, pos, ordered_assignments, status));
+                           ep->blk.off_flags, ctrl, pos, status));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags, (const uint32_t*)ctrl,
                            ep->world, status, (const int32_t*)nullptr, ep->rank, (uint32_t*)nullptr));
   // a warp per token
@@ -712,7 +709,8 @@ extern "C" int dsv4_ep_dispatch_q(dsv4_ep* ep, const void* x_bf16, const float* 
                                                      : ep_p2p_rows_kernel<DSV4_ROWS_BF16>;
   DSV4_CUDA_CHECK(launch_k(rows_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl, (const uint16_t*)x_bf16,
                            route_indices, route_weights, (const int32_t*)pos, T, k, ep->hidden, (int)n_experts, e_loc,
-                           expert_owner, ep->world, ep->rank, peers, ep->blk, cnt, ctrl, row_bytes));
+                           expert_owner, ep->world, ep->rank, peers, ep->blk, cnt, ctrl, row_bytes,
+                           ordered_assignments));
   DSV4_CUDA_CHECK(launch_k(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, pdl, flags + ep->world,
                            (const uint32_t*)ctrl, ep->world, status, cnt, ep->rank, ctrl + EPC_NRECV));
   // the return targets of the received assignments (for the scatter-mode down GEMM)
